@@ -1,0 +1,394 @@
+"""Binding of the b200q C ABI (include/b200q.h) and the ``torch.ops.b200q`` ops.
+
+The native library ``_lib/libb200q.so`` is built in-tree by ``csrc/build.py``.
+This module loads it with ctypes, passes raw device pointers, element strides
+and torch's current CUDA stream, and raises ``RuntimeError`` on any non-zero
+status.  There is no CPU fallback: if the library is missing or the device is
+not a B200 (sm_100), every op raises.
+
+The ``b200q`` torch.library namespace mirrors the reference's native module
+functions (pybind in the reference: _patches/int8_ext/int8_gemm.mm:2626-2715,
+_patches/fp8_ext/fp8_matmul2d.mm:355-360, _patches/fp8s_ext/w8a16_gemm.mm:316-329):
+
+  quant_rowwise_i8(x)                       -> (q int8 [M,K], scale f32 [M,1])
+  int_mm(a [M,K] i8, b [K,N] i8)            -> int32 [M,N]      (torch._int_mm contract)
+  i8_matmul_nt(a [M,K], w [N,K])            -> int32 [M,N]      (i8_matmul2d_nt)
+  i8_matmul_nt_fused(a, w, row_scale, bias) -> bf16 [M,N]       (i8_matmul2d_nt_fused)
+  i8_matmul_nt_fused_cs(a, w, row_scale, col_scale, bias, out_dtype) (i8_matmul2d_nt_fused_cs)
+  i8_linear(x, w, w_scale, bias, out_dtype) -> quant + GEMM + dequant epilogue
+  fp8_quant_tensorwise(x)                   -> (q e4m3 [M,K], scale f32 [])
+  fp8_scaled_mm(a, w_nk, scale_a, scale_b, scale_result, bias, out_dtype, act)
+  w8a16_linear(x, w_nk e4m3, w_scale, bias, act, out_dtype)
+  fp8_decode(t, out_dtype)
+"""
+
+import ctypes
+import os
+
+import torch
+
+TAG = "[b200q]"
+
+_LIB_PATH = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "_lib",
+                         "libb200q.so")
+
+B200Q_BF16, B200Q_F16, B200Q_F32, B200Q_I32 = 0, 1, 2, 3
+BIAS_NONE, BIAS_BF16, BIAS_F16, BIAS_F32 = 0, 1, 2, 3
+ACT_NONE, ACT_GELU_TANH, ACT_GELU_ERF = 0, 1, 2
+ACTS = {None: ACT_NONE, "none": ACT_NONE, "gelu_tanh": ACT_GELU_TANH, "gelu": ACT_GELU_ERF}
+
+_DT = {torch.bfloat16: B200Q_BF16, torch.float16: B200Q_F16, torch.float32: B200Q_F32}
+_BIAS_DT = {torch.bfloat16: BIAS_BF16, torch.float16: BIAS_F16, torch.float32: BIAS_F32}
+
+_lib = None
+
+_vp, _i64, _int, _sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t
+_SIGNATURES = {
+    "b200q_version": ([], _int),
+    "b200q_status_string": ([_int], ctypes.c_char_p),
+    "b200q_launch_count": ([], ctypes.c_uint64),
+    "b200q_get_device_status": ([_vp, _int], _int),
+    "b200q_quant_rowwise_i8": ([_vp, _int, _i64, _i64, _i64, _vp, _i64, _vp, _vp], _int),
+    "b200q_i8_matmul_nt": ([_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp], _int),
+    "b200q_i8_matmul_nt_dequant": ([_vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _int, _vp, _int,
+                                    _i64, _i64, _i64, _i64, _vp], _int),
+    "b200q_i8_linear": ([_vp, _int, _i64, _vp, _i64, _vp, _i64, _vp, _int, _vp, _int, _i64, _i64,
+                         _i64, _i64, _vp, _vp, _vp], _int),
+    "b200q_fp8_scaled_mm": ([_vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _int, _int, _vp,
+                             _int, _i64, _i64, _i64, _i64, _vp], _int),
+    "b200q_fp8_quant_tensorwise": ([_vp, _int, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp], _int),
+    "b200q_w8a16_workspace_size": ([_i64, _i64, _i64], _sz),
+    "b200q_w8a16_linear": ([_vp, _int, _i64, _vp, _i64, _vp, _vp, _int, _int, _vp, _int, _i64, _i64,
+                            _i64, _i64, _vp, _sz, _vp], _int),
+    "b200q_fp8_decode": ([_vp, _i64, _int, _vp, _int, _vp], _int),
+}
+
+
+def library_path():
+    return _LIB_PATH
+
+
+def lib():
+    """The loaded C-ABI library (raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            raise RuntimeError(f"{TAG} native library missing at {_LIB_PATH}; run the build "
+                               f"(__graft_entry__.build() or csrc/build.py)")
+        L = ctypes.CDLL(_LIB_PATH)
+        for name, (args, res) in _SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = L
+    return _lib
+
+
+def available():
+    """True when the library is built and the current CUDA device is a B200."""
+    if not os.path.exists(_LIB_PATH) or not torch.cuda.is_available():
+        return False
+    return torch.cuda.get_device_capability() == (10, 0)
+
+
+def launch_count():
+    return int(lib().b200q_launch_count())
+
+
+def device_status(reset=False):
+    v = ctypes.c_uint(0)
+    _check(lib().b200q_get_device_status(ctypes.byref(v), int(bool(reset))))
+    return int(v.value)
+
+
+def _check(status):
+    if status != 0:
+        msg = lib().b200q_status_string(status).decode()
+        raise RuntimeError(f"{TAG} native call failed: {msg} (status {status})")
+
+
+def _stream(t):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and t.device.type != "cuda":
+            raise RuntimeError(f"{TAG} expected CUDA tensors, got {t.device}")
+
+
+def _rows_2d(t, name):
+    """View as [rows, K] with unit inner stride (no copy when already so)."""
+    if t.dim() != 2:
+        raise RuntimeError(f"{TAG} {name} must be 2-D, got {tuple(t.shape)}")
+    if t.stride(1) != 1:
+        t = t.contiguous()
+    return t
+
+
+# ----------------------------------------------------------------------------- ops (eager)
+def quant_rowwise_i8(x):
+    _require_cuda(x)
+    x = _rows_2d(x, "x")
+    if x.dtype not in (torch.bfloat16, torch.float16):
+        raise RuntimeError(f"{TAG} quant_rowwise_i8 expects bf16/f16, got {x.dtype}")
+    M, K = x.shape
+    q = torch.empty((M, K), dtype=torch.int8, device=x.device)
+    s = torch.empty((M, 1), dtype=torch.float32, device=x.device)
+    _check(lib().b200q_quant_rowwise_i8(_p(x), _DT[x.dtype], M, K, x.stride(0), _p(q), K, _p(s),
+                                        _stream(x)))
+    return q, s
+
+
+def i8_matmul_nt(a, w):
+    _require_cuda(a, w)
+    a, w = _rows_2d(a, "a"), _rows_2d(w, "w")
+    if a.dtype != torch.int8 or w.dtype != torch.int8:
+        raise RuntimeError(f"{TAG} i8_matmul_nt expects int8 operands")
+    if a.shape[1] != w.shape[1]:
+        raise RuntimeError(f"{TAG} K mismatch: a {tuple(a.shape)} w {tuple(w.shape)}")
+    M, K = a.shape
+    N = w.shape[0]
+    c = torch.empty((M, N), dtype=torch.int32, device=a.device)
+    _check(lib().b200q_i8_matmul_nt(_p(a), a.stride(0), _p(w), w.stride(0), _p(c), N, M, N, K,
+                                    _stream(a)))
+    return c
+
+
+def int_mm(a, b):
+    """torch._int_mm contract: a [M,K] int8 @ b [K,N] int8 -> int32 [M,N].
+
+    b is consumed as W = b.t() ([N,K]); when b is the transpose view of a
+    row-major weight (the common ``weight.T`` call) no copy is made."""
+    if b.dim() != 2:
+        raise RuntimeError(f"{TAG} int_mm expects 2-D b")
+    return i8_matmul_nt(a, b.t())
+
+
+def _out_dtype_code(dt, allowed):
+    if dt not in allowed:
+        raise RuntimeError(f"{TAG} unsupported out dtype {dt}")
+    return _DT[dt]
+
+
+def i8_matmul_nt_fused_cs(a, w, row_scale, col_scale, bias=None, out_dtype=torch.bfloat16,
+                          act=None):
+    _require_cuda(a, w, row_scale, col_scale, bias)
+    a, w = _rows_2d(a, "a"), _rows_2d(w, "w")
+    M, K = a.shape
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise RuntimeError(f"{TAG} K mismatch")
+    row_scale = row_scale.reshape(-1).float().contiguous()
+    col_scale = col_scale.reshape(-1).float().contiguous()
+    if row_scale.numel() != M or col_scale.numel() not in (1, N):
+        raise RuntimeError(f"{TAG} scale numel mismatch: row {row_scale.numel()} (M={M}), "
+                           f"col {col_scale.numel()} (N={N})")
+    code = _out_dtype_code(out_dtype, (torch.bfloat16, torch.float16))
+    if bias is not None:
+        bias = bias.to(out_dtype).contiguous()
+        if bias.numel() != N:
+            raise RuntimeError(f"{TAG} bias numel {bias.numel()} != N {N}")
+    out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    _check(lib().b200q_i8_matmul_nt_dequant(_p(a), a.stride(0), _p(w), w.stride(0), _p(row_scale),
+                                            _p(col_scale), col_scale.numel(), _p(bias),
+                                            ACTS[act], _p(out), code, N, M, N, K, _stream(a)))
+    return out
+
+
+def i8_matmul_nt_fused(a, w, row_scale, bias=None):
+    """Tensorwise-weight variant: row_scale already holds weight_scale * x_scale."""
+    one = torch.ones(1, dtype=torch.float32, device=a.device)
+    return i8_matmul_nt_fused_cs(a, w, row_scale, one, bias, torch.bfloat16)
+
+
+def i8_linear(x, w, w_scale, bias=None, out_dtype=torch.bfloat16, act=None):
+    """Per-token quant + INT8 GEMM + reference dequant epilogue; x [..., K]."""
+    _require_cuda(x, w, w_scale, bias)
+    shp = x.shape
+    x2 = _rows_2d(x.reshape(-1, shp[-1]), "x")
+    M, K = x2.shape
+    N = w.shape[0]
+    w = _rows_2d(w, "w")
+    ws = w_scale.reshape(-1).float().contiguous()
+    if ws.numel() not in (1, N):
+        raise RuntimeError(f"{TAG} weight scale numel {ws.numel()} not in (1, {N})")
+    code = _out_dtype_code(out_dtype, (torch.bfloat16, torch.float16))
+    if bias is not None:
+        bias = bias.to(out_dtype).contiguous()
+    q = torch.empty((M, K), dtype=torch.int8, device=x.device)
+    s = torch.empty((M,), dtype=torch.float32, device=x.device)
+    out = torch.empty((M, N), dtype=out_dtype, device=x.device)
+    _check(lib().b200q_i8_linear(_p(x2), _DT[x2.dtype], x2.stride(0), _p(w), w.stride(0), _p(ws),
+                                 ws.numel(), _p(bias), ACTS[act], _p(out), code, N, M, N, K, _p(q),
+                                 _p(s), _stream(x2)))
+    return out.reshape(*shp[:-1], N)
+
+
+def fp8_quant_tensorwise(x):
+    _require_cuda(x)
+    x = _rows_2d(x.reshape(-1, x.shape[-1]) if x.dim() != 2 else x, "x")
+    M, K = x.shape
+    q = torch.empty((M, K), dtype=torch.float8_e4m3fn, device=x.device)
+    scale = torch.empty((), dtype=torch.float32, device=x.device)
+    amax = torch.empty((1,), dtype=torch.int32, device=x.device)
+    _check(lib().b200q_fp8_quant_tensorwise(_p(x), _DT[x.dtype], M, K, x.stride(0), _p(q), K,
+                                            _p(scale), _p(amax), _stream(x)))
+    return q, scale
+
+
+def _scale_arg(s, n_ok):
+    if s is None:
+        return None, 0
+    s = s.reshape(-1).float().contiguous()
+    if s.numel() not in n_ok:
+        raise RuntimeError(f"{TAG} scale numel {s.numel()} not in {n_ok}")
+    return s, s.numel()
+
+
+def fp8_scaled_mm(a, w, scale_a=None, scale_b=None, scale_result=None, bias=None,
+                  out_dtype=torch.bfloat16, act=None):
+    """a [M,K] e4m3, w [N,K] e4m3 (i.e. torch._scaled_mm's ``other`` = w.t())."""
+    _require_cuda(a, w, scale_a, scale_b, scale_result, bias)
+    a, w = _rows_2d(a, "a"), _rows_2d(w, "w")
+    M, K = a.shape
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise RuntimeError(f"{TAG} K mismatch")
+    sa, na = _scale_arg(scale_a, (1, M))
+    sb, nb = _scale_arg(scale_b, (1, N))
+    sr, _ = _scale_arg(scale_result, (1,))
+    out_dtype = out_dtype or torch.bfloat16
+    code = _out_dtype_code(out_dtype, (torch.bfloat16, torch.float16, torch.float32))
+    bdt = BIAS_NONE
+    if bias is not None:
+        bias = bias.contiguous()
+        if bias.dtype not in _BIAS_DT:
+            bias = bias.float()
+        bdt = _BIAS_DT[bias.dtype]
+    out = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    _check(lib().b200q_fp8_scaled_mm(_p(a), a.stride(0), _p(w), w.stride(0), _p(sa), na, _p(sb),
+                                     nb, _p(sr), _p(bias), bdt, ACTS[act], _p(out), code, N, M, N,
+                                     K, _stream(a)))
+    return out
+
+
+def w8a16_linear(x, w, w_scale=None, bias=None, act=None, out_dtype=None):
+    """x [..., K] bf16/f16, w [N,K] e4m3 -> act(x . w^T * w_scale + bias)."""
+    _require_cuda(x, w, w_scale, bias)
+    shp = x.shape
+    x2 = _rows_2d(x.reshape(-1, shp[-1]), "x")
+    if x2.dtype not in (torch.bfloat16, torch.float16):
+        raise RuntimeError(f"{TAG} w8a16 expects bf16/f16 activations, got {x2.dtype}")
+    w = _rows_2d(w, "w")
+    M, K = x2.shape
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise RuntimeError(f"{TAG} K mismatch")
+    ws, _ = _scale_arg(w_scale, (1,))
+    out_dtype = out_dtype or x2.dtype
+    code = _out_dtype_code(out_dtype, (torch.bfloat16, torch.float16, torch.float32))
+    bdt = BIAS_NONE
+    if bias is not None:
+        bias = bias.contiguous()
+        if bias.dtype not in _BIAS_DT:
+            bias = bias.float()
+        bdt = _BIAS_DT[bias.dtype]
+    out = torch.empty((M, N), dtype=out_dtype, device=x.device)
+    wsb = int(lib().b200q_w8a16_workspace_size(M, N, K))
+    work = torch.empty((wsb,), dtype=torch.uint8, device=x.device) if wsb else None
+    _check(lib().b200q_w8a16_linear(_p(x2), _DT[x2.dtype], x2.stride(0), _p(w), w.stride(0),
+                                    _p(ws), _p(bias), bdt, ACTS[act], _p(out), code, N, M, N, K,
+                                    _p(work), wsb, _stream(x2)))
+    return out.reshape(*shp[:-1], N)
+
+
+def fp8_decode(t, out_dtype=torch.float32):
+    _require_cuda(t)
+    kinds = {torch.float8_e4m3fn: 0, torch.float8_e5m2: 1}
+    if t.dtype not in kinds:
+        raise RuntimeError(f"{TAG} fp8_decode expects an FP8 tensor, got {t.dtype}")
+    src = t.contiguous()
+    code = _out_dtype_code(out_dtype, (torch.bfloat16, torch.float16, torch.float32))
+    out = torch.empty(src.shape, dtype=out_dtype, device=t.device)
+    _check(lib().b200q_fp8_decode(_p(src), src.numel(), kinds[t.dtype], _p(out), code,
+                                  _stream(src)))
+    return out
+
+
+# ----------------------------------------------------------------------------- torch.library
+_LIBRARY = None
+
+
+def _register_ops():
+    """Register the ``b200q`` namespace (CUDA kernels + shape-only fake kernels)."""
+    global _LIBRARY
+    if _LIBRARY is not None:
+        return
+    L = torch.library.Library("b200q", "DEF")
+    L.define("quant_rowwise_i8(Tensor x) -> (Tensor, Tensor)")
+    L.define("int_mm(Tensor a, Tensor b) -> Tensor")
+    L.define("i8_matmul_nt(Tensor a, Tensor w) -> Tensor")
+    L.define("i8_matmul_nt_fused(Tensor a, Tensor w, Tensor row_scale, Tensor? bias=None) -> Tensor")
+    L.define("i8_matmul_nt_fused_cs(Tensor a, Tensor w, Tensor row_scale, Tensor col_scale, "
+             "Tensor? bias=None, ScalarType out_dtype=15, str act='none') -> Tensor")
+    L.define("i8_linear(Tensor x, Tensor w, Tensor w_scale, Tensor? bias=None, "
+             "ScalarType out_dtype=15, str act='none') -> Tensor")
+    L.define("fp8_quant_tensorwise(Tensor x) -> (Tensor, Tensor)")
+    L.define("fp8_scaled_mm(Tensor a, Tensor w, Tensor? scale_a=None, Tensor? scale_b=None, "
+             "Tensor? scale_result=None, Tensor? bias=None, ScalarType out_dtype=15, "
+             "str act='none') -> Tensor")
+    L.define("w8a16_linear(Tensor x, Tensor w, Tensor? w_scale=None, Tensor? bias=None, "
+             "str act='none', ScalarType? out_dtype=None) -> Tensor")
+    L.define("fp8_decode(Tensor t, ScalarType out_dtype=6) -> Tensor")
+
+    impls = {
+        "quant_rowwise_i8": quant_rowwise_i8,
+        "int_mm": int_mm,
+        "i8_matmul_nt": i8_matmul_nt,
+        "i8_matmul_nt_fused": i8_matmul_nt_fused,
+        "i8_matmul_nt_fused_cs": i8_matmul_nt_fused_cs,
+        "i8_linear": i8_linear,
+        "fp8_quant_tensorwise": fp8_quant_tensorwise,
+        "fp8_scaled_mm": lambda a, w, sa=None, sb=None, sr=None, b=None, od=torch.bfloat16,
+        act="none": fp8_scaled_mm(a, w, sa, sb, sr, b, od, act),
+        "w8a16_linear": w8a16_linear,
+        "fp8_decode": fp8_decode,
+    }
+    for name, fn in impls.items():
+        L.impl(name, fn, "CUDA")
+
+    def fake_quant(x):
+        M = x.numel() // x.shape[-1]
+        return (x.new_empty((M, x.shape[-1]), dtype=torch.int8),
+                x.new_empty((M, 1), dtype=torch.float32))
+
+    fakes = {
+        "quant_rowwise_i8": fake_quant,
+        "int_mm": lambda a, b: a.new_empty((a.shape[0], b.shape[1]), dtype=torch.int32),
+        "i8_matmul_nt": lambda a, w: a.new_empty((a.shape[0], w.shape[0]), dtype=torch.int32),
+        "i8_matmul_nt_fused": lambda a, w, rs, bias=None: a.new_empty((a.shape[0], w.shape[0]),
+                                                                      dtype=torch.bfloat16),
+        "i8_matmul_nt_fused_cs": lambda a, w, rs, cs, bias=None, od=torch.bfloat16, act="none":
+        a.new_empty((a.shape[0], w.shape[0]), dtype=od),
+        "i8_linear": lambda x, w, ws, bias=None, od=torch.bfloat16, act="none": x.new_empty(
+            (*x.shape[:-1], w.shape[0]), dtype=od),
+        "fp8_quant_tensorwise": lambda x: (x.new_empty((x.numel() // x.shape[-1], x.shape[-1]),
+                                                       dtype=torch.float8_e4m3fn),
+                                           x.new_empty((), dtype=torch.float32)),
+        "fp8_scaled_mm": lambda a, w, sa=None, sb=None, sr=None, b=None, od=torch.bfloat16,
+        act="none": a.new_empty((a.shape[0], w.shape[0]), dtype=od),
+        "w8a16_linear": lambda x, w, ws=None, b=None, act="none", od=None: x.new_empty(
+            (*x.shape[:-1], w.shape[0]), dtype=od or x.dtype),
+        "fp8_decode": lambda t, od=torch.float32: t.new_empty(t.shape, dtype=od),
+    }
+    for name, fn in fakes.items():
+        torch.library.register_fake(f"b200q::{name}", fn, lib=L)
+    _LIBRARY = L
+
+
+_register_ops()

@@ -1,0 +1,250 @@
+"""INT8 W8A8 comfy Linear route: comfy ``int8_tensorwise`` layers on the B200 kernels.
+
+Mirrors the reference's _patches/int8_linear_kernel_mps.py: ``install()`` wraps
+``comfy.ops.mixed_precision_ops`` so each generated ``Linear.forward`` tries
+``_try_int8_kernel_forward`` first (eligibility :779-830), which runs
+``_int8_linear_kernel`` (:218-263): rowwise activation quant (with the 1-slot
+activation cache of :97-140), then the INT8 GEMM with the epilogue chosen as in
+``_int8_linear_prequant`` (:152-215) — scalar weight scale -> fused tensorwise
+epilogue, per-channel [N,1] -> fused channelwise epilogue, anything else -> raw
+int32 GEMM + the chunked eager rescale.  Outputs are bit-identical to
+comfy_kitchen's eager ``int8_linear`` (rowwise quant -> _int_mm -> chunked
+rescale -> + bias).  ``_kernel`` exposes the reference's native-module method
+names on top of ``torch.ops.b200q``.
+
+Convrot (Hadamard-rotated) checkpoints rotate with comfy_kitchen's own helpers
+before the quant, exactly as the reference does.  Opt-in: ASFP8_INT8_EXT=1.
+"""
+import inspect
+import os
+import sys
+import weakref
+
+import torch
+
+from . import _common
+
+TAG = "[b200q/int8_kernel]"
+
+_installed = False
+_orig_int8_linear = None
+_kernel = None
+_act_cache = None  # (x_weakref, convrot, groupsize, x_8, x_scale)
+_LINEAR_MAX_ELEMS = 2 ** 31 - 1
+
+
+class _NativeInt8Kernel:
+    """The reference's int8_ext module surface (int8_gemm.mm:2626-2715) on b200q ops."""
+
+    @staticmethod
+    def i8_quant_rowwise(x):
+        return torch.ops.b200q.quant_rowwise_i8(x)
+
+    @staticmethod
+    def i8_matmul2d_nt(a, b):
+        return torch.ops.b200q.i8_matmul_nt(a, b)
+
+    @staticmethod
+    def i8_matmul2d_nt_fused(a, b, row_scale, bias=None):
+        return torch.ops.b200q.i8_matmul_nt_fused(a, b, row_scale, bias)
+
+    @staticmethod
+    def i8_matmul2d_nt_fused_cs(a, b, row_scale, col_scale, bias=None, split_tail=False,
+                                long_schedule=True, moss_schedule=False, out_dtype=torch.bfloat16):
+        # split_tail / long / moss are Apple tile schedules; the persistent tcgen05
+        # kernel covers ragged M natively, and the bytes do not depend on them.
+        return torch.ops.b200q.i8_matmul_nt_fused_cs(a, b, row_scale, col_scale, bias, out_dtype)
+
+    @staticmethod
+    def warmup():
+        return None
+
+
+def _int8_linear_bounded(x, weight, weight_scale, bias, out_dtype, convrot, convrot_groupsize):
+    """Row-chunk calls whose element count exceeds 2**31-1 (int8_linear_kernel_mps.py:75-94).
+    The kernels use 64-bit offsets; chunking keeps the quant scratch bounded."""
+    flat = x.reshape(-1, x.shape[-1])
+    output = torch.empty((flat.shape[0], weight.shape[0]), device=x.device, dtype=out_dtype)
+    rows = max(1, min(8192, _LINEAR_MAX_ELEMS // max(flat.shape[-1], weight.shape[0])))
+    for start in range(0, flat.shape[0], rows):
+        stop = min(start + rows, flat.shape[0])
+        chunk = flat[start:stop]
+        output[start:stop].copy_(_int8_linear_kernel(chunk, weight, weight_scale, bias, out_dtype,
+                                                     convrot, convrot_groupsize))
+    return output.reshape(*x.shape[:-1], weight.shape[0])
+
+
+def _quant_cached(x, convrot, convrot_groupsize):
+    """Rotate (convrot) + rowwise quant, reusing the previous result for the same
+    live tensor object and settings (int8_linear_kernel_mps.py:97-140)."""
+    global _act_cache
+    c = _act_cache
+    if c is not None and c[0]() is x and c[1] == convrot and c[2] == convrot_groupsize:
+        return c[3], c[4]
+    xr = x
+    if convrot:
+        from comfy_kitchen.tensor.int8_utils import _build_hadamard, _rotate_activation
+        h = _build_hadamard(convrot_groupsize, device=x.device, dtype=x.dtype)
+        xr = _rotate_activation(xr, h, convrot_groupsize)
+    x_2d = xr.reshape(-1, xr.shape[-1])
+    x_8, x_scale = _kernel.i8_quant_rowwise(x_2d)
+    if os.environ.get("ASFP8_INT8_ACT_CACHE", "1") != "0":
+        try:
+            _act_cache = (weakref.ref(x), convrot, convrot_groupsize, x_8, x_scale)
+        except TypeError:
+            _act_cache = None
+    return x_8, x_scale
+
+
+def _int8_linear_prequant(x_8, x_scale, weight, weight_scale, bias, out_dtype, input_shape):
+    """Epilogue selection of int8_linear_kernel_mps.py:152-215."""
+    weight_scale = weight_scale.reshape(-1)
+    N = weight.shape[0]
+    if out_dtype in (torch.bfloat16, torch.float16) and weight_scale.numel() in (1, N):
+        if out_dtype == torch.bfloat16 and weight_scale.numel() == 1:
+            row_scale = (weight_scale.float() * x_scale.reshape(-1).float()).contiguous()
+            bias_arg = bias.to(torch.bfloat16) if bias is not None else None
+            result = _kernel.i8_matmul2d_nt_fused(x_8, weight, row_scale, bias_arg)
+        else:
+            bias_arg = bias.to(out_dtype) if bias is not None else None
+            result = _kernel.i8_matmul2d_nt_fused_cs(
+                x_8, weight, x_scale.reshape(-1).float(), weight_scale.float(), bias_arg,
+                out_dtype=out_dtype)
+        return result.reshape(*input_shape[:-1], N)
+    # Other output dtypes: exact int32 GEMM + the eager chunked rescale.
+    result = _kernel.i8_matmul2d_nt(x_8, weight)
+    m, n = result.shape
+    chunk_size = max(1, min(m, 256 * 1024 * 1024 // (n * 4)))
+    parts = []
+    for i in range(0, m, chunk_size):
+        end_i = min(i + chunk_size, m)
+        chunk = result[i:end_i].float() * (weight_scale * x_scale[i:end_i])
+        parts.append(chunk.to(out_dtype))
+    result = torch.cat(parts, dim=0)
+    if bias is not None:
+        result = result + bias.to(device=result.device, dtype=result.dtype)
+    return result.reshape(*input_shape[:-1], N)
+
+
+def _int8_linear_kernel(x, weight, weight_scale, bias=None, out_dtype=torch.bfloat16,
+                        convrot=False, convrot_groupsize=256):
+    """Kernel-backed drop-in for comfy_kitchen eager int8_linear (same signature)."""
+    if (_kernel is None or x.device.type != "cuda" or weight.device.type != "cuda"
+            or weight.dtype != torch.int8 or x.dtype not in (torch.bfloat16, torch.float16)):
+        return _orig_int8_linear(x, weight, weight_scale, bias, out_dtype, convrot,
+                                 convrot_groupsize)
+    rows = x.numel() // x.shape[-1]
+    if x.numel() > _LINEAR_MAX_ELEMS or rows * weight.shape[0] > _LINEAR_MAX_ELEMS:
+        return _int8_linear_bounded(x, weight, weight_scale, bias, out_dtype, convrot,
+                                    convrot_groupsize)
+    x_8, x_scale = _quant_cached(x, convrot, convrot_groupsize)
+    return _int8_linear_prequant(x_8, x_scale, weight, weight_scale, bias, out_dtype, x.shape)
+
+
+def _try_int8_kernel_forward(self, input):
+    """Layer output via the kernel W8A8 path, or None to fall back to comfy's forward
+    (eligibility of int8_linear_kernel_mps.py:779-830)."""
+    if _kernel is None:
+        return None
+    try:
+        from comfy_kitchen.tensor import QuantizedTensor
+    except Exception:
+        return None
+    if not isinstance(input, torch.Tensor) or input.device.type != "cuda":
+        return None
+    if isinstance(input, QuantizedTensor):
+        return None
+    w = self.weight
+    if not isinstance(w, QuantizedTensor) or getattr(w, "_layout_cls", None) != "TensorWiseINT8Layout":
+        return None
+    if getattr(self, "_full_precision_mm", False) or getattr(self, "comfy_force_cast_weights", False):
+        return None
+    if len(getattr(self, "weight_function", [])) or len(getattr(self, "bias_function", [])):
+        return None
+    params = w._params
+    if getattr(params, "transposed", False):
+        return None
+    return _int8_linear_kernel(input, w._qdata, params.scale, self.bias, input.dtype,
+                               getattr(params, "convrot", False),
+                               getattr(params, "convrot_groupsize", 256))
+
+
+def _load_kernel():
+    if not (_common.is_b200() and _common.native_ready()):
+        print(f"{TAG} b200q library unavailable or device is not a B200; route not installed.")
+        return None
+    return _NativeInt8Kernel()
+
+
+def install():
+    global _installed, _orig_int8_linear, _kernel
+    if _installed:
+        return
+    if os.environ.get("ASFP8_INT8_EXT") != "1":
+        return
+    if not torch.cuda.is_available():
+        return
+    _kernel = _load_kernel()
+    if _kernel is None:
+        return
+    try:
+        from comfy_kitchen.backends.eager.quantization import int8_linear as _orig
+        _orig_int8_linear = _orig
+    except Exception as e:
+        print(f"{TAG} could not import eager int8_linear: {e!r}")
+        return
+    try:
+        import comfy.ops as ops
+        orig_factory = ops.mixed_precision_ops
+        if getattr(orig_factory, "_asfp8_wrapped", False):
+            _installed = True
+            return
+        factory_signature = inspect.signature(orig_factory)
+
+        def wrapped_factory(*a, **k):
+            bound = factory_signature.bind(*a, **k)
+            disabled = bound.arguments.get("disabled")
+            if disabled is not None:
+                # comfy's hardware probe does not know this route; keep every
+                # other exclusion and precision request intact.
+                bound.arguments["disabled"] = [f for f in disabled if f != "int8_tensorwise"]
+            cls = orig_factory(*bound.args, **bound.kwargs)
+            linear_cls = getattr(cls, "Linear", None)
+            if linear_cls is not None and not getattr(linear_cls, "_asfp8_int8_patched", False):
+                orig_forward = linear_cls.forward
+
+                def forward(self, input, *args, **kwargs):
+                    res = _try_int8_kernel_forward(self, input)
+                    if res is not None:
+                        return res
+                    return orig_forward(self, input, *args, **kwargs)
+
+                linear_cls.forward = forward
+                linear_cls._asfp8_int8_patched = True
+            return cls
+
+        wrapped_factory._asfp8_wrapped = True
+        ops.mixed_precision_ops = wrapped_factory
+
+        if hasattr(ops, "linear_input_act") and not getattr(ops.linear_input_act, "_asfp8_wrapped", False):
+            _orig_lia = ops.linear_input_act
+
+            def linear_input_act_wrapped(linear, x, input_act, *args, **kwargs):
+                # Extended contracts (norm weights / residual epilogues) and the
+                # SwiGLU bridge stay on comfy's helper; a plain merged projection
+                # goes through Linear.forward, i.e. through this route.
+                if args or kwargs:
+                    return _orig_lia(linear, x, input_act, *args, **kwargs)
+                if (input_act is None and isinstance(linear, torch.nn.Module)
+                        and os.environ.get("ASFP8_INT8_PLAIN_LIA", "1") == "1"):
+                    return linear(x)
+                return _orig_lia(linear, x, input_act)
+
+            linear_input_act_wrapped._asfp8_wrapped = True
+            ops.linear_input_act = linear_input_act_wrapped
+    except Exception as e:
+        print(f"{TAG} could not wrap mixed_precision_ops: {e!r}")
+        return
+    _installed = True
+    print(f"{TAG} comfy int8_tensorwise Linear routed to the b200q W8A8 kernels "
+          f"(rowwise quant -> tcgen05 int8 GEMM -> fused dequant epilogue).")

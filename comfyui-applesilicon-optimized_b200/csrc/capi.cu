@@ -1,0 +1,455 @@
+// C ABI launch layer of the b200q kernels (declarations: include/b200q.h).
+//
+// Host-side responsibilities: validate every pointer/shape/stride before a
+// launch, pick the tensor-core (TMA) path when the operands satisfy TMA's
+// 16-byte rules and the SIMT path otherwise, encode the TMA descriptors, size
+// persistent grids to the SM count, and launch on the caller's stream.  No
+// device memory is allocated here and no call synchronises the device (except
+// b200q_get_device_status, which exists to read the device status word).
+#include <atomic>
+#include <cstdio>
+#include <mutex>
+
+#include "../../include/b200q.h"
+#include "gemm8.cuh"
+#include "quant.cuh"
+#include "w8a16.cuh"
+
+using namespace b200q;
+
+namespace {
+
+std::atomic<uint64_t> g_launches{0};
+
+struct DeviceInfo {
+  bool init = false;
+  bool sm100 = false;
+  int num_sms = 0;
+};
+DeviceInfo g_dev[64];
+std::mutex g_dev_mu;
+
+// Returns nullptr if the current device cannot run sm_100a code.
+const DeviceInfo* current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.init) {
+    int major = 0, minor = 0, sms = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    d.sm100 = (major == 10 && minor == 0);
+    d.num_sms = sms > 0 ? sms : 148;
+    d.init = true;
+  }
+  return d.sm100 ? &d : nullptr;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<EncodeTiledFn>(nullptr);
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+// 2-D row-major tensor [rows, cols] with row stride `ld_bytes`; box = box_cols x box_rows.
+bool make_tmap(CUtensorMap* map, const void* base, CUtensorMapDataType dt, uint64_t cols,
+               uint64_t rows, uint64_t ld_bytes, uint32_t box_cols, uint32_t box_rows,
+               CUtensorMapSwizzle sw) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int finish_launch() {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    fprintf(stderr, "[b200q] launch failed: %s\n", cudaGetErrorString(e));
+    return B200Q_ERR_CUDA;
+  }
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return B200Q_OK;
+}
+
+template <typename Kern>
+bool set_smem(Kern kern, int bytes) {
+  // Idempotent and cheap; done per call so multi-device processes stay correct.
+  return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) ==
+         cudaSuccess;
+}
+
+bool valid_dims(int64_t M, int64_t N, int64_t K) {
+  return M >= 0 && N >= 0 && K >= 0 && M < (int64_t(1) << 31) && N < (int64_t(1) << 31) &&
+         K < (int64_t(1) << 31);
+}
+
+// ------------------------------------------------------------ 8-bit GEMM dispatch
+template <MmaKind KIND, int BN, int STAGES, int EPI>
+int launch_gemm8_tc(const DeviceInfo* d, const void* a, int64_t lda, const void* w, int64_t ldw,
+                    int M, int N, int K, const EpiArgs& ep, cudaStream_t st) {
+  CUtensorMap ta, tb;
+  if (!make_tmap(&ta, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M, lda, kGemmBK, kGemmBM,
+                 CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tmap(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldw, kGemmBK, BN,
+                 CU_TENSOR_MAP_SWIZZLE_128B))
+    return B200Q_ERR_CUDA;
+  auto kern = gemm8_tc_kernel<KIND, BN, STAGES, EPI>;
+  constexpr int smem = Gemm8Layout<BN, STAGES>::kSmemBytes;
+  if (!set_smem(kern, smem)) return B200Q_ERR_CUDA;
+  const int64_t tiles = int64_t((M + kGemmBM - 1) / kGemmBM) * ((N + BN - 1) / BN);
+  const int grid = static_cast<int>(tiles < d->num_sms ? tiles : d->num_sms);
+  kern<<<grid, kGemmThreads, smem, st>>>(ta, tb, M, N, K, ep);
+  return finish_launch();
+}
+
+template <bool IS_FP8, int EPI>
+int launch_gemm8_simt(const void* a, int64_t lda, const void* w, int64_t ldw, int M, int N, int K,
+                      const EpiArgs& ep, cudaStream_t st) {
+  dim3 grid((N + 63) / 64, (M + 63) / 64);
+  if (grid.y > 65535u) return B200Q_ERR_INVALID;
+  gemm8_simt_kernel<IS_FP8, EPI><<<grid, 256, 0, st>>>(static_cast<const uint8_t*>(a), lda,
+                                                        static_cast<const uint8_t*>(w), ldw, M, N,
+                                                        K, ep);
+  return finish_launch();
+}
+
+template <MmaKind KIND, int EPI>
+int gemm8(const void* a, int64_t lda, const void* w, int64_t ldw, int64_t M, int64_t N, int64_t K,
+          const EpiArgs& ep, cudaStream_t st) {
+  const DeviceInfo* d = current_device();
+  if (!d) return B200Q_ERR_UNSUPPORTED;
+  if (M == 0 || N == 0) return B200Q_OK;
+  const bool tc = K > 0 && (K % 16 == 0) && (lda % 16 == 0) && (ldw % 16 == 0) && aligned16(a) &&
+                  aligned16(w);
+  constexpr bool kFp8 = KIND == MmaKind::F8F6F4;
+  if (!tc) return launch_gemm8_simt<kFp8, EPI>(a, lda, w, ldw, int(M), int(N), int(K), ep, st);
+  if (N <= 128)
+    return launch_gemm8_tc<KIND, 128, 6, EPI>(d, a, lda, w, ldw, int(M), int(N), int(K), ep, st);
+  return launch_gemm8_tc<KIND, 256, 4, EPI>(d, a, lda, w, ldw, int(M), int(N), int(K), ep, st);
+}
+
+EpiArgs make_epi(void* out, int64_t ldo, int out_dtype, int64_t M, int64_t N) {
+  EpiArgs e{};
+  e.out = out;
+  e.ldo = ldo;
+  e.out_dtype = out_dtype;
+  e.bias_dtype = kBiasNone;
+  e.act = kActNone;
+  e.M = static_cast<int>(M);
+  e.N = static_cast<int>(N);
+  return e;
+}
+
+// ------------------------------------------------------------ W8A16 planning
+struct W16Plan {
+  int bt;
+  int splits;
+  size_t partial_bytes;
+  size_t counter_bytes;
+};
+
+W16Plan w8a16_plan(int num_sms, int64_t M, int64_t N, int64_t K) {
+  W16Plan p{};
+  p.bt = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+  const int64_t num_n = (N + kW16BM - 1) / kW16BM;
+  const int64_t num_t = (M + p.bt - 1) / p.bt;
+  const int64_t tiles = num_n * num_t;
+  const int64_t num_kb = (K + kW16BK - 1) / kW16BK;
+  int best = 1;
+  double best_eff = 0.0;
+  for (int s = 1; s <= 8; ++s) {
+    if (s > 1 && s * 4 > num_kb) break;
+    // fp32 partial write + read must stay small next to the fp8 weight stream
+    if (s > 1 && double(s) * M * N * 8.0 > 0.5 * double(N) * K) break;
+    const int64_t units = tiles * s;
+    const int64_t waves = (units + num_sms - 1) / num_sms;
+    const double eff = double(units) / double(waves * num_sms);
+    if (eff > best_eff + 0.02) {
+      best_eff = eff;
+      best = s;
+    }
+  }
+  p.splits = best;
+  if (best > 1) {
+    p.partial_bytes = size_t(best) * size_t(M) * size_t(N) * sizeof(float);
+    p.counter_bytes = size_t(tiles) * sizeof(unsigned int);
+  }
+  return p;
+}
+
+template <int BT, bool XF16>
+int launch_w8a16_tc(const DeviceInfo* d, const void* x, int64_t ldx, const uint8_t* w, int64_t ldw,
+                    const W8A16Args& args, const EpiArgs& ep, cudaStream_t st) {
+  CUtensorMap tx, tw;
+  const CUtensorMapDataType xdt = XF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if (!make_tmap(&tx, x, xdt, args.K, args.M, ldx * 2, kW16BK, BT, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tmap(&tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, args.K, args.N, ldw, kW16BK, kW16BM,
+                 CU_TENSOR_MAP_SWIZZLE_NONE))
+    return B200Q_ERR_CUDA;
+  auto kern = w8a16_tc_kernel<BT, XF16>;
+  constexpr int smem = W8A16Layout<BT>::kSmemBytes;
+  if (!set_smem(kern, smem)) return B200Q_ERR_CUDA;
+  const int64_t units = int64_t((args.N + kW16BM - 1) / kW16BM) * ((args.M + BT - 1) / BT) * args.splits;
+  const int grid = static_cast<int>(units < d->num_sms ? units : d->num_sms);
+  kern<<<grid, kW16Threads, smem, st>>>(tx, tw, args, ep);
+  return finish_launch();
+}
+
+template <bool XF16>
+int dispatch_w8a16_tc(const DeviceInfo* d, int bt, const void* x, int64_t ldx, const uint8_t* w,
+                      int64_t ldw, const W8A16Args& args, const EpiArgs& ep, cudaStream_t st) {
+  switch (bt) {
+    case 16: return launch_w8a16_tc<16, XF16>(d, x, ldx, w, ldw, args, ep, st);
+    case 32: return launch_w8a16_tc<32, XF16>(d, x, ldx, w, ldw, args, ep, st);
+    case 64: return launch_w8a16_tc<64, XF16>(d, x, ldx, w, ldw, args, ep, st);
+    case 128: return launch_w8a16_tc<128, XF16>(d, x, ldx, w, ldw, args, ep, st);
+    default: return launch_w8a16_tc<256, XF16>(d, x, ldx, w, ldw, args, ep, st);
+  }
+}
+
+int grid_for(int64_t work, int per_block, const DeviceInfo* d) {
+  int64_t g = (work + per_block - 1) / per_block;
+  const int64_t cap = int64_t(d->num_sms) * 8;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return static_cast<int>(g);
+}
+
+}  // namespace
+
+// =====================================================================  C ABI
+extern "C" {
+
+int b200q_version(void) { return 1; }
+
+const char* b200q_status_string(int s) {
+  switch (s) {
+    case B200Q_OK: return "ok";
+    case B200Q_ERR_INVALID: return "invalid argument";
+    case B200Q_ERR_UNSUPPORTED: return "unsupported device (b200q kernels need sm_100 / B200)";
+    case B200Q_ERR_CUDA: return "CUDA error";
+    case B200Q_ERR_WORKSPACE: return "workspace too small";
+    default: return "unknown status";
+  }
+}
+
+uint64_t b200q_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int b200q_get_device_status(unsigned int* status, int reset) {
+  if (!status) return B200Q_ERR_INVALID;
+  if (cudaMemcpyFromSymbol(status, g_device_status, sizeof(unsigned int)) != cudaSuccess)
+    return B200Q_ERR_CUDA;
+  if (reset) {
+    const unsigned int zero = 0;
+    if (cudaMemcpyToSymbol(g_device_status, &zero, sizeof(unsigned int)) != cudaSuccess)
+      return B200Q_ERR_CUDA;
+  }
+  return B200Q_OK;
+}
+
+int b200q_quant_rowwise_i8(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
+                           int8_t* q, int64_t ldq, float* scales, void* stream) {
+  if (!x || !q || !scales || M < 0 || K <= 0 || ldx < K || ldq < K || M >= (int64_t(1) << 31) ||
+      (x_dtype != B200Q_BF16 && x_dtype != B200Q_F16))
+    return B200Q_ERR_INVALID;
+  const DeviceInfo* d = current_device();
+  if (!d) return B200Q_ERR_UNSUPPORTED;
+  if (M == 0) return B200Q_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int grid = static_cast<int>(M < int64_t(d->num_sms) * 16 ? M : int64_t(d->num_sms) * 16);
+  const bool vec = (K % 8 == 0) && (ldx % 8 == 0) && (ldq % 8 == 0) && aligned16(x) &&
+                   (reinterpret_cast<uintptr_t>(q) % 8 == 0);
+  if (x_dtype == B200Q_BF16) {
+    auto* xp = static_cast<const __nv_bfloat16*>(x);
+    if (vec) quant_rowwise_i8_vec_kernel<__nv_bfloat16><<<grid, kQuantThreads, 0, st>>>(xp, ldx, q, ldq, scales, int(M), int(K));
+    else quant_rowwise_i8_scalar_kernel<__nv_bfloat16><<<grid, kQuantThreads, 0, st>>>(xp, ldx, q, ldq, scales, int(M), int(K));
+  } else {
+    auto* xp = static_cast<const __half*>(x);
+    if (vec) quant_rowwise_i8_vec_kernel<__half><<<grid, kQuantThreads, 0, st>>>(xp, ldx, q, ldq, scales, int(M), int(K));
+    else quant_rowwise_i8_scalar_kernel<__half><<<grid, kQuantThreads, 0, st>>>(xp, ldx, q, ldq, scales, int(M), int(K));
+  }
+  return finish_launch();
+}
+
+int b200q_i8_matmul_nt(const int8_t* a, int64_t lda, const int8_t* w, int64_t ldw, int32_t* c,
+                       int64_t ldc, int64_t M, int64_t N, int64_t K, void* stream) {
+  if (!a || !w || !c || !valid_dims(M, N, K) || K == 0 || lda < K || ldw < K || ldc < N)
+    return B200Q_ERR_INVALID;
+  EpiArgs ep = make_epi(c, ldc, kOutI32, M, N);
+  return gemm8<MmaKind::I8, kEpiInt32>(a, lda, w, ldw, M, N, K, ep, static_cast<cudaStream_t>(stream));
+}
+
+int b200q_i8_matmul_nt_dequant(const int8_t* a, int64_t lda, const int8_t* w, int64_t ldw,
+                               const float* row_scale, const float* col_scale,
+                               int64_t col_scale_numel, const void* bias, int act, void* out,
+                               int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K,
+                               void* stream) {
+  if (!a || !w || !out || !row_scale || !col_scale || !valid_dims(M, N, K) || K == 0 || lda < K ||
+      ldw < K || ldo < N || (col_scale_numel != 1 && col_scale_numel != N) ||
+      (out_dtype != B200Q_BF16 && out_dtype != B200Q_F16) || act < B200Q_ACT_NONE ||
+      act > B200Q_ACT_GELU_ERF)
+    return B200Q_ERR_INVALID;
+  EpiArgs ep = make_epi(out, ldo, out_dtype, M, N);
+  ep.row_scale = row_scale;
+  ep.row_scale_vec = 1;
+  ep.col_scale = col_scale;
+  ep.col_scale_vec = col_scale_numel == N && N != 1 ? 1 : 0;
+  if (col_scale_numel == 1) ep.col_scale_vec = 0;
+  ep.bias = bias;
+  ep.bias_dtype = bias ? (out_dtype == B200Q_BF16 ? kBiasBF16 : kBiasF16) : kBiasNone;
+  ep.act = act;
+  return gemm8<MmaKind::I8, kEpiI8Dequant>(a, lda, w, ldw, M, N, K, ep, static_cast<cudaStream_t>(stream));
+}
+
+int b200q_i8_linear(const void* x, int x_dtype, int64_t ldx, const int8_t* w, int64_t ldw,
+                    const float* col_scale, int64_t col_scale_numel, const void* bias, int act,
+                    void* out, int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K,
+                    int8_t* q_scratch, float* scale_scratch, void* stream) {
+  int s = b200q_quant_rowwise_i8(x, x_dtype, M, K, ldx, q_scratch, K, scale_scratch, stream);
+  if (s != B200Q_OK) return s;
+  return b200q_i8_matmul_nt_dequant(q_scratch, K, w, ldw, scale_scratch, col_scale,
+                                    col_scale_numel, bias, act, out, out_dtype, ldo, M, N, K,
+                                    stream);
+}
+
+int b200q_fp8_scaled_mm(const uint8_t* a, int64_t lda, const uint8_t* w, int64_t ldw,
+                        const float* scale_a, int64_t scale_a_numel, const float* scale_b,
+                        int64_t scale_b_numel, const float* scale_result, const void* bias,
+                        int bias_dtype, int act, void* out, int out_dtype, int64_t ldo, int64_t M,
+                        int64_t N, int64_t K, void* stream) {
+  if (!a || !w || !out || !valid_dims(M, N, K) || K == 0 || lda < K || ldw < K || ldo < N ||
+      (scale_a && scale_a_numel != 1 && scale_a_numel != M) ||
+      (scale_b && scale_b_numel != 1 && scale_b_numel != N) ||
+      (out_dtype != B200Q_BF16 && out_dtype != B200Q_F16 && out_dtype != B200Q_F32) ||
+      bias_dtype < B200Q_BIAS_NONE || bias_dtype > B200Q_BIAS_F32 || (bias_dtype != B200Q_BIAS_NONE && !bias) ||
+      act < B200Q_ACT_NONE || act > B200Q_ACT_GELU_ERF)
+    return B200Q_ERR_INVALID;
+  EpiArgs ep = make_epi(out, ldo, out_dtype, M, N);
+  ep.row_scale = scale_a;
+  ep.row_scale_vec = scale_a && scale_a_numel == M && M != 1 ? 1 : 0;
+  ep.col_scale = scale_b;
+  ep.col_scale_vec = scale_b && scale_b_numel == N && N != 1 ? 1 : 0;
+  ep.extra_scale = scale_result;
+  ep.bias = bias;
+  ep.bias_dtype = bias ? bias_dtype : kBiasNone;
+  ep.act = act;
+  return gemm8<MmaKind::F8F6F4, kEpiScaled>(a, lda, w, ldw, M, N, K, ep, static_cast<cudaStream_t>(stream));
+}
+
+int b200q_fp8_quant_tensorwise(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
+                               uint8_t* q, int64_t ldq, float* scale, unsigned int* amax_scratch,
+                               void* stream) {
+  if (!x || !q || !scale || !amax_scratch || M < 0 || K <= 0 || ldx < K || ldq < K ||
+      (x_dtype != B200Q_BF16 && x_dtype != B200Q_F16))
+    return B200Q_ERR_INVALID;
+  const DeviceInfo* d = current_device();
+  if (!d) return B200Q_ERR_UNSUPPORTED;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(amax_scratch, 0, sizeof(unsigned int), st) != cudaSuccess) return B200Q_ERR_CUDA;
+  const int64_t total = M * K;
+  const int grid = grid_for(total / 8 + 1, 256, d);
+  if (x_dtype == B200Q_BF16) {
+    auto* xp = static_cast<const __nv_bfloat16*>(x);
+    absmax_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(xp, ldx, M, int(K), amax_scratch);
+    int s = finish_launch();
+    if (s) return s;
+    fp8_quantize_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(xp, ldx, M, int(K), amax_scratch, q, ldq, scale);
+  } else {
+    auto* xp = static_cast<const __half*>(x);
+    absmax_kernel<__half><<<grid, 256, 0, st>>>(xp, ldx, M, int(K), amax_scratch);
+    int s = finish_launch();
+    if (s) return s;
+    fp8_quantize_kernel<__half><<<grid, 256, 0, st>>>(xp, ldx, M, int(K), amax_scratch, q, ldq, scale);
+  }
+  return finish_launch();
+}
+
+size_t b200q_w8a16_workspace_size(int64_t M, int64_t N, int64_t K) {
+  const DeviceInfo* d = current_device();
+  const int sms = d ? d->num_sms : 148;
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  const W16Plan p = w8a16_plan(sms, M, N, K);
+  if (p.splits <= 1) return 0;
+  return ((p.partial_bytes + 255) & ~size_t(255)) + p.counter_bytes;
+}
+
+int b200q_w8a16_linear(const void* x, int x_dtype, int64_t ldx, const uint8_t* w, int64_t ldw,
+                       const float* w_scale, const void* bias, int bias_dtype, int act, void* out,
+                       int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+  if (!x || !w || !out || !valid_dims(M, N, K) || K == 0 || ldx < K || ldw < K || ldo < N ||
+      (x_dtype != B200Q_BF16 && x_dtype != B200Q_F16) ||
+      (out_dtype != B200Q_BF16 && out_dtype != B200Q_F16 && out_dtype != B200Q_F32) ||
+      bias_dtype < B200Q_BIAS_NONE || bias_dtype > B200Q_BIAS_F32 || (bias_dtype != B200Q_BIAS_NONE && !bias) ||
+      act < B200Q_ACT_NONE || act > B200Q_ACT_GELU_ERF)
+    return B200Q_ERR_INVALID;
+  const DeviceInfo* d = current_device();
+  if (!d) return B200Q_ERR_UNSUPPORTED;
+  if (M == 0 || N == 0) return B200Q_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  EpiArgs ep = make_epi(out, ldo, out_dtype, M, N);
+  ep.extra_scale = w_scale;
+  ep.bias = bias;
+  ep.bias_dtype = bias ? bias_dtype : kBiasNone;
+  ep.act = act;
+  const bool tc = (K % 16 == 0) && (ldw % 16 == 0) && (ldx % 8 == 0) && aligned16(x) && aligned16(w);
+  if (!tc) {
+    dim3 grid((N + 31) / 32, (M + 31) / 32);
+    if (grid.y > 65535u) return B200Q_ERR_INVALID;
+    if (x_dtype == B200Q_BF16)
+      w8a16_simt_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), ldx, w, ldw, int(M), int(N), int(K), ep);
+    else
+      w8a16_simt_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(x), ldx, w, ldw, int(M), int(N), int(K), ep);
+    return finish_launch();
+  }
+  const W16Plan p = w8a16_plan(d->num_sms, M, N, K);
+  W8A16Args args{};
+  args.M = int(M);
+  args.N = int(N);
+  args.K = int(K);
+  args.splits = p.splits;
+  if (p.splits > 1) {
+    const size_t part = (p.partial_bytes + 255) & ~size_t(255);
+    if (!workspace || workspace_bytes < part + p.counter_bytes || !aligned16(workspace))
+      return B200Q_ERR_WORKSPACE;
+    args.partial = static_cast<float*>(workspace);
+    args.counters = reinterpret_cast<unsigned int*>(static_cast<uint8_t*>(workspace) + part);
+    if (cudaMemsetAsync(args.counters, 0, p.counter_bytes, st) != cudaSuccess) return B200Q_ERR_CUDA;
+  }
+  if (x_dtype == B200Q_F16) return dispatch_w8a16_tc<true>(d, p.bt, x, ldx, w, ldw, args, ep, st);
+  return dispatch_w8a16_tc<false>(d, p.bt, x, ldx, w, ldw, args, ep, st);
+}
+
+int b200q_fp8_decode(const uint8_t* src, int64_t n, int fp8_kind, void* dst, int out_dtype,
+                     void* stream) {
+  if (!src || !dst || n < 0 || (fp8_kind != B200Q_FP8_E4M3 && fp8_kind != B200Q_FP8_E5M2) ||
+      (out_dtype != B200Q_BF16 && out_dtype != B200Q_F16 && out_dtype != B200Q_F32))
+    return B200Q_ERR_INVALID;
+  const DeviceInfo* d = current_device();
+  if (!d) return B200Q_ERR_UNSUPPORTED;
+  if (n == 0) return B200Q_OK;
+  fp8_decode_kernel<<<grid_for(n, 256, d), 256, 0, static_cast<cudaStream_t>(stream)>>>(src, n, fp8_kind, dst, out_dtype);
+  return finish_launch();
+}
+
+}  // extern "C"

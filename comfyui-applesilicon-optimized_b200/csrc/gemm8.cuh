@@ -1,0 +1,341 @@
+// 8-bit x 8-bit GEMM on the sm_100a tensor cores:  C[M,N] = A[M,K] . W[N,K]^T
+// (the "NT" layout of the reference, int8_gemm.mm:4), both operands K-major.
+//
+//  kind::i8      int8 x int8 -> int32 in TMEM   (INT8 W8A8 route, torch._int_mm)
+//  kind::f8f6f4  e4m3 x e4m3 -> fp32 in TMEM    (FP8 W8A8 route, torch._scaled_mm)
+//
+// Structure (one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: 128x128-byte A tile + BNx128-byte W tile per stage,
+//               128-byte swizzle, STAGES-deep mbarrier ring.
+//   warp 1      MMA issuer: one elected thread issues 4 tcgen05.mma (K=32 each)
+//               per stage into a TMEM accumulator; tcgen05.commit frees the stage.
+//   warp 2      TMEM allocator (2 x BN columns: double-buffered accumulator so the
+//               epilogue of tile i overlaps the MMAs of tile i+1).
+//   warps 4..7  epilogue: tcgen05.ld 32 columns at a time, per-element epilogue
+//               (raw int32 / reference two-rounding INT8 dequant / FP8 scaled
+//               + bias + GELU), vectorised global stores.
+// Tiles are walked in groups of 16 M-tiles so the ~148 concurrently running
+// tiles share A row panels and W column panels in L2.
+#pragma once
+
+#include "numerics.cuh"
+#include "ptx.cuh"
+
+namespace b200q {
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBK = 128;  // bytes = elements per k-block (one 128B swizzle atom)
+constexpr int kGemmThreads = 256;
+constexpr int kGemmGroupM = 16;
+
+enum EpiMode : int { kEpiInt32 = 0, kEpiI8Dequant = 1, kEpiScaled = 2 };
+
+template <int BN, int STAGES>
+struct Gemm8Layout {
+  static constexpr int kATile = kGemmBM * kGemmBK;
+  static constexpr int kBTile = BN * kGemmBK;
+  static constexpr int kStageBytes = kATile + kBTile;
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  // full[S], empty[S], acc_full[2], acc_empty[2], tmem slot, abort flag
+  static constexpr int kBarBytes = (2 * STAGES + 4) * 8 + 16;
+  static constexpr int kSmemBytes = kBarOffset + kBarBytes + 1024;  // + alignment slack
+  static constexpr uint32_t kTmemCols = 2 * BN;
+};
+
+__device__ __forceinline__ void gemm_tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
+  const int group_size = kGemmGroupM * num_n;
+  const int g = tile / group_size;
+  const int first_m = g * kGemmGroupM;
+  const int gm = min(num_m - first_m, kGemmGroupM);
+  const int idx = tile - g * group_size;
+  mb = first_m + idx % gm;
+  nb = idx / gm;
+}
+
+template <int EPI>
+__device__ __forceinline__ float epi_value(uint32_t raw, float rs, float cs, float xs,
+                                           const EpiArgs& e, int n, bool acc_is_int) {
+  if constexpr (EPI == kEpiI8Dequant) {
+    return epi_i8_dequant(static_cast<int32_t>(raw), rs, cs, e, n);
+  } else {
+    const float acc = acc_is_int ? __int2float_rn(static_cast<int32_t>(raw)) : __uint_as_float(raw);
+    return epi_scaled(acc, rs, cs, xs, e, n);
+  }
+}
+
+// Stores 32 accumulator columns [n0, n0+32) of row m.
+template <int EPI>
+__device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int64_t m, int n0,
+                                               const EpiArgs& e, float rs, float xs,
+                                               bool acc_is_int) {
+  if constexpr (EPI == kEpiInt32) {
+    int32_t* out = static_cast<int32_t*>(e.out) + m * e.ldo;
+    const bool vec = (n0 + 32 <= e.N) && ((e.ldo & 3) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(e.out) & 15) == 0);
+    if (vec) {
+      int4* o = reinterpret_cast<int4*>(out + n0);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        o[j] = make_int4(static_cast<int>(r[4 * j]), static_cast<int>(r[4 * j + 1]),
+                         static_cast<int>(r[4 * j + 2]), static_cast<int>(r[4 * j + 3]));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n0 + j < e.N) out[n0 + j] = static_cast<int32_t>(r[j]);
+    }
+  } else {
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int n = min(n0 + j, e.N - 1);
+      const float cs = e.col_scale ? __ldg(e.col_scale + (e.col_scale_vec ? n : 0)) : 1.0f;
+      v[j] = epi_value<EPI>(r[j], rs, cs, xs, e, n, acc_is_int);
+    }
+    const bool full = (n0 + 32 <= e.N);
+    if (e.out_dtype == kOutBF16 || e.out_dtype == kOutF16) {
+      const bool vec = full && ((e.ldo & 7) == 0) && ((reinterpret_cast<uintptr_t>(e.out) & 15) == 0);
+      if (vec) {
+        uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(e.out) + m * e.ldo + n0);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint4 w;
+          if (e.out_dtype == kOutBF16) {
+            w.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+            w.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+            w.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+            w.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+          } else {
+            w.x = pack_f16x2(v[8 * j + 0], v[8 * j + 1]);
+            w.y = pack_f16x2(v[8 * j + 2], v[8 * j + 3]);
+            w.z = pack_f16x2(v[8 * j + 4], v[8 * j + 5]);
+            w.w = pack_f16x2(v[8 * j + 6], v[8 * j + 7]);
+          }
+          o[j] = w;
+        }
+        return;
+      }
+    } else if (full && ((e.ldo & 3) == 0) && ((reinterpret_cast<uintptr_t>(e.out) & 15) == 0)) {
+      float4* o = reinterpret_cast<float4*>(static_cast<float*>(e.out) + m * e.ldo + n0);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      return;
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (n0 + j < e.N) store_out(e, m, n0 + j, v[j]);
+  }
+}
+
+template <MmaKind KIND, int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    int M, int N, int K, EpiArgs ep) {
+  using L = Gemm8Layout<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * L::kATile;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_m = (M + kGemmBM - 1) / kGemmBM;
+  const int num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (K + kGemmBK - 1) / kGemmBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4 * 32);
+    }
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int mb, nb;
+        gemm_tile_coords(tile, num_m, num_n, mb, nb);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+          tma_load_2d(&tmA, &full[stage], sA + stage * L::kATile, kb * kGemmBK, mb * kGemmBM);
+          tma_load_2d(&tmB, &full[stage], sB + stage * L::kBTile, kb * kGemmBK, nb * BN);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdesc =
+          KIND == MmaKind::I8 ? make_idesc(2, 1, 1, kGemmBM, BN)   // s32 <- s8 x s8
+                              : make_idesc(1, 0, 0, kGemmBM, BN);  // f32 <- e4m3 x e4m3
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++it) {
+        const int buf = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&acc_empty[buf], acc_phase ^ 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t adesc = make_sw128_desc(smem_u32(sA + stage * L::kATile));
+          const uint64_t bdesc = make_sw128_desc(smem_u32(sB + stage * L::kBTile));
+#pragma unroll
+          for (int k = 0; k < kGemmBK / 32; ++k) {
+            // +32 bytes along K inside the swizzle atom = +2 in the >>4 address field
+            umma_ss<KIND>(d_tmem, adesc + 2 * k, bdesc + 2 * k, kIdesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (ok) umma_commit(&acc_full[buf]);
+      }
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_local = q * 32 + lane;
+    const float xs = ep.extra_scale ? __ldg(ep.extra_scale) : 1.0f;
+    constexpr bool kAccInt = KIND == MmaKind::I8;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+      int mb, nb;
+      gemm_tile_coords(tile, num_m, num_n, mb, nb);
+      const int buf = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait_warp(&acc_full[buf], acc_phase, abort_flag)) break;
+      tc_fence_after();
+      const int64_t m = static_cast<int64_t>(mb) * kGemmBM + row_local;
+      const bool row_ok = m < M;
+      float rs = 1.0f;
+      if (EPI != kEpiInt32 && ep.row_scale && row_ok) rs = __ldg(ep.row_scale + (ep.row_scale_vec ? m : 0));
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(taddr + c * 32, r);
+        tmem_ld_wait();
+        const int n0 = nb * BN + c * 32;
+        if (row_ok && n0 < N) epilogue_chunk<EPI>(r, m, n0, ep, rs, xs, kAccInt);
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 2) tmem_dealloc(tmem_base, L::kTmemCols);
+}
+
+// ---------------------------------------------------------------------------
+// SIMT fallback for shapes the TMA path cannot describe (K or a row stride not a
+// multiple of 16 bytes, unaligned base pointers).  Same epilogues; int8 sums are
+// exact, fp8 sums accumulate in fp32.  64x64 tile, 256 threads, 4x4 per thread.
+template <bool IS_FP8, int EPI>
+__global__ void __launch_bounds__(256)
+    gemm8_simt_kernel(const uint8_t* __restrict__ A, int64_t lda, const uint8_t* __restrict__ B,
+                      int64_t ldb, int M, int N, int K, EpiArgs ep) {
+  constexpr int T = 64, TK = 32;
+  using Acc = typename std::conditional<IS_FP8, float, int32_t>::type;
+  __shared__ Acc sa[TK][T + 1];
+  __shared__ Acc sb[TK][T + 1];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int m0 = blockIdx.y * T, n0 = blockIdx.x * T;
+  Acc acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = Acc(0);
+  for (int k0 = 0; k0 < K; k0 += TK) {
+    for (int i = threadIdx.x; i < T * TK; i += 256) {
+      const int r = i / TK, k = i % TK;
+      const int gm = m0 + r, gn = n0 + r, gk = k0 + k;
+      Acc va = Acc(0), vb = Acc(0);
+      if (gm < M && gk < K) {
+        const uint8_t b = A[static_cast<int64_t>(gm) * lda + gk];
+        if constexpr (IS_FP8) va = decode_e4m3(b); else va = static_cast<int8_t>(b);
+      }
+      if (gn < N && gk < K) {
+        const uint8_t b = B[static_cast<int64_t>(gn) * ldb + gk];
+        if constexpr (IS_FP8) vb = decode_e4m3(b); else vb = static_cast<int8_t>(b);
+      }
+      sa[k][r] = va;
+      sb[k][r] = vb;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int k = 0; k < TK; ++k) {
+      Acc a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = sa[k][ty + 16 * i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = sb[k][tx + 16 * j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] += a[i] * b[j];
+    }
+    __syncthreads();
+  }
+  const float xs = ep.extra_scale ? *ep.extra_scale : 1.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int m = m0 + ty + 16 * i;
+    if (m >= M) continue;
+    const float rs = ep.row_scale ? ep.row_scale[ep.row_scale_vec ? m : 0] : 1.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + tx + 16 * j;
+      if (n >= N) continue;
+      if constexpr (EPI == kEpiInt32) {
+        static_cast<int32_t*>(ep.out)[static_cast<int64_t>(m) * ep.ldo + n] = static_cast<int32_t>(acc[i][j]);
+      } else {
+        const float cs = ep.col_scale ? ep.col_scale[ep.col_scale_vec ? n : 0] : 1.0f;
+        uint32_t raw;
+        if constexpr (IS_FP8) raw = __float_as_uint(static_cast<float>(acc[i][j]));
+        else raw = static_cast<uint32_t>(acc[i][j]);
+        store_out(ep, m, n, epi_value<EPI>(raw, rs, cs, xs, ep, n, !IS_FP8));
+      }
+    }
+  }
+}
+
+}  // namespace b200q

@@ -1,0 +1,160 @@
+// Scalar numerics shared by every b200q kernel: rounding to 16-bit floats,
+// FP8 (e4m3) encode/decode, GELU, and the element-wise GEMM epilogues.
+//
+// This translation unit is compiled WITHOUT --use_fast_math and every
+// multiply/add that must reproduce the reference's fp32 arithmetic uses the
+// explicit round-to-nearest intrinsics (__fmul_rn / __fadd_rn / __fdiv_rn), so
+// the compiler cannot contract them into FMAs or approximate divides.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <stdint.h>
+
+namespace b200q {
+
+enum OutDtype : int { kOutBF16 = 0, kOutF16 = 1, kOutF32 = 2, kOutI32 = 3 };
+enum BiasDtype : int { kBiasNone = 0, kBiasBF16 = 1, kBiasF16 = 2, kBiasF32 = 3 };
+enum Act : int { kActNone = 0, kActGeluTanh = 1, kActGeluErf = 2 };
+
+// float -> 16-bit float -> float, round to nearest even.
+__device__ __forceinline__ float round_bf16(float v) {
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
+__device__ __forceinline__ float round_f16(float v) { return __half2float(__float2half_rn(v)); }
+
+template <typename T>
+__device__ __forceinline__ float to_float(T v);
+template <>
+__device__ __forceinline__ float to_float<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+template <>
+__device__ __forceinline__ float to_float<__half>(__half v) {
+  return __half2float(v);
+}
+
+// FP8 e4m3 (OCP "fn" variant: no infinities, 0x7F/0xFF are NaN).
+__device__ __forceinline__ uint8_t encode_e4m3_sat(float v) {
+  return static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
+}
+__device__ __forceinline__ float decode_e4m3(uint8_t b) {
+  __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(b), __NV_E4M3);
+  return __half2float(__half(h));
+}
+__device__ __forceinline__ float decode_e5m2(uint8_t b) {
+  __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(b), __NV_E5M2);
+  return __half2float(__half(h));
+}
+
+// Two e4m3 codes (low byte first) -> two bf16 packed in 32 bits.  Exact: every
+// e4m3 value is an fp16 normal and a bf16 value.
+__device__ __forceinline__ uint32_t e4m3x2_to_bf16x2(uint16_t two) {
+  __half2_raw h2 = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(two), __NV_E4M3);
+  float2 f = __half22float2(__half2(h2));
+  __nv_bfloat162 b = __float22bfloat162_rn(f);
+  return *reinterpret_cast<uint32_t*>(&b);
+}
+
+// GELU with the tanh approximation (torch approximate="tanh") and exact erf GELU.
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
+  const float k1 = 0.044715f;
+  float inner = k0 * (x + k1 * x * x * x);
+  return 0.5f * x * (1.0f + tanhf(inner));
+}
+__device__ __forceinline__ float gelu_erf(float x) {
+  return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f));
+}
+__device__ __forceinline__ float apply_act(float v, int act) {
+  if (act == kActGeluTanh) return gelu_tanh(v);
+  if (act == kActGeluErf) return gelu_erf(v);
+  return v;
+}
+
+__device__ __forceinline__ float load_bias(const void* bias, int dtype, int n) {
+  if (dtype == kBiasBF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(bias)[n]);
+  if (dtype == kBiasF16) return __half2float(static_cast<const __half*>(bias)[n]);
+  if (dtype == kBiasF32) return static_cast<const float*>(bias)[n];
+  return 0.0f;
+}
+
+// Everything an epilogue needs besides the accumulator.  Scale pointers may be
+// null (factor 1, multiply skipped); *_vec = 0 broadcasts element 0.
+struct EpiArgs {
+  void* out;
+  int64_t ldo;  // elements
+  int out_dtype;
+  const float* row_scale;
+  int row_scale_vec;
+  const float* col_scale;
+  int col_scale_vec;
+  const float* extra_scale;  // one scalar (scale_result / weight scale), or null
+  const void* bias;
+  int bias_dtype;
+  int act;
+  int M, N;
+};
+
+// The INT8 W8A8 dequant epilogue of the reference (int8_gemm.mm:417-443 and the
+// eager chunked path int8_linear_kernel_mps.py:203-215):
+//   s = col_scale[n] * row_scale[m]           (fp32, this order)
+//   r = OutT(float(C) * s)                    (round #1)
+//   r = OutT(float(r) + float(bias[n]))       (round #2, bias already in OutT)
+// OutT is bf16 (out_dtype 0) or fp16 (out_dtype 1).
+__device__ __forceinline__ float epi_i8_dequant(int32_t c, float rs, float cs, const EpiArgs& e,
+                                                int n) {
+  const float s = __fmul_rn(cs, rs);
+  float v = __fmul_rn(__int2float_rn(c), s);
+  if (e.out_dtype == kOutF16) {
+    v = round_f16(v);
+    if (e.bias_dtype != kBiasNone) v = round_f16(__fadd_rn(v, load_bias(e.bias, e.bias_dtype, n)));
+  } else {
+    v = round_bf16(v);
+    if (e.bias_dtype != kBiasNone)
+      v = round_bf16(__fadd_rn(v, load_bias(e.bias, e.bias_dtype, n)));
+  }
+  // Optional activation on the (already reference-exact) result; the store
+  // rounds once more to OutT.
+  return e.act == kActNone ? v : apply_act(v, e.act);
+}
+
+// The FP8 scaled epilogue (scaled_mm_fp8.py:136-146 order): fp32 accumulator
+// times scale_a[m], scale_b[n], scale_result, plus fp32 bias, optional GELU,
+// one rounding to the output type.
+__device__ __forceinline__ float epi_scaled(float acc, float rs, float cs, float xs,
+                                            const EpiArgs& e, int n) {
+  float v = acc;
+  if (e.row_scale) v = __fmul_rn(v, rs);
+  if (e.col_scale) v = __fmul_rn(v, cs);
+  if (e.extra_scale) v = __fmul_rn(v, xs);
+  if (e.bias_dtype != kBiasNone) v = __fadd_rn(v, load_bias(e.bias, e.bias_dtype, n));
+  return apply_act(v, e.act);
+}
+
+__device__ __forceinline__ void store_out(const EpiArgs& e, int64_t m, int n, float v) {
+  const int64_t off = m * e.ldo + n;
+  switch (e.out_dtype) {
+    case kOutBF16:
+      static_cast<__nv_bfloat16*>(e.out)[off] = __float2bfloat16_rn(v);
+      break;
+    case kOutF16:
+      static_cast<__half*>(e.out)[off] = __float2half_rn(v);
+      break;
+    default:
+      static_cast<float*>(e.out)[off] = v;
+      break;
+  }
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 p = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&p);
+}
+__device__ __forceinline__ uint32_t pack_f16x2(float a, float b) {
+  __half2 p = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&p);
+}
+
+}  // namespace b200q

@@ -1,0 +1,144 @@
+/*
+ * b200q — C ABI of the B200 (sm_100a) quantized DiT-linear kernels.
+ *
+ * Every entry point takes raw device pointers, element strides and sizes, and
+ * the cudaStream_t to launch on (passed as void*; NULL = legacy default stream).
+ * Nothing here allocates device memory: outputs and scratch words are owned by
+ * the caller.  Calls are asynchronous (no device synchronisation) and return
+ * B200Q_OK or an error code; b200q_status_string() names it.  Shapes/strides
+ * are validated on the host before any launch.
+ *
+ * Each declaration cites the reference interface it replaces (paths inside
+ * luix93/ComfyUI-AppleSilicon-Optimized).
+ */
+#ifndef B200Q_H_
+#define B200Q_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define B200Q_API __attribute__((visibility("default")))
+#else
+#define B200Q_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define B200Q_OK 0
+#define B200Q_ERR_INVALID 1     /* bad pointer / shape / stride / dtype argument */
+#define B200Q_ERR_UNSUPPORTED 2 /* device is not sm_100 or feature not built     */
+#define B200Q_ERR_CUDA 3        /* a CUDA runtime/driver call failed             */
+#define B200Q_ERR_WORKSPACE 4   /* caller-provided workspace too small           */
+
+/* element types */
+#define B200Q_BF16 0
+#define B200Q_F16 1
+#define B200Q_F32 2
+#define B200Q_I32 3
+
+/* bias types (B200Q_BIAS_NONE = no bias) */
+#define B200Q_BIAS_NONE 0
+#define B200Q_BIAS_BF16 1
+#define B200Q_BIAS_F16 2
+#define B200Q_BIAS_F32 3
+
+/* epilogue activations */
+#define B200Q_ACT_NONE 0
+#define B200Q_ACT_GELU_TANH 1
+#define B200Q_ACT_GELU_ERF 2
+
+/* FP8 encodings */
+#define B200Q_FP8_E4M3 0
+#define B200Q_FP8_E5M2 1
+
+B200Q_API int b200q_version(void);
+B200Q_API const char* b200q_status_string(int status);
+/* Number of kernels this library has launched in this process. */
+B200Q_API uint64_t b200q_launch_count(void);
+/* Reads (and optionally clears) the device-side status word of the current
+ * device: bit 0 = a pipeline wait timed out, bit 1 = bad argument.  Synchronous. */
+B200Q_API int b200q_get_device_status(unsigned int* status, int reset);
+
+/* Per-token INT8 activation quantization, bit-exact to the reference's
+ * i8_quant_rowwise (_patches/int8_ext/int8_gemm.mm:2332, kernel body :1346-1381).
+ * x [M,K] bf16/f16 (x_dtype B200Q_BF16/B200Q_F16) row stride ldx elements;
+ * q [M,K] int8 row stride ldq; scales [M] fp32. */
+B200Q_API int b200q_quant_rowwise_i8(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
+                           int8_t* q, int64_t ldq, float* scales, void* stream);
+
+/* Exact int8 x int8 -> int32 NT GEMM, C[M,N] = A[M,K] . W[N,K]^T.
+ * Replaces i8_matmul2d_nt (_patches/int8_ext/int8_gemm.mm:1655) and the
+ * torch._int_mm seam (_patches/int_mm_mps.py:90). */
+B200Q_API int b200q_i8_matmul_nt(const int8_t* a, int64_t lda, const int8_t* w, int64_t ldw, int32_t* c,
+                       int64_t ldc, int64_t M, int64_t N, int64_t K, void* stream);
+
+/* INT8 W8A8 GEMM with the reference's fused dequant epilogue:
+ *   out[m,n] = T( T(float(C[m,n]) * (col_scale[n] * row_scale[m])) + bias[n] )
+ * (T = bf16 or f16, two RNE roundings; bias is in T or NULL).  col_scale_numel is
+ * N (channelwise) or 1 (tensorwise weight scale).  act != B200Q_ACT_NONE applies
+ * the activation to that result and rounds once more: T(act(out)).  Replaces i8_matmul2d_nt_fused
+ * (int8_gemm.mm:1709) and i8_matmul2d_nt_fused_cs (int8_gemm.mm:1823). */
+B200Q_API int b200q_i8_matmul_nt_dequant(const int8_t* a, int64_t lda, const int8_t* w, int64_t ldw,
+                               const float* row_scale, const float* col_scale,
+                               int64_t col_scale_numel, const void* bias, int act, void* out,
+                               int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K,
+                               void* stream);
+
+/* Per-token quant + INT8 GEMM + dequant epilogue in one call (the comfy
+ * int8_tensorwise Linear: _patches/int8_linear_kernel_mps.py:218 _int8_linear_kernel).
+ * x [M,K] bf16/f16; q_scratch [M,K] int8 and scale_scratch [M] fp32 receive the
+ * quantized activation (they stay valid after the call, as the reference's
+ * activation cache expects). */
+B200Q_API int b200q_i8_linear(const void* x, int x_dtype, int64_t ldx, const int8_t* w, int64_t ldw,
+                    const float* col_scale, int64_t col_scale_numel, const void* bias, int act,
+                    void* out, int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K,
+                    int8_t* q_scratch, float* scale_scratch, void* stream);
+
+/* FP8 (e4m3 x e4m3) scaled GEMM, out = act(((A.W^T) * scale_a * scale_b * scale_result)
+ * + bias) in fp32, one rounding to out_dtype (bf16/f16/f32).  scale_a numel 1 or M,
+ * scale_b numel 1 or N, any scale may be NULL.  W is [N,K] row-major, i.e. the
+ * column-major [K,N] `other` operand of torch._scaled_mm consumed in place.
+ * Replaces _mps_scaled_mm / _fast_route (_patches/scaled_mm_fp8.py:123-207) and
+ * fp8fp8_matmul2d_nt (_patches/fp8_ext/fp8_matmul2d.mm:229). */
+B200Q_API int b200q_fp8_scaled_mm(const uint8_t* a, int64_t lda, const uint8_t* w, int64_t ldw,
+                        const float* scale_a, int64_t scale_a_numel, const float* scale_b,
+                        int64_t scale_b_numel, const float* scale_result, const void* bias,
+                        int bias_dtype, int act, void* out, int out_dtype, int64_t ldo,
+                        int64_t M, int64_t N, int64_t K, void* stream);
+
+/* Per-tensor FP8 activation quantization: amax = max|x|, scale = max(amax/448, 1e-30),
+ * q = e4m3 saturating RNE of x/scale.  amax_scratch: one caller-owned device word
+ * (overwritten).  No reference counterpart (comfy's quant ops produce the e4m3
+ * activation upstream of torch._scaled_mm, _patches/scaled_mm_fp8.py:149). */
+B200Q_API int b200q_fp8_quant_tensorwise(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
+                               uint8_t* q, int64_t ldq, float* scale, unsigned int* amax_scratch,
+                               void* stream);
+
+/* Bytes of device workspace b200q_w8a16_linear needs for this shape (0 = none). */
+B200Q_API size_t b200q_w8a16_workspace_size(int64_t M, int64_t N, int64_t K);
+
+/* FP8 weight-only linear: out = act((X . decode(W)^T) * w_scale + bias), fp32
+ * accumulation, one rounding to out_dtype.  X [M,K] bf16/f16, W [N,K] e4m3 bytes,
+ * w_scale one fp32 or NULL, bias bf16/f16/f32 or NULL.  Replaces w8a16_bias_bf16 /
+ * w8a16_f32 (_patches/fp8s_ext/w8a16_gemm.mm:286-314), fp8_matmul2d_nt
+ * (_patches/fp8_ext/fp8_matmul2d.mm:312) and _w8a16_forward
+ * (_patches/linear_fp8_w8a16.py:151). */
+B200Q_API int b200q_w8a16_linear(const void* x, int x_dtype, int64_t ldx, const uint8_t* w, int64_t ldw,
+                       const float* w_scale, const void* bias, int bias_dtype, int act,
+                       void* out, int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* Exact FP8 -> bf16/f16/f32 decode of n contiguous codes.  Replaces decode_fp8
+ * (_patches/_common.py:249-273). */
+B200Q_API int b200q_fp8_decode(const uint8_t* src, int64_t n, int fp8_kind, void* dst, int out_dtype,
+                     void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200Q_H_ */

@@ -1,0 +1,282 @@
+"""CPU oracle for the quantized DiT-linear path — TEST INFRASTRUCTURE ONLY.
+
+A restatement, in numpy (+ torch CPU for the FP8 casts), of the reference's own
+CPU-side / eager semantics for the three routes.  It is imported only by the
+tests, by ``__graft_entry__.smoke()`` and by ``bench.py``'s CPU-baseline leg, and
+only as the checker; the product path (the CUDA library behind the torch ops)
+never calls it.
+
+Pinning: the FP8 decode table and the INT8 dequant epilogue order are checked
+against the reference's own Python code run in this container
+(``tests/golden/make_golden.py`` -> ``tests/golden/*.npz``).  The INT8 rowwise
+quant lives in comfy_kitchen (absent here); it is pinned through the
+reference's restatement (int8_gemm.mm:1337-1381) and the known-answer cases of
+its tests (zero and 1e-30 rows, corner codes, ragged K).
+
+Reference citations are paths inside luix93/ComfyUI-AppleSilicon-Optimized.
+"""
+
+import numpy as np
+import torch
+
+BF16_TINY = np.float32(2.0 ** -126)
+F16_TINY = np.float32(2.0 ** -14)
+
+
+# ------------------------------------------------------------------ roundings
+def round_bf16(a):
+    """float32 -> nearest-even bf16, returned as float32 (NaN preserved)."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    u = a.view(np.uint32).astype(np.uint64)
+    lsb = (u >> np.uint64(16)) & np.uint64(1)
+    r = ((u + np.uint64(0x7FFF) + lsb) & np.uint64(0xFFFF0000)).astype(np.uint32)
+    out = r.view(np.float32).copy()
+    nan = np.isnan(a)
+    out[nan] = np.nan
+    return out
+
+
+def round_f16(a):
+    return np.asarray(a, dtype=np.float32).astype(np.float16).astype(np.float32)
+
+
+def _rounder(dtype):
+    if dtype == torch.bfloat16:
+        return round_bf16, BF16_TINY
+    if dtype == torch.float16:
+        return round_f16, F16_TINY
+    raise ValueError(f"unsupported dtype {dtype}")
+
+
+def to_f32(t):
+    """Exact widening of a bf16/f16/f32 tensor to a float32 numpy array."""
+    return t.detach().to(torch.float32).cpu().numpy()
+
+
+def from_f32(a, dtype):
+    """float32 numpy values that are already representable in `dtype` -> tensor."""
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(dtype)
+
+
+# ------------------------------------------------------------------ INT8 route
+def quantize_int8_rowwise(x):
+    """Per-token symmetric INT8 quant (comfy_kitchen quantize_int8_rowwise with
+    stochastic rounding off, as restated step by step at
+    _patches/int8_ext/int8_gemm.mm:1337-1381):
+
+      absmax = max|x| per row (exact)
+      scale  = max(absmax / 127, 1e-30)  (fp32, correctly rounded)  -> returned [M,1]
+      s      = x.dtype(scale); s == 0 -> finfo(x.dtype).tiny
+      q      = int8(clamp(rint(x.dtype(x / s)), -128, 127))
+    """
+    rnd, tiny = _rounder(x.dtype)
+    xf = to_f32(x.reshape(-1, x.shape[-1]))
+    absmax = np.abs(xf).max(axis=1).astype(np.float32) if xf.shape[1] else np.zeros(xf.shape[0], np.float32)
+    scale = np.maximum(absmax / np.float32(127.0), np.float32(1e-30)).astype(np.float32)
+    s = rnd(scale)
+    s = np.where(s == 0, tiny, s).astype(np.float32)
+    d = rnd((xf / s[:, None]).astype(np.float32))
+    q = np.clip(np.rint(d), -128, 127).astype(np.int8)
+    return torch.from_numpy(q), torch.from_numpy(scale.reshape(-1, 1))
+
+
+def int_mm(a, b):
+    """Exact int8 x int8 -> int32: a [M,K] @ b [K,N].  float64 BLAS is exact here
+    because |sum| <= 128*128*K < 2**53 for every K this library accepts."""
+    af = a.numpy().astype(np.float64)
+    bf = b.numpy().astype(np.float64)
+    return torch.from_numpy((af @ bf).astype(np.int64).astype(np.int32))
+
+
+def int8_dequant_epilogue(c, x_scale, w_scale, bias=None, out_dtype=torch.bfloat16, act=None):
+    """The eager chunked epilogue of _patches/int8_linear_kernel_mps.py:203-215
+    (== fused kernels int8_gemm.mm:96-122, 417-443):
+      out = T( T(float(C) * (w_scale[n] * x_scale[m])) + T(bias[n]) )
+    """
+    rnd, _ = _rounder(out_dtype)
+    cf = c.numpy().astype(np.float32)
+    ws = to_f32(w_scale.reshape(-1))
+    xs = to_f32(x_scale.reshape(-1, 1))
+    s = (ws[None, :] * xs).astype(np.float32)  # [M,N] (or [M,1] for a scalar scale)
+    out = rnd((cf * s).astype(np.float32))
+    if bias is not None:
+        b = to_f32(bias.to(out_dtype).reshape(-1))
+        out = rnd((out + b[None, :]).astype(np.float32))
+    if act == "gelu_tanh":  # BASELINE block extension: T(gelu(result))
+        out = rnd(gelu_tanh(out))
+    return from_f32(out, out_dtype)
+
+
+def int8_linear(x, weight, weight_scale, bias=None, out_dtype=torch.bfloat16, act=None):
+    """comfy_kitchen eager int8_linear without convrot (the oracle named at
+    _patches/int8_linear_kernel_mps.py:218-263): rowwise quant -> int8 GEMM with
+    the [N,K] weight -> chunked rescale -> bias."""
+    shp = x.shape
+    q, xs = quantize_int8_rowwise(x.reshape(-1, shp[-1]))
+    c = int_mm(q, weight.t())
+    out = int8_dequant_epilogue(c, xs, weight_scale, bias, out_dtype, act)
+    return out.reshape(*shp[:-1], weight.shape[0])
+
+
+def quantize_weight_int8_per_channel(w):
+    """Symmetric per-output-channel int8 weight quant (BASELINE configs 1 and 4):
+    s_w[n] = absmax_n / 127, q = rint(w / s_w) clamped (round-half-even)."""
+    wf = to_f32(w)
+    s = np.maximum(np.abs(wf).max(axis=1) / np.float32(127.0), np.float32(1e-30)).astype(np.float32)
+    q = np.clip(np.rint(wf / s[:, None]), -128, 127).astype(np.int8)
+    return torch.from_numpy(q), torch.from_numpy(s.reshape(-1, 1))
+
+
+# ------------------------------------------------------------------ FP8 routes
+def decode_fp8(t, out_dtype=torch.float32):
+    """Exact FP8 -> float decode (every code, NaNs included); equal to the
+    reference's LUT decode (_patches/_common.py:203-273)."""
+    return t.cpu().to(out_dtype)
+
+
+def quantize_fp8_tensorwise(x):
+    """Per-tensor e4m3 activation quant: scale = max(amax/448, 1e-30),
+    q = e4m3(x / scale) with saturation, round-to-nearest-even."""
+    xf = to_f32(x.reshape(-1, x.shape[-1]))
+    amax = np.float32(np.abs(xf).max()) if xf.size else np.float32(0)
+    scale = np.float32(max(np.float32(amax / np.float32(448.0)), np.float32(1e-30)))
+    v = np.clip((xf / scale).astype(np.float32), -448.0, 448.0)
+    q = torch.from_numpy(v).to(torch.float8_e4m3fn)
+    return q, torch.tensor(scale, dtype=torch.float32)
+
+
+def gelu_tanh(v):
+    v = np.asarray(v, dtype=np.float64)
+    return (0.5 * v * (1.0 + np.tanh(0.7978845608028654 * (v + 0.044715 * v ** 3)))).astype(np.float32)
+
+
+def _apply_scale(acc, scale, axis):
+    """acc * scale in fp32; scale numel 1 (tensorwise) or per-row/per-column."""
+    v = to_f32(scale)
+    if v.size == 1:
+        return (acc * v.reshape(())).astype(np.float32)
+    return (acc * (v.reshape(-1, 1) if axis == 0 else v.reshape(1, -1))).astype(np.float32)
+
+
+def scaled_mm_fp8(a, w, scale_a=None, scale_b=None, scale_result=None, bias=None,
+                  out_dtype=torch.bfloat16, act=None):
+    """torch._scaled_mm on e4m3 operands with the arithmetic of the reference's
+    native FP8 route (_fast_route, _patches/scaled_mm_fp8.py:123-146): exact
+    fp32 product (fp8fp8_matmul2d_nt), then * scale_a, * scale_b,
+    * scale_result and + bias in fp32, one cast to out_dtype.  `w` is the [N,K]
+    weight (torch._scaled_mm's `other` is w.t()).  `act` ("gelu_tanh") is the
+    BASELINE epilogue extension, applied after the bias.  out_dtype=None returns
+    the fp32 value before the final cast (what parity is measured against)."""
+    af = decode_fp8(a, torch.float32).numpy().astype(np.float64)
+    wf = decode_fp8(w, torch.float32).numpy().astype(np.float64)
+    out = (af @ wf.T).astype(np.float32)
+    if scale_a is not None:
+        out = _apply_scale(out, scale_a, 0)
+    if scale_b is not None:
+        out = _apply_scale(out, scale_b, 1)
+    if scale_result is not None:
+        out = _apply_scale(out, scale_result, 0)
+    if bias is not None:
+        out = (out + to_f32(bias).reshape(1, -1)).astype(np.float32)
+    if act == "gelu_tanh":
+        out = gelu_tanh(out)
+    res = torch.from_numpy(np.ascontiguousarray(out, dtype=np.float32))
+    return res if out_dtype is None else res.to(out_dtype)
+
+
+def scaled_mm_fp8_decode_path(a, w, scale_a=None, scale_b=None, scale_result=None, bias=None,
+                              out_dtype=torch.bfloat16):
+    """The reference's decode fallback of _mps_scaled_mm (_patches/scaled_mm_fp8.py:178-207):
+    decode to bf16, bf16 matmul (bf16 result), fp32 scales -> bf16, fp32 bias, cast.
+    Three roundings, so it is looser than the fast route; used for reporting."""
+    af = decode_fp8(a, torch.float32).numpy().astype(np.float64)
+    wf = decode_fp8(w, torch.float32).numpy().astype(np.float64)
+    out = round_bf16((af @ wf.T).astype(np.float32))
+    if scale_a is not None or scale_b is not None or scale_result is not None:
+        acc = out
+        if scale_a is not None:
+            acc = _apply_scale(acc, scale_a, 0)
+        if scale_b is not None:
+            acc = _apply_scale(acc, scale_b, 1)
+        if scale_result is not None:
+            acc = _apply_scale(acc, scale_result, 0)
+        out = round_bf16(acc)
+    if bias is not None:
+        out = (out + to_f32(bias).reshape(1, -1)).astype(np.float32)
+    return torch.from_numpy(np.ascontiguousarray(out, dtype=np.float32)).to(out_dtype)
+
+
+def w8a16_linear(x, w, w_scale=None, bias=None, act=None, out_dtype=None):
+    """FP8 weight-only linear: the reference decode path (decode W -> compute
+    dtype -> F.linear; _patches/linear_fp8_w8a16.py:1-11, _common.py:249) in fp32,
+    plus the BASELINE per-tensor weight scale and tanh-GELU epilogue.
+    out_dtype="fp32" returns the fp32 value before the final cast."""
+    shp = x.shape
+    xf = to_f32(x.reshape(-1, shp[-1])).astype(np.float64)
+    wf = decode_fp8(w, torch.float32).numpy().astype(np.float64)
+    out = (xf @ wf.T).astype(np.float32)
+    if w_scale is not None:
+        out = (out * to_f32(w_scale).reshape(())).astype(np.float32)
+    if bias is not None:
+        out = (out + to_f32(bias).reshape(1, -1)).astype(np.float32)
+    if act == "gelu_tanh":
+        out = gelu_tanh(out)
+    res = torch.from_numpy(np.ascontiguousarray(out))
+    if out_dtype != "fp32":
+        res = res.to(out_dtype or x.dtype)
+    return res.reshape(*shp[:-1], w.shape[0])
+
+
+# ------------------------------------------------------------------ error metrics
+def fp8_errors(out, ref):
+    """(max|d| / rms(ref), max|d| / max|ref|): the BASELINE bound and the
+    reference's own rel_err (dev/bench_gemm.py; tests/test_scaled_mm_fp8.py:79)."""
+    o = out.detach().float().cpu().numpy().astype(np.float64)
+    r = ref.detach().float().cpu().numpy().astype(np.float64)
+    d = np.abs(o - r).max() if o.size else 0.0
+    rms = np.sqrt((r ** 2).mean()) if r.size else 1.0
+    mx = np.abs(r).max() if r.size else 1.0
+    return float(d / max(rms, 1e-30)), float(d / max(mx, 1e-30))
+
+
+def ulp_size(v, dtype=torch.bfloat16):
+    """Spacing of `dtype` at |v| (float32 numpy array in, float64 out)."""
+    mant = 7 if dtype == torch.bfloat16 else 10
+    min_exp = -126 if dtype == torch.bfloat16 else -14
+    a = np.abs(np.asarray(v, dtype=np.float64))
+    e = np.floor(np.log2(np.maximum(a, 2.0 ** min_exp)))
+    return 2.0 ** (e - mant)
+
+
+def elementwise_ulp_ratio(out, ref32, ulps=1.0, atol_rms=1e-3):
+    """max over elements of |out - ref| / (ulps * ULP(ref) + atol_rms * rms(ref)).
+
+    <= 1 means every element is within `ulps` ULPs of the fp32 oracle value, with
+    an absolute slack of atol_rms * RMS for elements so close to zero that the
+    accumulation order alone can move them by more than their own ULP."""
+    o = out.detach().float().cpu().numpy().astype(np.float64)
+    r = ref32.detach().float().cpu().numpy().astype(np.float64)
+    if not r.size:
+        return 0.0
+    rms = np.sqrt((r ** 2).mean())
+    tol = ulps * ulp_size(r, out.dtype) + atol_rms * rms
+    return float((np.abs(o - r) / tol).max())
+
+
+def ulp_vs_fp32(out, ref32):
+    """Max distance, in ULPs of out's dtype (bf16/f16), between `out` and the
+    fp32 oracle value rounded to that dtype."""
+    ref = ref32.detach().float().cpu().to(out.dtype)
+    return bf16_ulp_diff(out.detach().cpu(), ref)
+
+
+def bf16_ulp_diff(a, b):
+    """Max distance in bf16 ULPs (ordered bit patterns) between two bf16 tensors."""
+    ia = a.contiguous().view(torch.int16).numpy().astype(np.int32)
+    ib = b.contiguous().view(torch.int16).numpy().astype(np.int32)
+
+    def ordered(i):
+        i = i & 0xFFFF
+        return np.where(i & 0x8000, 0x8000 - (i & 0x7FFF), 0x8000 + i)
+
+    return int(np.abs(ordered(ia) - ordered(ib)).max()) if ia.size else 0
