@@ -11,9 +11,12 @@
 //               per stage into a TMEM accumulator; tcgen05.commit frees the stage.
 //   warp 2      TMEM allocator (2 x BN columns: double-buffered accumulator so the
 //               epilogue of tile i overlaps the MMAs of tile i+1).
-//   warps 4..7  epilogue: tcgen05.ld 32 columns at a time, per-element epilogue
-//               (raw int32 / reference two-rounding INT8 dequant / FP8 scaled
-//               + bias + GELU), vectorised global stores.
+//   warps 4..11 epilogue: two warps per TMEM lane quarter, each taking half of
+//               the tile's columns; tcgen05.ld 32 columns at a time with the
+//               chunk's column scales / bias fetched by uniform vector loads
+//               before the TMEM wait; element math (raw int32 / reference
+//               two-rounding INT8 dequant / FP8 scaled + bias + GELU) and
+//               16-byte global stores.
 // Tiles are walked in groups of 16 M-tiles so the ~148 concurrently running
 // tiles share A row panels and W column panels in L2.
 #pragma once
@@ -25,7 +28,7 @@ namespace b200q {
 
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 128;  // bytes = elements per k-block (one 128B swizzle atom)
-constexpr int kGemmThreads = 256;
+constexpr int kGemmThreads = 384;  // 4 control warps + 8 epilogue warps
 constexpr int kGemmGroupM = 16;
 
 enum EpiMode : int { kEpiInt32 = 0, kEpiI8Dequant = 1, kEpiScaled = 2 };
@@ -52,77 +55,157 @@ __device__ __forceinline__ void gemm_tile_coords(int tile, int num_m, int num_n,
   nb = idx / gm;
 }
 
-template <int EPI>
-__device__ __forceinline__ float epi_value(uint32_t raw, float rs, float cs, float xs,
-                                           const EpiArgs& e, int n, bool acc_is_int) {
-  if constexpr (EPI == kEpiI8Dequant) {
-    return epi_i8_dequant(static_cast<int32_t>(raw), rs, cs, e, n);
+// Column parameters of one 32-column chunk (scale and bias per output column),
+// fetched with uniform vector loads: every lane of the warp reads the same
+// addresses, so each load is one broadcast transaction.  Absent scales read as
+// 1.0 (an exact multiply); bias presence is returned so the caller can skip the
+// add (adding +0.0 would flip the sign of a -0.0 result).
+__device__ __forceinline__ bool load_col_params(const EpiArgs& e, int n0, float (&cs)[32],
+                                                float (&bi)[32]) {
+  const bool full = n0 + 32 <= e.N;
+  if (e.col_scale && e.col_scale_vec) {
+    const float* p = e.col_scale + n0;
+    if (full && ((reinterpret_cast<uintptr_t>(p) & 15) == 0)) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(p) + j);
+        cs[4 * j] = v.x; cs[4 * j + 1] = v.y; cs[4 * j + 2] = v.z; cs[4 * j + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) cs[j] = __ldg(e.col_scale + min(n0 + j, e.N - 1));
+    }
   } else {
-    const float acc = acc_is_int ? __int2float_rn(static_cast<int32_t>(raw)) : __uint_as_float(raw);
-    return epi_scaled(acc, rs, cs, xs, e, n);
+    const float c = e.col_scale ? __ldg(e.col_scale) : 1.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) cs[j] = c;
+  }
+  if (e.bias_dtype == kBiasNone) return false;
+  if (e.bias_dtype == kBiasF32) {
+    const float* p = static_cast<const float*>(e.bias) + n0;
+    if (full && ((reinterpret_cast<uintptr_t>(p) & 15) == 0)) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(p) + j);
+        bi[4 * j] = v.x; bi[4 * j + 1] = v.y; bi[4 * j + 2] = v.z; bi[4 * j + 3] = v.w;
+      }
+      return true;
+    }
+  } else {
+    const uint16_t* p = static_cast<const uint16_t*>(e.bias) + n0;
+    if (full && ((reinterpret_cast<uintptr_t>(p) & 15) == 0)) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(p) + j);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint16_t lo = static_cast<uint16_t>(w[k] & 0xFFFFu), hi = static_cast<uint16_t>(w[k] >> 16);
+          if (e.bias_dtype == kBiasBF16) {
+            bi[8 * j + 2 * k] = __uint_as_float(static_cast<uint32_t>(lo) << 16);
+            bi[8 * j + 2 * k + 1] = __uint_as_float(static_cast<uint32_t>(hi) << 16);
+          } else {
+            bi[8 * j + 2 * k] = __half2float(__ushort_as_half(lo));
+            bi[8 * j + 2 * k + 1] = __half2float(__ushort_as_half(hi));
+          }
+        }
+      }
+      return true;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) bi[j] = load_bias(e.bias, e.bias_dtype, min(n0 + j, e.N - 1));
+  return true;
+}
+
+// Stores 32 values of row m at columns [n0, n0+32): 16-byte vector stores when
+// the chunk is whole and aligned, element stores on ragged edges.
+__device__ __forceinline__ void store_chunk(const EpiArgs& e, int64_t m, int n0, const float (&v)[32]) {
+  const bool full = n0 + 32 <= e.N;
+  if (e.out_dtype == kOutBF16 || e.out_dtype == kOutF16) {
+    if (full && ((e.ldo & 7) == 0) && ((reinterpret_cast<uintptr_t>(e.out) & 15) == 0)) {
+      uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(e.out) + m * e.ldo + n0);
+      if (e.out_dtype == kOutBF16) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          o[j] = make_uint4(pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                            pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          o[j] = make_uint4(pack_f16x2(v[8 * j], v[8 * j + 1]), pack_f16x2(v[8 * j + 2], v[8 * j + 3]),
+                            pack_f16x2(v[8 * j + 4], v[8 * j + 5]), pack_f16x2(v[8 * j + 6], v[8 * j + 7]));
+      }
+      return;
+    }
+  } else if (full && ((e.ldo & 3) == 0) && ((reinterpret_cast<uintptr_t>(e.out) & 15) == 0)) {
+    float4* o = reinterpret_cast<float4*>(static_cast<float*>(e.out) + m * e.ldo + n0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    if (n0 + j < e.N) store_out(e, m, n0 + j, v[j]);
+}
+
+__device__ __forceinline__ void store_chunk_i32(const EpiArgs& e, int64_t m, int n0, const uint32_t (&r)[32]) {
+  int32_t* out = static_cast<int32_t*>(e.out) + m * e.ldo;
+  if (n0 + 32 <= e.N && ((e.ldo & 3) == 0) && ((reinterpret_cast<uintptr_t>(e.out) & 15) == 0)) {
+    int4* o = reinterpret_cast<int4*>(out + n0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      o[j] = make_int4(static_cast<int>(r[4 * j]), static_cast<int>(r[4 * j + 1]),
+                       static_cast<int>(r[4 * j + 2]), static_cast<int>(r[4 * j + 3]));
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (n0 + j < e.N) out[n0 + j] = static_cast<int32_t>(r[j]);
   }
 }
 
-// Stores 32 accumulator columns [n0, n0+32) of row m.
-template <int EPI>
-__device__ __forceinline__ void epilogue_chunk(const uint32_t (&r)[32], int64_t m, int n0,
-                                               const EpiArgs& e, float rs, float xs,
-                                               bool acc_is_int) {
-  if constexpr (EPI == kEpiInt32) {
-    int32_t* out = static_cast<int32_t*>(e.out) + m * e.ldo;
-    const bool vec = (n0 + 32 <= e.N) && ((e.ldo & 3) == 0) &&
-                     ((reinterpret_cast<uintptr_t>(e.out) & 15) == 0);
-    if (vec) {
-      int4* o = reinterpret_cast<int4*>(out + n0);
+// Element math of one chunk.  Uniform flags are tested outside the unrolled loops.
+template <int EPI, bool ACC_INT>
+__device__ __forceinline__ void epilogue_math(const uint32_t (&r)[32], const float (&cs)[32],
+                                              const float (&bi)[32], bool has_bias, float rs,
+                                              float xs, const EpiArgs& e, float (&v)[32]) {
+  if constexpr (EPI == kEpiI8Dequant) {
+    // Reference order (int8_gemm.mm:417-443): s = cs*rs; T(C*s); T(r + bias).
+    if (e.out_dtype == kOutF16) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        o[j] = make_int4(static_cast<int>(r[4 * j]), static_cast<int>(r[4 * j + 1]),
-                         static_cast<int>(r[4 * j + 2]), static_cast<int>(r[4 * j + 3]));
+      for (int j = 0; j < 32; ++j)
+        v[j] = round_f16(__fmul_rn(__int2float_rn(static_cast<int32_t>(r[j])), __fmul_rn(cs[j], rs)));
+      if (has_bias) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = round_f16(__fadd_rn(v[j], bi[j]));
+      }
     } else {
 #pragma unroll
       for (int j = 0; j < 32; ++j)
-        if (n0 + j < e.N) out[n0 + j] = static_cast<int32_t>(r[j]);
+        v[j] = round_bf16(__fmul_rn(__int2float_rn(static_cast<int32_t>(r[j])), __fmul_rn(cs[j], rs)));
+      if (has_bias) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = round_bf16(__fadd_rn(v[j], bi[j]));
+      }
     }
   } else {
-    float v[32];
+    // FP8 route order (scaled_mm_fp8.py:136-146): ((acc*sa)*sb)*sr + bias, fp32.
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-      const int n = min(n0 + j, e.N - 1);
-      const float cs = e.col_scale ? __ldg(e.col_scale + (e.col_scale_vec ? n : 0)) : 1.0f;
-      v[j] = epi_value<EPI>(r[j], rs, cs, xs, e, n, acc_is_int);
+      const float acc = ACC_INT ? __int2float_rn(static_cast<int32_t>(r[j])) : __uint_as_float(r[j]);
+      v[j] = __fmul_rn(__fmul_rn(__fmul_rn(acc, rs), cs[j]), xs);
     }
-    const bool full = (n0 + 32 <= e.N);
-    if (e.out_dtype == kOutBF16 || e.out_dtype == kOutF16) {
-      const bool vec = full && ((e.ldo & 7) == 0) && ((reinterpret_cast<uintptr_t>(e.out) & 15) == 0);
-      if (vec) {
-        uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(e.out) + m * e.ldo + n0);
+    if (has_bias) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint4 w;
-          if (e.out_dtype == kOutBF16) {
-            w.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
-            w.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
-            w.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
-            w.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
-          } else {
-            w.x = pack_f16x2(v[8 * j + 0], v[8 * j + 1]);
-            w.y = pack_f16x2(v[8 * j + 2], v[8 * j + 3]);
-            w.z = pack_f16x2(v[8 * j + 4], v[8 * j + 5]);
-            w.w = pack_f16x2(v[8 * j + 6], v[8 * j + 7]);
-          }
-          o[j] = w;
-        }
-        return;
-      }
-    } else if (full && ((e.ldo & 3) == 0) && ((reinterpret_cast<uintptr_t>(e.out) & 15) == 0)) {
-      float4* o = reinterpret_cast<float4*>(static_cast<float*>(e.out) + m * e.ldo + n0);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-      return;
+      for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], bi[j]);
     }
+  }
+  if (e.act == kActGeluTanh) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (n0 + j < e.N) store_out(e, m, n0 + j, v[j]);
+    for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+  } else if (e.act == kActGeluErf) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
   }
 }
 
@@ -157,7 +240,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4 * 32);
+      mbar_init(&acc_empty[b], 8 * 32);
     }
     *abort_flag = 0;
     fence_mbarrier_init();
@@ -229,10 +312,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncwarp();
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    // 8 warps: warp w reads TMEM lane quarter (w % 4) and column half (w - 4) / 4.
+    const int q = warp & 3;
+    const int half = (warp - 4) >> 2;
     const int row_local = q * 32 + lane;
     const float xs = ep.extra_scale ? __ldg(ep.extra_scale) : 1.0f;
     constexpr bool kAccInt = KIND == MmaKind::I8;
+    constexpr int kChunks = BN / 64;  // 32-column chunks per warp
     int it = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       int mb, nb;
@@ -247,12 +333,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (EPI != kEpiInt32 && ep.row_scale && row_ok) rs = __ldg(ep.row_scale + (ep.row_scale_vec ? m : 0));
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(taddr + c * 32, r);
-        tmem_ld_wait();
+      for (int c = half * kChunks; c < (half + 1) * kChunks; ++c) {
         const int n0 = nb * BN + c * 32;
-        if (row_ok && n0 < N) epilogue_chunk<EPI>(r, m, n0, ep, rs, xs, kAccInt);
+        uint32_t r[32];
+        if constexpr (EPI == kEpiInt32) {
+          tmem_ld32(taddr + c * 32, r);
+          tmem_ld_wait();
+          if (row_ok && n0 < N) store_chunk_i32(ep, m, n0, r);
+        } else {
+          float cs[32], bi[32], v[32];
+          const bool has_bias = n0 < N ? load_col_params(ep, n0, cs, bi) : false;
+          tmem_ld32(taddr + c * 32, r);
+          tmem_ld_wait();
+          if (row_ok && n0 < N) {
+            epilogue_math<EPI, kAccInt>(r, cs, bi, has_bias, rs, xs, ep, v);
+            store_chunk(ep, m, n0, v);
+          }
+        }
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);
@@ -263,6 +360,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 2) tmem_dealloc(tmem_base, L::kTmemCols);
+}
+
+template <int EPI>
+__device__ __forceinline__ float epi_value(uint32_t raw, float rs, float cs, float xs,
+                                           const EpiArgs& e, int n, bool acc_is_int) {
+  if constexpr (EPI == kEpiI8Dequant) {
+    return epi_i8_dequant(static_cast<int32_t>(raw), rs, cs, e, n);
+  } else {
+    const float acc = acc_is_int ? __int2float_rn(static_cast<int32_t>(raw)) : __uint_as_float(raw);
+    return epi_scaled(acc, rs, cs, xs, e, n);
+  }
 }
 
 // ---------------------------------------------------------------------------
