@@ -161,30 +161,10 @@ __global__ void __launch_bounds__(kQuantThreads)
 }
 
 // ------------------------------------------------------------ FP8 per-tensor
-// amax_bits must be zeroed before the launch.  Rows of length K with stride ldx.
-template <typename T>
-__global__ void __launch_bounds__(256)
-    absmax_kernel(const T* __restrict__ x, int64_t ldx, int64_t M, int K, unsigned int* amax_bits) {
-  float m = 0.0f;
-  const int64_t total = M * static_cast<int64_t>(K);
-  const bool vec = (K % 8 == 0) && (ldx % 8 == 0) &&
-                   (reinterpret_cast<uintptr_t>(x) % 16 == 0);
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  if (vec) {
-    const int64_t nvec = total >> 3;
-    const int vpr = K >> 3;
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < nvec;
-         i += stride) {
-      const int64_t r = i / vpr, c = i - r * vpr;
-      m = fmaxf(m, absmax8<T>(__ldg(reinterpret_cast<const uint4*>(x + r * ldx) + c)));
-    }
-  } else {
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-         i += stride) {
-      const int64_t r = i / K, c = i - r * K;
-      m = fmaxf(m, fabsf(to_float<T>(x[r * ldx + c])));
-    }
-  }
+// Two addressing modes, chosen per launch: contiguous tensors (ldx == K) are
+// walked as one flat array of 16-byte vectors; strided ones row by row (one
+// CTA per row, grid-stride over rows).  No 64-bit division in either loop.
+__device__ __forceinline__ void block_atomic_max(float m, unsigned int* amax_bits) {
   m = warp_max(m);
   __shared__ float red[8];
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
@@ -196,8 +176,50 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// amax_bits must be zeroed before the launch.  Rows of length K with stride ldx.
+template <typename T>
+__global__ void __launch_bounds__(256)
+    absmax_kernel(const T* __restrict__ x, int64_t ldx, int64_t M, int K, unsigned int* amax_bits) {
+  float m0 = 0.0f, m1 = 0.0f;
+  const bool vec = (K % 8 == 0) && (ldx % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
+  if (vec && ldx == K) {
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    const int64_t nvec = (M * static_cast<int64_t>(K)) >> 3;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    for (; i + stride < nvec; i += 2 * stride) {
+      const uint4 a = __ldcs(xv + i), b = __ldcs(xv + i + stride);
+      m0 = fmaxf(m0, absmax8<T>(a));
+      m1 = fmaxf(m1, absmax8<T>(b));
+    }
+    if (i < nvec) m0 = fmaxf(m0, absmax8<T>(__ldcs(xv + i)));
+  } else {
+    for (int64_t r = blockIdx.x; r < M; r += gridDim.x) {
+      const T* xr = x + r * ldx;
+      if (vec) {
+        for (int c = threadIdx.x; c < (K >> 3); c += blockDim.x)
+          m0 = fmaxf(m0, absmax8<T>(__ldcs(reinterpret_cast<const uint4*>(xr) + c)));
+      } else {
+        for (int c = threadIdx.x; c < K; c += blockDim.x) m0 = fmaxf(m0, fabsf(to_float<T>(xr[c])));
+      }
+    }
+  }
+  block_atomic_max(fmaxf(m0, m1), amax_bits);
+}
+
 __device__ __forceinline__ float fp8_scale_from_amax(unsigned int bits) {
   return fmaxf(__fdiv_rn(__uint_as_float(bits), 448.0f), 1e-30f);
+}
+
+template <typename T>
+__device__ __forceinline__ uint2 fp8_quant8(const uint4& v, float s) {
+  const T* e = reinterpret_cast<const T*>(&v);
+  uint32_t lo = 0, hi = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) lo |= static_cast<uint32_t>(encode_e4m3_sat(__fdiv_rn(to_float<T>(e[j]), s))) << (8 * j);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) hi |= static_cast<uint32_t>(encode_e4m3_sat(__fdiv_rn(to_float<T>(e[j + 4]), s))) << (8 * j);
+  return make_uint2(lo, hi);
 }
 
 template <typename T>
@@ -207,31 +229,32 @@ __global__ void __launch_bounds__(256)
                         int64_t ldq, float* __restrict__ scale_out) {
   const float s = fp8_scale_from_amax(*amax_bits);
   if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = s;
-  const int64_t total = M * static_cast<int64_t>(K);
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const bool vec = (K % 8 == 0) && (ldx % 8 == 0) && (ldq % 8 == 0) &&
                    (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
                    (reinterpret_cast<uintptr_t>(q) % 8 == 0);
-  if (vec) {
-    const int64_t nvec = total >> 3;
-    const int vpr = K >> 3;
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < nvec;
-         i += stride) {
-      const int64_t r = i / vpr, c = i - r * vpr;
-      const uint4 v = __ldcs(reinterpret_cast<const uint4*>(x + r * ldx) + c);
-      const T* e = reinterpret_cast<const T*>(&v);
-      uint32_t lo = 0, hi = 0;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) lo |= static_cast<uint32_t>(encode_e4m3_sat(__fdiv_rn(to_float<T>(e[j]), s))) << (8 * j);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) hi |= static_cast<uint32_t>(encode_e4m3_sat(__fdiv_rn(to_float<T>(e[j + 4]), s))) << (8 * j);
-      reinterpret_cast<uint2*>(q + r * ldq)[c] = make_uint2(lo, hi);
+  if (vec && ldx == K && ldq == K) {
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    uint2* qv = reinterpret_cast<uint2*>(q);
+    const int64_t nvec = (M * static_cast<int64_t>(K)) >> 3;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    for (; i + stride < nvec; i += 2 * stride) {
+      const uint4 a = __ldcs(xv + i), b = __ldcs(xv + i + stride);
+      qv[i] = fp8_quant8<T>(a, s);
+      qv[i + stride] = fp8_quant8<T>(b, s);
     }
+    if (i < nvec) qv[i] = fp8_quant8<T>(__ldcs(xv + i), s);
   } else {
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-         i += stride) {
-      const int64_t r = i / K, c = i - r * K;
-      q[r * ldq + c] = encode_e4m3_sat(__fdiv_rn(to_float<T>(x[r * ldx + c]), s));
+    for (int64_t r = blockIdx.x; r < M; r += gridDim.x) {
+      const T* xr = x + r * ldx;
+      uint8_t* qr = q + r * ldq;
+      if (vec) {
+        for (int c = threadIdx.x; c < (K >> 3); c += blockDim.x)
+          reinterpret_cast<uint2*>(qr)[c] = fp8_quant8<T>(__ldcs(reinterpret_cast<const uint4*>(xr) + c), s);
+      } else {
+        for (int c = threadIdx.x; c < K; c += blockDim.x)
+          qr[c] = encode_e4m3_sat(__fdiv_rn(to_float<T>(xr[c]), s));
+      }
     }
   }
 }
