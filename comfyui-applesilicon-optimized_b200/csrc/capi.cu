@@ -249,6 +249,9 @@ const char* b200q_status_string(int s) {
     case B200Q_ERR_UNSUPPORTED: return "unsupported device (b200q kernels need sm_100 / B200)";
     case B200Q_ERR_CUDA: return "CUDA error";
     case B200Q_ERR_WORKSPACE: return "workspace too small";
+    case B200Q_ERR_TOO_LARGE:
+      return "shape needs more split-K scratch than the allocation-free entry point's static "
+             "buffer (B200Q_NOALLOC_SCRATCH_BYTES) holds; use b200q_w8a16_linear with a workspace";
     default: return "unknown status";
   }
 }
@@ -438,6 +441,60 @@ int b200q_w8a16_linear(const void* x, int x_dtype, int64_t ldx, const uint8_t* w
   }
   if (x_dtype == B200Q_F16) return dispatch_w8a16_tc<true>(d, p.bt, x, ldx, w, ldw, args, ep, st);
   return dispatch_w8a16_tc<false>(d, p.bt, x, ldx, w, ldw, args, ep, st);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free W8A16.  The split-K partials and tile counters live in this
+// file-scope device array instead of a caller workspace.  In host code the name
+// g_noalloc_scratch is only a host-side stand-in for the symbol, never a device
+// address: the device address is looked up once per device with
+// cudaGetSymbolAddress (with that device current) and cached.
+}  // extern "C"
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[B200Q_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+void* g_noalloc_addr[64] = {};
+std::mutex g_noalloc_mu;
+
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return B200Q_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      fprintf(stderr, "[b200q] cudaGetSymbolAddress(noalloc scratch) failed: %s\n",
+              cudaGetErrorString(e));
+      return B200Q_ERR_CUDA;
+    }
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return B200Q_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int b200q_w8a16_linear_noalloc(const void* x, int x_dtype, int64_t ldx, const uint8_t* w,
+                               int64_t ldw, const float* w_scale, const void* bias, int bias_dtype,
+                               int act, void* out, int out_dtype, int64_t ldo, int64_t M, int64_t N,
+                               int64_t K, void* stream) {
+  if (!x || !w || !out || !valid_dims(M, N, K) || K == 0) return B200Q_ERR_INVALID;
+  const size_t need = b200q_w8a16_workspace_size(M, N, K);
+  if (need > B200Q_NOALLOC_SCRATCH_BYTES) return B200Q_ERR_TOO_LARGE;
+  void* scratch = nullptr;
+  if (need) {
+    const int st = noalloc_scratch(&scratch);
+    if (st != B200Q_OK) return st;
+  }
+  // The shared path clears the tile counters on `stream` before the kernel
+  // (the partials need no clearing: every split writes its slice first).
+  return b200q_w8a16_linear(x, x_dtype, ldx, w, ldw, w_scale, bias, bias_dtype, act, out,
+                            out_dtype, ldo, M, N, K, scratch,
+                            need ? size_t(B200Q_NOALLOC_SCRATCH_BYTES) : 0, stream);
 }
 
 int b200q_fp8_decode(const uint8_t* src, int64_t n, int fp8_kind, void* dst, int out_dtype,

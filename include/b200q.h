@@ -132,6 +132,27 @@ B200Q_API int b200q_w8a16_linear(const void* x, int x_dtype, int64_t ldx, const 
                        void* out, int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K,
                        void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free variant of b200q_w8a16_linear (same arguments minus the
+ * workspace).  No counterpart in the reference: it exists for callers that
+ * cannot allocate device memory themselves -- a host that reaches this library
+ * only through the C ABI with buffers it registered up front (no device
+ * allocator of its own), or a runtime with a fixed device-memory budget in which
+ * every allocation must be planned before the model runs.  The split-K scratch
+ * lives in a static device array of B200Q_NOALLOC_SCRATCH_BYTES that every GPU
+ * loading this library holds until exit; shapes whose plan needs more scratch
+ * are rejected with B200Q_ERR_TOO_LARGE and nothing is launched.  The first
+ * call on each device looks up that array's device address (once per device;
+ * make that first call before any stream capture).  All calls share the array:
+ * calls whose kernels overlap on the GPU (other streams, other threads) race on
+ * it and must be serialised by the caller.  Never calls cudaMalloc/cudaFree. */
+#define B200Q_NOALLOC_SCRATCH_BYTES (16u << 20)
+#define B200Q_ERR_TOO_LARGE 5   /* needs more scratch than the static buffer */
+B200Q_API int b200q_w8a16_linear_noalloc(const void* x, int x_dtype, int64_t ldx, const uint8_t* w,
+                                         int64_t ldw, const float* w_scale, const void* bias,
+                                         int bias_dtype, int act, void* out, int out_dtype,
+                                         int64_t ldo, int64_t M, int64_t N, int64_t K,
+                                         void* stream);
+
 /* Exact FP8 -> bf16/f16/f32 decode of n contiguous codes.  Replaces decode_fp8
  * (_patches/_common.py:249-273). */
 B200Q_API int b200q_fp8_decode(const uint8_t* src, int64_t n, int fp8_kind, void* dst, int out_dtype,
