@@ -7,6 +7,7 @@
 // device memory is allocated here and no call synchronises the device (except
 // b200q_get_device_status, which exists to read the device status word).
 #include <atomic>
+#include <cstdlib>
 #include <cstdio>
 #include <mutex>
 
@@ -177,7 +178,7 @@ W16Plan w8a16_plan(int num_sms, int64_t M, int64_t N, int64_t K) {
   const int64_t num_kb = (K + kW16BK - 1) / kW16BK;
   int best = 1;
   double best_eff = 0.0;
-  for (int s = 1; s <= 8; ++s) {
+  for (int s = 1; s <= kW16MaxSplits; ++s) {
     if (s > 1 && s * 4 > num_kb) break;
     // fp32 partial write + read must stay small next to the fp8 weight stream
     if (s > 1 && double(s) * M * N * 8.0 > 0.5 * double(N) * K) break;
@@ -188,6 +189,15 @@ W16Plan w8a16_plan(int num_sms, int64_t M, int64_t N, int64_t K) {
       best_eff = eff;
       best = s;
     }
+  }
+  // Tuning override (B200Q_W8A16_SPLITS=n) for measurements; clamped to the plan's limits.
+  static const int forced = [] {
+    const char* e = getenv("B200Q_W8A16_SPLITS");
+    return e ? atoi(e) : 0;
+  }();
+  if (forced > 0) {
+    best = forced > kW16MaxSplits ? kW16MaxSplits : forced;
+    while (best > 1 && best * 2 > num_kb) --best;
   }
   p.splits = best;
   if (best > 1) {
@@ -215,13 +225,32 @@ int launch_w8a16_tc(const DeviceInfo* d, const void* x, int64_t ldx, const uint8
   return finish_launch();
 }
 
+// Small token counts: the streaming kernel (deep raw-weight ring, 128-byte boxes).
+template <int BT, bool XF16>
+int launch_w8a16_stream(const DeviceInfo* d, const void* x, int64_t ldx, const uint8_t* w,
+                        int64_t ldw, const W8A16Args& args, const EpiArgs& ep, cudaStream_t st) {
+  CUtensorMap tx, tw;
+  const CUtensorMapDataType xdt = XF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if (!make_tmap(&tx, x, xdt, args.K, args.M, ldx * 2, 64, BT, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tmap(&tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, args.K, args.N, ldw, kWsBK, kW16BM,
+                 CU_TENSOR_MAP_SWIZZLE_NONE))
+    return B200Q_ERR_CUDA;
+  auto kern = w8a16_stream_kernel<BT, XF16>;
+  constexpr int smem = W8A16StreamLayout<BT>::kSmemBytes;
+  if (!set_smem(kern, smem)) return B200Q_ERR_CUDA;
+  const int64_t units = int64_t((args.N + kW16BM - 1) / kW16BM) * ((args.M + BT - 1) / BT) * args.splits;
+  const int grid = static_cast<int>(units < d->num_sms ? units : d->num_sms);
+  kern<<<grid, kWsThreads, smem, st>>>(tx, tw, args, ep);
+  return finish_launch();
+}
+
 template <bool XF16>
 int dispatch_w8a16_tc(const DeviceInfo* d, int bt, const void* x, int64_t ldx, const uint8_t* w,
                       int64_t ldw, const W8A16Args& args, const EpiArgs& ep, cudaStream_t st) {
   switch (bt) {
-    case 16: return launch_w8a16_tc<16, XF16>(d, x, ldx, w, ldw, args, ep, st);
-    case 32: return launch_w8a16_tc<32, XF16>(d, x, ldx, w, ldw, args, ep, st);
-    case 64: return launch_w8a16_tc<64, XF16>(d, x, ldx, w, ldw, args, ep, st);
+    case 16: return launch_w8a16_stream<16, XF16>(d, x, ldx, w, ldw, args, ep, st);
+    case 32: return launch_w8a16_stream<32, XF16>(d, x, ldx, w, ldw, args, ep, st);
+    case 64: return launch_w8a16_stream<64, XF16>(d, x, ldx, w, ldw, args, ep, st);
     case 128: return launch_w8a16_tc<128, XF16>(d, x, ldx, w, ldw, args, ep, st);
     default: return launch_w8a16_tc<256, XF16>(d, x, ldx, w, ldw, args, ep, st);
   }

@@ -93,6 +93,39 @@ struct W8A16Args {
   unsigned int* counters;    // one per (nt, tt) tile, zero on entry
 };
 
+constexpr int kW16MaxSplits = 8;
+
+// Split-K fix-up run by the last CTA to finish a tile: sums the fp32 partials of
+// tokens [t0, t0 + tcount) for output feature n in split order 0, 1, ... (fixed,
+// so the result is bit-reproducible) and applies the epilogue.  Four tokens x up
+// to kW16MaxSplits splits are loaded together so the L2 latencies overlap.
+__device__ __forceinline__ void splitk_reduce_store(const W8A16Args& a, const EpiArgs& ep, int t0,
+                                                    int tcount, int n, float xs, float bias_v) {
+  const int64_t split_stride = static_cast<int64_t>(a.M) * a.N;
+  const float* base = a.partial + static_cast<int64_t>(t0) * a.N + n;
+  for (int j0 = 0; j0 < tcount; j0 += 4) {
+    float p[kW16MaxSplits][4];
+#pragma unroll
+    for (int s2 = 0; s2 < kW16MaxSplits; ++s2)
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj)
+        p[s2][jj] = (s2 < a.splits && j0 + jj < tcount)
+                        ? __ldcg(base + s2 * split_stride + static_cast<int64_t>(j0 + jj) * a.N)
+                        : 0.0f;
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      if (j0 + jj >= tcount) break;
+      float v = 0.0f;
+#pragma unroll
+      for (int s2 = 0; s2 < kW16MaxSplits; ++s2)
+        if (s2 < a.splits) v = __fadd_rn(v, p[s2][jj]);
+      if (ep.extra_scale) v = __fmul_rn(v, xs);
+      if (ep.bias_dtype != kBiasNone) v = __fadd_rn(v, bias_v);
+      store_out(ep, t0 + j0 + jj, n, apply_act(v, ep.act));
+    }
+  }
+}
+
 template <int BT, bool X_F16>
 __global__ void __launch_bounds__(kW16Threads, 1)
     w8a16_tc_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
@@ -302,16 +335,319 @@ __global__ void __launch_bounds__(kW16Threads, 1)
         named_bar_sync(1, 128);  // everyone has read last_flag before it is rewritten
         if (last && n_ok && valid) {
           __threadfence();
-          const int tmax = min(BT, a.M - tt * BT);
-          for (int j = 0; j < tmax; ++j) {
-            const int tok = tt * BT + j;
-            float v = 0.0f;
-            for (int s2 = 0; s2 < S; ++s2)
-              v = __fadd_rn(v, __ldcg(a.partial + (static_cast<int64_t>(s2) * a.M + tok) * a.N + n));
-            if (ep.extra_scale) v = __fmul_rn(v, xs);
-            if (ep.bias_dtype != kBiasNone) v = __fadd_rn(v, bias_v);
-            store_out(ep, tok, n, apply_act(v, ep.act));
+          splitk_reduce_store(a, ep, tt * BT, min(BT, a.M - tt * BT), n, xs, bias_v);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 2) tmem_dealloc(tmem_base, L::kTmemCols);
+}
+
+// ---------------------------------------------------------------------------
+// Streaming variant for small token counts (BT <= 64), where the call is bound by
+// the FP8 weight stream from HBM.  Three rings, so no load waits on an MMA:
+//   W ring     RS slots x (128 rows x 128 B e4m3): one full-cache-line TMA box each
+//   X ring     RX slots x (BT x 128 bf16 as two 128B-swizzle atoms), TMA straight
+//              into the MMA operand layout
+//   conv ring  2 slots x (128 x 128 bf16 as two atoms), written by the converters
+//   warp 0  weight producer (waits only on the W ring)
+//   warp 3  activation producer (waits only on the X ring)
+//   warps 4..11 converters: W slot -> conv slot (e4m3 -> fp16, one cvt per pair,
+//           exact) and the X slot in place (bf16 -> fp16, clamped to +-65504 as
+//           the reference does before its fp16 x fp8 kernel, linear_fp8_w8a16.py:
+//           166-171); frees the W slot
+//   warp 1  MMA: 8 x kind::f16 (fp16 x fp16 -> fp32) K=16 per 128-wide K block;
+//           one commit frees the conv slot, one frees the X slot
+//   warps 12..15 epilogue (same split-K protocol as w8a16_tc_kernel)
+// A standalone TMA probe on B200 streamed 128x128-byte boxes at ~94% of the
+// measured copy bandwidth with 128 KB in flight per SM; the rings are sized so
+// about that much weight data is in flight.
+constexpr int kWsBK = 128;
+constexpr int kWsThreads = 512;   // 16 warps: 4 control, 8 converters, 4 epilogue
+constexpr int kWsConv = 256;      // converter threads
+
+template <int BT>
+struct W8A16StreamLayout {
+  static constexpr int kRawSlot = kW16BM * kWsBK;        // 16 KB e4m3
+  static constexpr int kCSlot = kW16BM * kWsBK * 2;      // 32 KB bf16 (two atoms)
+  static constexpr int kXSlot = BT * kWsBK * 2;          // bf16 activations (two atoms)
+  static constexpr int kConvSlots = 2;
+  static constexpr int kXSlots = BT <= 16 ? 6 : BT <= 32 ? 4 : 3;
+  static constexpr int kFree = 200 * 1024 - kConvSlots * kCSlot - kXSlots * kXSlot;
+  static constexpr int kRawSlots = kFree / kRawSlot > 8 ? 8 : kFree / kRawSlot;
+  static constexpr int kCOff = 0;
+  static constexpr int kXOff = kConvSlots * kCSlot;
+  static constexpr int kRawOff = kXOff + kXSlots * kXSlot;
+  static constexpr int kBarOff = kRawOff + kRawSlots * kRawSlot;
+  // wfull/wempty[RS], xfull/xempty[RX], cfull/cempty[2], acc_full/acc_empty[2], slot, abort, last
+  static constexpr int kBarBytes = (2 * kRawSlots + 2 * kXSlots + 2 * kConvSlots + 4) * 8 + 16;
+  static constexpr int kSmemBytes = kBarOff + kBarBytes + 1024;
+  static constexpr uint32_t kTmemCols = 2 * BT < 32 ? 32 : 2 * BT;
+};
+
+template <int BT, bool X_F16>
+__global__ void __launch_bounds__(kWsThreads, 1)
+    w8a16_stream_kernel(const __grid_constant__ CUtensorMap tmX,
+                        const __grid_constant__ CUtensorMap tmW, W8A16Args a, EpiArgs ep) {
+  using L = W8A16StreamLayout<BT>;
+  constexpr int RS = L::kRawSlots;
+  constexpr int RX = L::kXSlots;
+  constexpr int CS = L::kConvSlots;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sC = smem + L::kCOff;
+  uint8_t* sX = smem + L::kXOff;
+  uint8_t* sW = smem + L::kRawOff;
+  uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* wempty = wfull + RS;
+  uint64_t* xfull = wempty + RS;
+  uint64_t* xempty = xfull + RX;
+  uint64_t* cfull = xempty + RX;
+  uint64_t* cempty = cfull + CS;
+  uint64_t* acc_full = cempty + CS;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_n = (a.N + kW16BM - 1) / kW16BM;
+  const int num_t = (a.M + BT - 1) / BT;
+  const int S = a.splits;
+  const int num_units = num_n * num_t * S;
+  const int num_kb = (a.K + kWsBK - 1) / kWsBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < RS; ++s) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&wempty[s], kWsConv);
+    }
+    for (int s = 0; s < RX; ++s) {
+      mbar_init(&xfull[s], 1);
+      mbar_init(&xempty[s], 1);
+    }
+    for (int s = 0; s < CS; ++s) {
+      mbar_init(&cfull[s], kWsConv);
+      mbar_init(&cempty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    *abort_flag = 0;
+    *last_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmX);
+    tma_prefetch_desc(&tmW);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ weight producer
+    if (lane == 0) {
+      int rs = 0;
+      uint32_t rph = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        int nt, tt, sp;
+        w16_unit_coords(u, S, num_t, nt, tt, sp);
+        const int kb0 = sp * num_kb / S, kb1 = (sp + 1) * num_kb / S;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&wempty[rs], rph ^ 1u, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&wfull[rs], L::kRawSlot);
+          tma_load_2d(&tmW, &wfull[rs], sW + rs * L::kRawSlot, kb * kWsBK, nt * kW16BM);
+          if (++rs == RS) { rs = 0; rph ^= 1u; }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 3) {
+    // ------------------------------------------------------------ activation producer
+    if (lane == 0) {
+      int xs = 0;
+      uint32_t xph = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        int nt, tt, sp;
+        w16_unit_coords(u, S, num_t, nt, tt, sp);
+        const int kb0 = sp * num_kb / S, kb1 = (sp + 1) * num_kb / S;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&xempty[xs], xph ^ 1u, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&xfull[xs], L::kXSlot);
+          uint8_t* dst = sX + xs * L::kXSlot;
+          tma_load_2d(&tmX, &xfull[xs], dst, kb * kWsBK, tt * BT);
+          tma_load_2d(&tmX, &xfull[xs], dst + L::kXSlot / 2, kb * kWsBK + 64, tt * BT);
+          if (++xs == RX) { xs = 0; xph ^= 1u; }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdesc = make_idesc(1, 0, 0, kW16BM, BT);  // f32 <- f16 x f16
+      int cs = 0, xs = 0;
+      uint32_t cph = 0, xph = 0;
+      bool ok = true;
+      int it = 0;
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++it) {
+        int nt, tt, sp;
+        w16_unit_coords(u, S, num_t, nt, tt, sp);
+        const int kb0 = sp * num_kb / S, kb1 = (sp + 1) * num_kb / S;
+        const int buf = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&acc_empty[buf], acc_phase ^ 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BT;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          // cfull covers the X slot too: the converters waited for it and converted it
+          if (!mbar_wait(&cfull[cs], cph, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int atom = 0; atom < 2; ++atom) {
+            const uint64_t adesc = make_sw128_desc(smem_u32(sC + cs * L::kCSlot + atom * (L::kCSlot / 2)));
+            const uint64_t bdesc = make_sw128_desc(smem_u32(sX + xs * L::kXSlot + atom * (L::kXSlot / 2)));
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              umma_ss<MmaKind::F16>(d_tmem, adesc + 2 * k, bdesc + 2 * k, kIdesc,
+                                    (kb != kb0 || atom != 0 || k != 0) ? 1u : 0u);
           }
+          umma_commit(&cempty[cs]);
+          umma_commit(&xempty[xs]);
+          if (++cs == CS) { cs = 0; cph ^= 1u; }
+          if (++xs == RX) { xs = 0; xph ^= 1u; }
+        }
+        if (ok) umma_commit(&acc_full[buf]);
+      }
+    }
+    __syncwarp();
+  } else if (warp >= 4 && warp < 12) {
+    // ------------------------------------------------------------ converters
+    const int t = threadIdx.x - 128;
+    int rs = 0, cs = 0, xs = 0;
+    uint32_t rph = 0, cph = 0, xph = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+      int nt, tt, sp;
+      w16_unit_coords(u, S, num_t, nt, tt, sp);
+      const int kb0 = sp * num_kb / S, kb1 = (sp + 1) * num_kb / S;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&wfull[rs], rph, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&cempty[cs], cph ^ 1u, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&xfull[xs], xph, abort_flag)) { ok = false; break; }
+        const uint8_t* src = sW + rs * L::kRawSlot;
+        uint8_t* dst = sC + cs * L::kCSlot;
+#pragma unroll 4
+        for (int i = 0; i < (kW16BM * kWsBK / 8) / kWsConv; ++i) {
+          const int idx = i * kWsConv + t;
+          const int r = idx >> 4, c = idx & 15;  // row, 8-element chunk (0..15)
+          const uint2 v = *reinterpret_cast<const uint2*>(src + r * kWsBK + c * 8);
+          uint4 o;
+          o.x = e4m3x2_to_f16x2(static_cast<uint16_t>(v.x & 0xFFFFu));
+          o.y = e4m3x2_to_f16x2(static_cast<uint16_t>(v.x >> 16));
+          o.z = e4m3x2_to_f16x2(static_cast<uint16_t>(v.y & 0xFFFFu));
+          o.w = e4m3x2_to_f16x2(static_cast<uint16_t>(v.y >> 16));
+          const int atom = c >> 3, cc = c & 7;
+          *reinterpret_cast<uint4*>(dst + atom * (L::kCSlot / 2) + r * 128 + ((cc ^ (r & 7)) << 4)) = o;
+        }
+        if constexpr (!X_F16) {
+          // bf16 -> fp16 in place; the 128B swizzle only permutes 16-byte chunks.
+          uint4* xv = reinterpret_cast<uint4*>(sX + xs * L::kXSlot);
+          for (int i = t; i < L::kXSlot / 16; i += kWsConv) {
+            uint4 w = xv[i];
+            uint32_t* h = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&h[j]));
+              f.x = fminf(fmaxf(f.x, -65504.0f), 65504.0f);
+              f.y = fminf(fmaxf(f.y, -65504.0f), 65504.0f);
+              __half2 o = __float22half2_rn(f);
+              h[j] = *reinterpret_cast<uint32_t*>(&o);
+            }
+            xv[i] = w;
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&cfull[cs]);
+        mbar_arrive(&wempty[rs]);
+        if (++rs == RS) { rs = 0; rph ^= 1u; }
+        if (++cs == CS) { cs = 0; cph ^= 1u; }
+        if (++xs == RX) { xs = 0; xph ^= 1u; }
+      }
+    }
+  } else if (warp >= 12) {
+    // ------------------------------------------------------------ epilogue
+    constexpr int CH = BT < 32 ? BT : 32;
+    const int q = warp & 3;
+    const int et = threadIdx.x - 384;
+    const float xs = ep.extra_scale ? __ldg(ep.extra_scale) : 1.0f;
+    int it = 0;
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++it) {
+      int nt, tt, sp;
+      w16_unit_coords(u, S, num_t, nt, tt, sp);
+      const int buf = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      const bool valid = mbar_wait_warp(&acc_full[buf], acc_phase, abort_flag);
+      tc_fence_after();
+      const int n = nt * kW16BM + q * 32 + lane;
+      const bool n_ok = n < a.N;
+      const float bias_v = (n_ok && ep.bias_dtype != kBiasNone) ? load_bias(ep.bias, ep.bias_dtype, n) : 0.0f;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BT;
+#pragma unroll 1
+      for (int c = 0; valid && c < BT / CH; ++c) {
+        uint32_t r[CH];
+        tmem_ld_cols<CH>(taddr + c * CH, r);
+        tmem_ld_wait();
+        const int t0 = tt * BT + c * CH;
+        if (n_ok) {
+#pragma unroll
+          for (int j = 0; j < CH; ++j) {
+            const int tok = t0 + j;
+            if (tok < a.M) {
+              const float acc = __uint_as_float(r[j]);
+              if (S > 1) {
+                a.partial[(static_cast<int64_t>(sp) * a.M + tok) * a.N + n] = acc;
+              } else {
+                float v = ep.extra_scale ? __fmul_rn(acc, xs) : acc;
+                if (ep.bias_dtype != kBiasNone) v = __fadd_rn(v, bias_v);
+                store_out(ep, tok, n, apply_act(v, ep.act));
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
+      if (S > 1) {
+        __threadfence();
+        named_bar_sync(1, 128);
+        if (et == 0) {
+          const unsigned int old = atomicAdd(&a.counters[nt * num_t + tt], 1u);
+          const int last = old == static_cast<unsigned int>(S - 1);
+          if (last) a.counters[nt * num_t + tt] = 0u;
+          *last_flag = last;
+        }
+        named_bar_sync(1, 128);
+        const bool last = *last_flag != 0;
+        named_bar_sync(1, 128);
+        if (last && n_ok && valid) {
+          __threadfence();
+          splitk_reduce_store(a, ep, tt * BT, min(BT, a.M - tt * BT), n, xs, bias_v);
         }
       }
     }
