@@ -85,6 +85,13 @@ class Layer:
 
 
 def _workload_spec(name, m_override=None):
+    spec = _base_spec(name)
+    if m_override:
+        spec["M"] = m_override
+    return spec
+
+
+def _base_spec(name):
     if name == "c5":
         return dict(route="fp8", M=65520, seed=4, hidden=5120, layers=[
             Layer("qkv", 5120, 15360), Layer("out", 5120, 5120),
@@ -103,7 +110,7 @@ def _workload_spec(name, m_override=None):
         return dict(route="fp8", M=8192, seed=2, hidden=12288, layers=[Layer("down", 12288, 3072)],
                     inputs=["x"], desc="FP8 W8A8 scaled_mm (BASELINE config 3)")
     if name == "c2":
-        return dict(route="w8a16", M=m_override or 4096, seed=1, hidden=3072,
+        return dict(route="w8a16", M=4096, seed=1, hidden=3072,
                     layers=[Layer("up", 3072, 12288, "gelu_tanh")], inputs=["x"],
                     desc="FP8 W8A16 linear (BASELINE config 2)")
     raise SystemExit(f"unknown workload {name}")
@@ -174,6 +181,43 @@ class B200Block:
             outs.append(y)
             h = y
         return outs
+
+    def build_graphs(self, inputs):
+        """Captures every op of one step as its own CUDA graph over static buffers.
+        Returns [(graph, gemm_flops)] in execution order (flops 0 for quant ops) and
+        the number of b200q kernel launches one step makes."""
+        from b200q._patches import _native
+        ops = torch.ops.b200q
+        spec = self.spec
+        pool = torch.cuda.graph_pool_handle()
+        seq, h, self.graph_outs = [], None, []
+        n0 = _native.launch_count()
+
+        def capture(fn):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=pool):
+                out = fn()
+            return g, out
+
+        for i, (l, (w, s, b)) in enumerate(zip(spec["layers"], self.weights)):
+            x = inputs[spec["inputs"][i]] if i < len(spec["inputs"]) else h
+            flops = 2.0 * self.M * l.K * l.N
+            act = l.act or "none"
+            if spec["route"] == "fp8":
+                g, (xq, xs) = capture(lambda: ops.fp8_quant_tensorwise(x))
+                seq.append((g, 0.0))
+                g, y = capture(lambda: ops.fp8_scaled_mm(xq, w, xs.reshape(1), s, None, b,
+                                                         torch.bfloat16, act))
+            elif spec["route"] == "int8":
+                g, (xq, xs) = capture(lambda: ops.quant_rowwise_i8(x))
+                seq.append((g, 0.0))
+                g, y = capture(lambda: ops.i8_matmul_nt_fused_cs(xq, w, xs, s, b, torch.bfloat16, act))
+            else:
+                g, y = capture(lambda: ops.w8a16_linear(x, w, s, b, act))
+            seq.append((g, flops))
+            self.graph_outs.append(y)
+            h = y
+        return seq, _native.launch_count() - n0
 
     def _ev(self, record):
         if not record:
@@ -266,6 +310,12 @@ def run_b200q(args):
     for _ in range(args.warmup):
         blk.step(blk.inputs)
     barrier()
+    graphs = None
+    if args.launch == "graph":
+        graphs, launches_per_step = blk.build_graphs(blk.inputs)
+        for g, _ in graphs:  # one untimed replay after capture
+            g.replay()
+        barrier()
 
     # ---- device-resident timing: per-step events, L2 flushed between steps (untimed)
     launches0 = _native.launch_count()
@@ -278,11 +328,24 @@ def run_b200q(args):
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record()
-            blk.step(blk.inputs, record=True)
+            if graphs is None:
+                blk.step(blk.inputs, record=True)
+            else:
+                for g, fl in graphs:
+                    if fl:
+                        ea = torch.cuda.Event(enable_timing=True)
+                        eb = torch.cuda.Event(enable_timing=True)
+                        ea.record()
+                        g.replay()
+                        eb.record()
+                        blk.gemm_events.append((ea, eb, fl))
+                    else:
+                        g.replay()
             e1.record()
             step_ms.append((e0, e1))
         barrier()
-    launches = _native.launch_count() - launches0
+    launches = (_native.launch_count() - launches0 if graphs is None
+                else launches_per_step * args.steps)
     t_dev = sum(a.elapsed_time(b) for a, b in step_ms)
     gemm_ms = sum(a.elapsed_time(b) for a, b, _ in blk.gemm_events)
     gemm_flops = sum(f for _, _, f in blk.gemm_events)
@@ -337,7 +400,9 @@ def run_b200q(args):
             "config": {"workload": f"{args.workload}: {spec['desc']}", "M_total": spec["M"],
                        "M_per_rank": M, "layers": [(l.name, l.K, l.N, l.act) for l in spec["layers"]],
                        "parallelism": f"token-rows split over {world} rank(s), weights replicated, no collective",
-                       "l2": "flushed (256 MB write) between timed steps, outside the events"},
+                       "l2": "flushed (256 MB write) between timed steps, outside the events",
+                       "launch": ("each op of the step captured once as a CUDA graph, replayed per step"
+                                  if args.launch == "graph" else "eager torch.ops calls")},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1) if achieved else None,
                          "peak": round(peak, 1), "unit": "TFLOP/s",
                          "frac": round(achieved / peak, 4) if achieved else None,
@@ -453,7 +518,9 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--workload", default="c5", choices=["c1", "c2", "c3", "c4", "c5"])
-    ap.add_argument("--m", type=int, default=None, help="token count for c2")
+    ap.add_argument("--m", type=int, default=None, help="override the workload's total token count M")
+    ap.add_argument("--launch", default="graph", choices=["graph", "eager"],
+                    help="replay per-op CUDA graphs (default) or call the torch ops eagerly")
     ap.add_argument("--impl", default="b200q", choices=["b200q", "reference"])
     ap.add_argument("--cpu-rows", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")

@@ -178,7 +178,11 @@ W16Plan w8a16_plan(int num_sms, int64_t M, int64_t N, int64_t K) {
   const int64_t num_kb = (K + kW16BK - 1) / kW16BK;
   int best = 1;
   double best_eff = 0.0;
-  for (int s = 1; s <= kW16MaxSplits; ++s) {
+  // Token tiles of <= 64 run the streaming kernel, whose per-SM rate is bound by
+  // its MMA issue rate (measured on B200: ~80 ns per 128 x N x 16 MMA at N <= 64),
+  // not by how many SMs stream; split-K only adds partial traffic there.
+  const int max_splits = p.bt <= 64 ? 1 : kW16MaxSplits;
+  for (int s = 1; s <= max_splits; ++s) {
     if (s > 1 && s * 4 > num_kb) break;
     // fp32 partial write + read must stay small next to the fp8 weight stream
     if (s > 1 && double(s) * M * N * 8.0 > 0.5 * double(N) * K) break;
@@ -233,7 +237,7 @@ int launch_w8a16_stream(const DeviceInfo* d, const void* x, int64_t ldx, const u
   const CUtensorMapDataType xdt = XF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   if (!make_tmap(&tx, x, xdt, args.K, args.M, ldx * 2, 64, BT, CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_tmap(&tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, args.K, args.N, ldw, kWsBK, kW16BM,
-                 CU_TENSOR_MAP_SWIZZLE_NONE))
+                 CU_TENSOR_MAP_SWIZZLE_128B))
     return B200Q_ERR_CUDA;
   auto kern = w8a16_stream_kernel<BT, XF16>;
   constexpr int smem = W8A16StreamLayout<BT>::kSmemBytes;

@@ -349,45 +349,73 @@ __global__ void __launch_bounds__(kW16Threads, 1)
 
 // ---------------------------------------------------------------------------
 // Streaming variant for small token counts (BT <= 64), where the call is bound by
-// the FP8 weight stream from HBM.  Three rings, so no load waits on an MMA:
-//   W ring     RS slots x (128 rows x 128 B e4m3): one full-cache-line TMA box each
-//   X ring     RX slots x (BT x 128 bf16 as two 128B-swizzle atoms), TMA straight
-//              into the MMA operand layout
-//   conv ring  2 slots x (128 x 128 bf16 as two atoms), written by the converters
-//   warp 0  weight producer (waits only on the W ring)
-//   warp 3  activation producer (waits only on the X ring)
-//   warps 4..11 converters: W slot -> conv slot (e4m3 -> fp16, one cvt per pair,
-//           exact) and the X slot in place (bf16 -> fp16, clamped to +-65504 as
-//           the reference does before its fp16 x fp8 kernel, linear_fp8_w8a16.py:
-//           166-171); frees the W slot
-//   warp 1  MMA: 8 x kind::f16 (fp16 x fp16 -> fp32) K=16 per 128-wide K block;
-//           one commit frees the conv slot, one frees the X slot
-//   warps 12..15 epilogue (same split-K protocol as w8a16_tc_kernel)
-// A standalone TMA probe on B200 streamed 128x128-byte boxes at ~94% of the
-// measured copy bandwidth with 128 KB in flight per SM; the rings are sized so
-// about that much weight data is in flight.
+// the FP8 weight stream from HBM.  The dequantized weight tile never touches
+// shared memory: converters read the raw e4m3 tile, convert to bf16 in registers
+// and tcgen05.st it into a TMEM buffer, and the MMA takes its A operand from TMEM
+// (tcgen05.mma ... [a_tmem], b_desc).  Shared-memory traffic per 16 KB weight
+// block is then ~40 KB (TMA write + one read of the raw tile, the activation
+// tile) instead of ~110 KB for a shared-memory converted operand -- on B200 the
+// latter saturated the 128 B/clk shared-memory port before HBM.
+//   W ring   RS slots x (128 rows x 128 B e4m3, 128B swizzle -> conflict-free reads)
+//   X ring   RX slots x (BT x 128 bf16 as two 128B-swizzle atoms), read by the MMA
+//   A ring   4 TMEM buffers x 64 columns (128 rows x 128 bf16)
+//   warp 0   weight producer            warp 3   activation producer
+//   warps 4..11 converters: warp w owns TMEM lane quarter w % 4 (the rows it may
+//            access) and half of the block's K; one thread per weight row
+//   warp 1   MMA: 8 x kind::f16 (bf16 x bf16 -> fp32), K=16 each, A from TMEM,
+//            rotated over kNacc independent accumulators: with N = 16..32 tokens an
+//            MMA is tiny and a single accumulator serializes them on latency
+//            (measured ~80 ns each); the epilogue sums the accumulators in order
+//   warps 12..15 epilogue (split-K protocol as in w8a16_tc_kernel)
 constexpr int kWsBK = 128;
-constexpr int kWsThreads = 512;   // 16 warps: 4 control, 8 converters, 4 epilogue
-constexpr int kWsConv = 256;      // converter threads
+constexpr int kWsThreads = 512;
+constexpr int kWsConv = 256;
+constexpr int kWsABufs = 4;
+constexpr int kWsACols = kWsBK / 2;  // 128 bf16 per row = 64 32-bit columns
 
 template <int BT>
 struct W8A16StreamLayout {
   static constexpr int kRawSlot = kW16BM * kWsBK;        // 16 KB e4m3
-  static constexpr int kCSlot = kW16BM * kWsBK * 2;      // 32 KB bf16 (two atoms)
   static constexpr int kXSlot = BT * kWsBK * 2;          // bf16 activations (two atoms)
-  static constexpr int kConvSlots = 2;
-  static constexpr int kXSlots = BT <= 16 ? 6 : BT <= 32 ? 4 : 3;
-  static constexpr int kFree = 200 * 1024 - kConvSlots * kCSlot - kXSlots * kXSlot;
-  static constexpr int kRawSlots = kFree / kRawSlot > 8 ? 8 : kFree / kRawSlot;
-  static constexpr int kCOff = 0;
-  static constexpr int kXOff = kConvSlots * kCSlot;
-  static constexpr int kRawOff = kXOff + kXSlots * kXSlot;
+  static constexpr int kXSlots = BT <= 16 ? 6 : BT <= 32 ? 5 : 4;
+  static constexpr int kFree = 204 * 1024 - kXSlots * kXSlot;
+  static constexpr int kRawSlots = kFree / kRawSlot > 10 ? 10 : kFree / kRawSlot;
+  static constexpr int kXOff = 0;
+  static constexpr int kRawOff = kXSlots * kXSlot;
   static constexpr int kBarOff = kRawOff + kRawSlots * kRawSlot;
-  // wfull/wempty[RS], xfull/xempty[RX], cfull/cempty[2], acc_full/acc_empty[2], slot, abort, last
-  static constexpr int kBarBytes = (2 * kRawSlots + 2 * kXSlots + 2 * kConvSlots + 4) * 8 + 16;
+  // wfull/wempty[RS], xfull/xempty[RX], afull/aempty[4], acc_full/acc_empty[2], slot, abort, last
+  static constexpr int kBarBytes = (2 * kRawSlots + 2 * kXSlots + 2 * kWsABufs + 4) * 8 + 16;
   static constexpr int kSmemBytes = kBarOff + kBarBytes + 1024;
-  static constexpr uint32_t kTmemCols = 2 * BT < 32 ? 32 : 2 * BT;
+  static constexpr int kNacc = BT <= 16 ? 4 : BT <= 32 ? 2 : 1;
+  static constexpr uint32_t kAccCols = 2 * kNacc * BT;
+  static constexpr uint32_t kTmemCols = 512;  // accumulators + 4 x 64 A columns
 };
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+      "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]),
+      "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]),
+      "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// D(tmem) (+)= A(tmem) x B(smem desc)^T, kind::f16, one thread.
+__device__ __forceinline__ void umma_ts_f16(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 
 template <int BT, bool X_F16>
 __global__ void __launch_bounds__(kWsThreads, 1)
@@ -396,20 +424,19 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   using L = W8A16StreamLayout<BT>;
   constexpr int RS = L::kRawSlots;
   constexpr int RX = L::kXSlots;
-  constexpr int CS = L::kConvSlots;
+  constexpr int AB = kWsABufs;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* sC = smem + L::kCOff;
   uint8_t* sX = smem + L::kXOff;
   uint8_t* sW = smem + L::kRawOff;
   uint64_t* wfull = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
   uint64_t* wempty = wfull + RS;
   uint64_t* xfull = wempty + RS;
   uint64_t* xempty = xfull + RX;
-  uint64_t* cfull = xempty + RX;
-  uint64_t* cempty = cfull + CS;
-  uint64_t* acc_full = cempty + CS;
+  uint64_t* afull = xempty + RX;
+  uint64_t* aempty = afull + AB;
+  uint64_t* acc_full = aempty + AB;
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -432,9 +459,9 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       mbar_init(&xfull[s], 1);
       mbar_init(&xempty[s], 1);
     }
-    for (int s = 0; s < CS; ++s) {
-      mbar_init(&cfull[s], kWsConv);
-      mbar_init(&cempty[s], 1);
+    for (int s = 0; s < AB; ++s) {
+      mbar_init(&afull[s], kWsConv);
+      mbar_init(&aempty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
@@ -456,6 +483,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  const uint32_t tmem_a0 = tmem_base + L::kAccCols;  // A buffers follow the accumulators
 
   if (warp == 0) {
     // ------------------------------------------------------------ weight producer
@@ -500,9 +528,10 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t kIdesc = make_idesc(1, 0, 0, kW16BM, BT);  // f32 <- f16 x f16
-      int cs = 0, xs = 0;
-      uint32_t cph = 0, xph = 0;
+      // f32 <- bf16 x bf16 (or fp16 x fp16), M=128, N=BT, both K-major.
+      constexpr uint32_t kIdesc = X_F16 ? make_idesc(1, 0, 0, kW16BM, BT) : make_idesc(1, 1, 1, kW16BM, BT);
+      int ab = 0, xs = 0;
+      uint32_t aph = 0, xph = 0;
       bool ok = true;
       int it = 0;
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++it) {
@@ -513,23 +542,24 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         const uint32_t acc_phase = (it >> 1) & 1;
         if (!mbar_wait(&acc_empty[buf], acc_phase ^ 1u, abort_flag)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + buf * BT;
+        const uint32_t d_tmem = tmem_base + buf * L::kNacc * BT;
+        int mi = 0;  // MMA index within the unit (selects the accumulator)
         for (int kb = kb0; kb < kb1; ++kb) {
-          // cfull covers the X slot too: the converters waited for it and converted it
-          if (!mbar_wait(&cfull[cs], cph, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&afull[ab], aph, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&xfull[xs], xph, abort_flag)) { ok = false; break; }
           tc_fence_after();
+          const uint32_t a_tmem = tmem_a0 + ab * kWsACols;
 #pragma unroll
           for (int atom = 0; atom < 2; ++atom) {
-            const uint64_t adesc = make_sw128_desc(smem_u32(sC + cs * L::kCSlot + atom * (L::kCSlot / 2)));
             const uint64_t bdesc = make_sw128_desc(smem_u32(sX + xs * L::kXSlot + atom * (L::kXSlot / 2)));
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-              umma_ss<MmaKind::F16>(d_tmem, adesc + 2 * k, bdesc + 2 * k, kIdesc,
-                                    (kb != kb0 || atom != 0 || k != 0) ? 1u : 0u);
+            for (int k = 0; k < 4; ++k, ++mi)  // K=16 per MMA = 8 TMEM columns of A, +32 B of B
+              umma_ts_f16(d_tmem + (mi % L::kNacc) * BT, a_tmem + (atom * 4 + k) * 8, bdesc + 2 * k,
+                          kIdesc, mi >= L::kNacc ? 1u : 0u);
           }
-          umma_commit(&cempty[cs]);
+          umma_commit(&aempty[ab]);
           umma_commit(&xempty[xs]);
-          if (++cs == CS) { cs = 0; cph ^= 1u; }
+          if (++ab == AB) { ab = 0; aph ^= 1u; }
           if (++xs == RX) { xs = 0; xph ^= 1u; }
         }
         if (ok) umma_commit(&acc_full[buf]);
@@ -538,56 +568,49 @@ __global__ void __launch_bounds__(kWsThreads, 1)
     __syncwarp();
   } else if (warp >= 4 && warp < 12) {
     // ------------------------------------------------------------ converters
-    const int t = threadIdx.x - 128;
-    int rs = 0, cs = 0, xs = 0;
-    uint32_t rph = 0, cph = 0, xph = 0;
+    // Thread = weight row (TMEM lane q*32 + lane); `half` picks K 0..63 or 64..127.
+    const int q = warp & 3;
+    const int half = (warp - 4) >> 2;
+    const int r = q * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    int rs = 0, ab = 0;
+    uint32_t rph = 0, aph = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
       int nt, tt, sp;
       w16_unit_coords(u, S, num_t, nt, tt, sp);
       const int kb0 = sp * num_kb / S, kb1 = (sp + 1) * num_kb / S;
       for (int kb = kb0; kb < kb1; ++kb) {
-        if (!mbar_wait(&wfull[rs], rph, abort_flag)) { ok = false; break; }
-        if (!mbar_wait(&cempty[cs], cph ^ 1u, abort_flag)) { ok = false; break; }
-        if (!mbar_wait(&xfull[xs], xph, abort_flag)) { ok = false; break; }
-        const uint8_t* src = sW + rs * L::kRawSlot;
-        uint8_t* dst = sC + cs * L::kCSlot;
-#pragma unroll 4
-        for (int i = 0; i < (kW16BM * kWsBK / 8) / kWsConv; ++i) {
-          const int idx = i * kWsConv + t;
-          const int r = idx >> 4, c = idx & 15;  // row, 8-element chunk (0..15)
-          const uint2 v = *reinterpret_cast<const uint2*>(src + r * kWsBK + c * 8);
-          uint4 o;
-          o.x = e4m3x2_to_f16x2(static_cast<uint16_t>(v.x & 0xFFFFu));
-          o.y = e4m3x2_to_f16x2(static_cast<uint16_t>(v.x >> 16));
-          o.z = e4m3x2_to_f16x2(static_cast<uint16_t>(v.y & 0xFFFFu));
-          o.w = e4m3x2_to_f16x2(static_cast<uint16_t>(v.y >> 16));
-          const int atom = c >> 3, cc = c & 7;
-          *reinterpret_cast<uint4*>(dst + atom * (L::kCSlot / 2) + r * 128 + ((cc ^ (r & 7)) << 4)) = o;
-        }
-        if constexpr (!X_F16) {
-          // bf16 -> fp16 in place; the 128B swizzle only permutes 16-byte chunks.
-          uint4* xv = reinterpret_cast<uint4*>(sX + xs * L::kXSlot);
-          for (int i = t; i < L::kXSlot / 16; i += kWsConv) {
-            uint4 w = xv[i];
-            uint32_t* h = reinterpret_cast<uint32_t*>(&w);
+        if (!mbar_wait_warp(&wfull[rs], rph, abort_flag)) { ok = false; break; }
+        if (!mbar_wait_warp(&aempty[ab], aph ^ 1u, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        // Row r's 64 bytes: 16-byte chunks c = half*4 .. half*4+3, stored at chunk
+        // position c ^ (r & 7) by the 128-byte TMA swizzle.
+        const uint8_t* row = sW + rs * L::kRawSlot + r * kWsBK;
+        uint32_t v[32];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&h[j]));
-              f.x = fminf(fmaxf(f.x, -65504.0f), 65504.0f);
-              f.y = fminf(fmaxf(f.y, -65504.0f), 65504.0f);
-              __half2 o = __float22half2_rn(f);
-              h[j] = *reinterpret_cast<uint32_t*>(&o);
+        for (int j = 0; j < 4; ++j) {
+          const int c = half * 4 + j;
+          const uint4 w = *reinterpret_cast<const uint4*>(row + ((c ^ (r & 7)) << 4));
+          const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            if constexpr (X_F16) {
+              v[j * 8 + 2 * k] = e4m3x2_to_f16x2(static_cast<uint16_t>(wd[k] & 0xFFFFu));
+              v[j * 8 + 2 * k + 1] = e4m3x2_to_f16x2(static_cast<uint16_t>(wd[k] >> 16));
+            } else {
+              v[j * 8 + 2 * k] = e4m3x2_to_bf16x2(static_cast<uint16_t>(wd[k] & 0xFFFFu));
+              v[j * 8 + 2 * k + 1] = e4m3x2_to_bf16x2(static_cast<uint16_t>(wd[k] >> 16));
             }
-            xv[i] = w;
           }
         }
-        fence_proxy_async_smem();
-        mbar_arrive(&cfull[cs]);
+        tmem_st32(tmem_a0 + lane_off + ab * kWsACols + half * 32, v);
+        tmem_st_wait();
+        tc_fence_before();
         mbar_arrive(&wempty[rs]);
+        mbar_arrive(&afull[ab]);
         if (++rs == RS) { rs = 0; rph ^= 1u; }
-        if (++cs == CS) { cs = 0; cph ^= 1u; }
-        if (++xs == RX) { xs = 0; xph ^= 1u; }
+        if (++ab == AB) { ab = 0; aph ^= 1u; }
       }
     }
   } else if (warp >= 12) {
@@ -607,25 +630,33 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       const int n = nt * kW16BM + q * 32 + lane;
       const bool n_ok = n < a.N;
       const float bias_v = (n_ok && ep.bias_dtype != kBiasNone) ? load_bias(ep.bias, ep.bias_dtype, n) : 0.0f;
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BT;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * L::kNacc * BT;
 #pragma unroll 1
       for (int c = 0; valid && c < BT / CH; ++c) {
-        uint32_t r[CH];
-        tmem_ld_cols<CH>(taddr + c * CH, r);
+        uint32_t rr[CH];
+        tmem_ld_cols<CH>(taddr + c * CH, rr);
         tmem_ld_wait();
+#pragma unroll
+        for (int j2 = 1; j2 < L::kNacc; ++j2) {  // fixed-order sum of the accumulators
+          uint32_t r2[CH];
+          tmem_ld_cols<CH>(taddr + j2 * BT + c * CH, r2);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < CH; ++j) rr[j] = __float_as_uint(__fadd_rn(__uint_as_float(rr[j]), __uint_as_float(r2[j])));
+        }
         const int t0 = tt * BT + c * CH;
         if (n_ok) {
 #pragma unroll
           for (int j = 0; j < CH; ++j) {
             const int tok = t0 + j;
             if (tok < a.M) {
-              const float acc = __uint_as_float(r[j]);
+              const float acc = __uint_as_float(rr[j]);
               if (S > 1) {
                 a.partial[(static_cast<int64_t>(sp) * a.M + tok) * a.N + n] = acc;
               } else {
-                float v = ep.extra_scale ? __fmul_rn(acc, xs) : acc;
-                if (ep.bias_dtype != kBiasNone) v = __fadd_rn(v, bias_v);
-                store_out(ep, tok, n, apply_act(v, ep.act));
+                float vv = ep.extra_scale ? __fmul_rn(acc, xs) : acc;
+                if (ep.bias_dtype != kBiasNone) vv = __fadd_rn(vv, bias_v);
+                store_out(ep, tok, n, apply_act(vv, ep.act));
               }
             }
           }
