@@ -123,6 +123,37 @@ int launch_gemm8_tc(const DeviceInfo* d, const void* a, int64_t lda, const void*
   return finish_launch();
 }
 
+// CTA-pair kernel: clusters of 2, grid = 2 x min(tiles, SMs / 2).
+template <MmaKind KIND, int STAGES, int EPI>
+int launch_gemm8_tc2(const DeviceInfo* d, const void* a, int64_t lda, const void* w, int64_t ldw,
+                     int M, int N, int K, const EpiArgs& ep, cudaStream_t st) {
+  CUtensorMap ta, tb;
+  if (!make_tmap(&ta, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M, lda, kGemmBK, 128,
+                 CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tmap(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldw, kGemmBK, 128,
+                 CU_TENSOR_MAP_SWIZZLE_128B))
+    return B200Q_ERR_CUDA;
+  auto kern = gemm8_tc2_kernel<KIND, STAGES, EPI>;
+  constexpr int smem = Gemm8PairLayout<STAGES>::kSmemBytes;
+  if (!set_smem(kern, smem)) return B200Q_ERR_CUDA;
+  const int64_t tiles = int64_t((M + 255) / 256) * ((N + 255) / 256);
+  const int64_t pairs = tiles < d->num_sms / 2 ? tiles : d->num_sms / 2;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, ep) != cudaSuccess) return finish_launch();
+  return finish_launch();
+}
+
 template <bool IS_FP8, int EPI>
 int launch_gemm8_simt(const void* a, int64_t lda, const void* w, int64_t ldw, int M, int N, int K,
                       const EpiArgs& ep, cudaStream_t st) {
@@ -132,6 +163,15 @@ int launch_gemm8_simt(const void* a, int64_t lda, const void* w, int64_t ldw, in
                                                         static_cast<const uint8_t*>(w), ldw, M, N,
                                                         K, ep);
   return finish_launch();
+}
+
+// B200Q_PAIR_GEMM=0 selects the single-CTA kernel everywhere (A/B measurements).
+bool pair_kernels_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("B200Q_PAIR_GEMM");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 template <MmaKind KIND, int EPI>
@@ -146,6 +186,8 @@ int gemm8(const void* a, int64_t lda, const void* w, int64_t ldw, int64_t M, int
   if (!tc) return launch_gemm8_simt<kFp8, EPI>(a, lda, w, ldw, int(M), int(N), int(K), ep, st);
   if (N <= 128)
     return launch_gemm8_tc<KIND, 128, 6, EPI>(d, a, lda, w, ldw, int(M), int(N), int(K), ep, st);
+  if (M >= 256 && pair_kernels_enabled())
+    return launch_gemm8_tc2<KIND, 6, EPI>(d, a, lda, w, ldw, int(M), int(N), int(K), ep, st);
   return launch_gemm8_tc<KIND, 256, 4, EPI>(d, a, lda, w, ldw, int(M), int(N), int(K), ep, st);
 }
 

@@ -362,6 +362,195 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 2) tmem_dealloc(tmem_base, L::kTmemCols);
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair variant: a cluster of 2 CTAs computes 256x256 output tiles with
+// tcgen05.mma.cta_group::2 (M=256).  Each CTA stages its own 128 A rows and
+// 128 of the tile's 256 W rows, so per CTA and per K step the tensor core gets
+// the same 128x256 work as the single-CTA kernel from 2/3 of the operand bytes
+// (32 KB instead of 48 KB per 128-byte K block); the freed shared memory buys
+// 6 pipeline stages.  The even CTA's warp 1 issues the MMAs; both CTAs' TMA
+// loads complete on the even CTA's `full` barrier; each MMA batch's commit
+// signals both CTAs' `empty` barriers; accumulators land in each CTA's own TMEM
+// (its 128 rows x 256 columns) and each CTA runs its own epilogue.
+template <int STAGES>
+struct Gemm8PairLayout {
+  static constexpr int kATile = 128 * kGemmBK;  // this CTA's A rows
+  static constexpr int kBTile = 128 * kGemmBK;  // this CTA's half of the W rows
+  static constexpr int kStageBytes = kATile + kBTile;
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kBarBytes = (2 * STAGES + 4) * 8 + 16;
+  static constexpr int kSmemBytes = kBarOffset + kBarBytes + 1024;
+  static constexpr uint32_t kTmemCols = 512;  // 2 x 256-column accumulators
+};
+
+template <MmaKind KIND, int STAGES, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm8_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     int M, int N, int K, EpiArgs ep) {
+  using L = Gemm8PairLayout<STAGES>;
+  constexpr int BM = 256, BN = 256;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * L::kATile;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0 = MMA-issuing CTA
+  const uint32_t peer = rank ^ 1u;
+  const int pair = blockIdx.x >> 1;
+  const int num_pairs = gridDim.x >> 1;
+  const int num_m = (M + BM - 1) / BM;
+  const int num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (K + kGemmBK - 1) / kGemmBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);   // the even CTA's producer arrives with both CTAs' bytes
+      mbar_init(&empty[s], 1);  // one MMA commit per use
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 2 * 8);  // 8 epilogue warps in each CTA
+    }
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 2) {
+    tmem_alloc_pair(tmem_slot, L::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      const uint32_t leader_full0 = mapa_shared(smem_u32(&full[0]), 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
+        int mb, nb;
+        gemm_tile_coords(tile, num_m, num_n, mb, nb);
+        const int a_row = mb * BM + static_cast<int>(rank) * 128;
+        const int b_row = nb * BN + static_cast<int>(rank) * 128;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * L::kStageBytes);
+          const uint32_t bar = leader_full0 + stage * 8;
+          tma_load_2d_pair(&tmA, bar, sA + stage * L::kATile, kb * kGemmBK, a_row);
+          tma_load_2d_pair(&tmB, bar, sB + stage * L::kBTile, kb * kGemmBK, b_row);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (even CTA)
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t kIdesc =
+          KIND == MmaKind::I8 ? make_idesc(2, 1, 1, BM, BN) : make_idesc(1, 0, 0, BM, BN);
+      const uint32_t empty_self = smem_u32(&empty[0]);
+      const uint32_t empty_peer = mapa_shared(empty_self, peer);
+      const uint32_t accf_self = smem_u32(&acc_full[0]);
+      const uint32_t accf_peer = mapa_shared(accf_self, peer);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int it = 0;
+      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs, ++it) {
+        const int buf = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&acc_empty[buf], acc_phase ^ 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t adesc = make_sw128_desc(smem_u32(sA + stage * L::kATile));
+          const uint64_t bdesc = make_sw128_desc(smem_u32(sB + stage * L::kBTile));
+#pragma unroll
+          for (int k = 0; k < kGemmBK / 32; ++k)
+            umma_ss_pair<KIND>(d_tmem, adesc + 2 * k, bdesc + 2 * k, kIdesc, (kb | k) != 0 ? 1u : 0u);
+          umma_commit_pair(empty_self + stage * 8);
+          umma_commit_pair(empty_peer + stage * 8);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (ok) {
+          umma_commit_pair(accf_self + buf * 8);
+          umma_commit_pair(accf_peer + buf * 8);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;
+    const int half = (warp - 4) >> 2;
+    const int row_local = q * 32 + lane;
+    const float xs = ep.extra_scale ? __ldg(ep.extra_scale) : 1.0f;
+    const uint32_t acce_leader = mapa_shared(smem_u32(&acc_empty[0]), 0);
+    constexpr bool kAccInt = KIND == MmaKind::I8;
+    constexpr int kChunks = BN / 64;
+    int it = 0;
+    for (int tile = pair; tile < num_tiles; tile += num_pairs, ++it) {
+      int mb, nb;
+      gemm_tile_coords(tile, num_m, num_n, mb, nb);
+      const int buf = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait_warp(&acc_full[buf], acc_phase, abort_flag)) break;
+      tc_fence_after();
+      const int64_t m = static_cast<int64_t>(mb) * BM + static_cast<int64_t>(rank) * 128 + row_local;
+      const bool row_ok = m < M;
+      float rs = 1.0f;
+      if (EPI != kEpiInt32 && ep.row_scale && row_ok) rs = __ldg(ep.row_scale + (ep.row_scale_vec ? m : 0));
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+#pragma unroll 1
+      for (int c = half * kChunks; c < (half + 1) * kChunks; ++c) {
+        const int n0 = nb * BN + c * 32;
+        uint32_t r[32];
+        if constexpr (EPI == kEpiInt32) {
+          tmem_ld32(taddr + c * 32, r);
+          tmem_ld_wait();
+          if (row_ok && n0 < N) store_chunk_i32(ep, m, n0, r);
+        } else {
+          float cs[32], bi[32], v[32];
+          const bool has_bias = n0 < N ? load_col_params(ep, n0, cs, bi) : false;
+          tmem_ld32(taddr + c * 32, r);
+          tmem_ld_wait();
+          if (row_ok && n0 < N) {
+            epilogue_math<EPI, kAccInt>(r, cs, bi, has_bias, rs, xs, ep, v);
+            store_chunk(ep, m, n0, v);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acce_leader + buf * 8);
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // the peer's shared memory and barriers stay alive until both are done
+  tc_fence_after();
+  if (warp == 2) tmem_dealloc_pair(tmem_base, L::kTmemCols);
+}
+
 template <int EPI>
 __device__ __forceinline__ float epi_value(uint32_t raw, float rs, float cs, float xs,
                                            const EpiArgs& e, int n, bool acc_is_int) {
