@@ -45,11 +45,15 @@ struct Gemm8Layout {
   static constexpr uint32_t kTmemCols = 2 * BN;
 };
 
-__device__ __forceinline__ void gemm_tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
-  const int group_size = kGemmGroupM * num_n;
+// Tile order: groups of `group_m` M-tiles, M fastest inside a group.  group_m = 1
+// is a plain N-fastest sweep (each A row panel is read once while the whole W
+// stays in L2); the host picks it when W fits comfortably in L2.
+__device__ __forceinline__ void gemm_tile_coords(int tile, int num_m, int num_n, int group_m,
+                                                 int& mb, int& nb) {
+  const int group_size = group_m * num_n;
   const int g = tile / group_size;
-  const int first_m = g * kGemmGroupM;
-  const int gm = min(num_m - first_m, kGemmGroupM);
+  const int first_m = g * group_m;
+  const int gm = min(num_m - first_m, group_m);
   const int idx = tile - g * group_size;
   mb = first_m + idx % gm;
   nb = idx / gm;
@@ -212,7 +216,7 @@ __device__ __forceinline__ void epilogue_math(const uint32_t (&r)[32], const flo
 template <MmaKind KIND, int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    int M, int N, int K, EpiArgs ep) {
+                    int M, int N, int K, int group_m, EpiArgs ep) {
   using L = Gemm8Layout<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -266,7 +270,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         int mb, nb;
-        gemm_tile_coords(tile, num_m, num_n, mb, nb);
+        gemm_tile_coords(tile, num_m, num_n, group_m, mb, nb);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
@@ -322,7 +326,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int it = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       int mb, nb;
-      gemm_tile_coords(tile, num_m, num_n, mb, nb);
+      gemm_tile_coords(tile, num_m, num_n, group_m, mb, nb);
       const int buf = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait_warp(&acc_full[buf], acc_phase, abort_flag)) break;
@@ -386,7 +390,7 @@ struct Gemm8PairLayout {
 template <MmaKind KIND, int STAGES, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm8_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     int M, int N, int K, EpiArgs ep) {
+                     int M, int N, int K, int group_m, EpiArgs ep) {
   using L = Gemm8PairLayout<STAGES>;
   constexpr int BM = 256, BN = 256;
   extern __shared__ uint8_t smem_raw[];
@@ -446,7 +450,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool ok = true;
       for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
         int mb, nb;
-        gemm_tile_coords(tile, num_m, num_n, mb, nb);
+        gemm_tile_coords(tile, num_m, num_n, group_m, mb, nb);
         const int a_row = mb * BM + static_cast<int>(rank) * 128;
         const int b_row = nb * BN + static_cast<int>(rank) * 128;
         for (int kb = 0; kb < num_kb; ++kb) {
@@ -510,7 +514,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int it = 0;
     for (int tile = pair; tile < num_tiles; tile += num_pairs, ++it) {
       int mb, nb;
-      gemm_tile_coords(tile, num_m, num_n, mb, nb);
+      gemm_tile_coords(tile, num_m, num_n, group_m, mb, nb);
       const int buf = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait_warp(&acc_full[buf], acc_phase, abort_flag)) break;
