@@ -385,7 +385,7 @@ def run_b200q(args):
     eight_bit = spec["route"] in ("fp8", "int8")
     peak = (2.0 if eight_bit else 1.0) * peaks["bf16_sustained"]
     achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None
-    traffic = _committed_traffic(args.workload)
+    traffic, traffic_src = _committed_traffic(args.workload) if args.m is None else (None, None)
 
     if rank == 0:
         clocks = clk.summary()
@@ -406,7 +406,8 @@ def run_b200q(args):
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1) if achieved else None,
                          "peak": round(peak, 1), "unit": "TFLOP/s",
                          "frac": round(achieved / peak, 4) if achieved else None,
-                         "traffic": traffic,
+                         "traffic": traffic, "traffic_source": traffic_src,
+                         "algorithmic_flops_per_launch": (round(gemm_flops / n_gemm) if n_gemm else None),
                          "kernel": "gemm8_tc_kernel" if eight_bit else "w8a16_tc_kernel",
                          "peak_source": (f"{'2 x ' if eight_bit else ''}bf16_tflops_sustained of "
                                          f"{peaks['source']} MEASURED_PEAKS.json"
@@ -427,12 +428,14 @@ def run_b200q(args):
 
 
 def _committed_traffic(workload):
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary
+    (profiles/ncu_traffic.json), and where that number comes from."""
     p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
     try:
-        return json.load(open(p)).get(workload)
+        t = json.load(open(p)).get(workload)
+        return (t["bytes_per_launch"], t["source"]) if t else (None, None)
     except Exception:
-        return None
+        return None, None
 
 
 # ----------------------------------------------------------------------------- CPU arm
