@@ -123,8 +123,9 @@ def _flops(spec, M):
 class B200Block:
     """Device-resident weights + the step, through the public torch.ops.b200q API."""
 
-    def __init__(self, spec, M, dev, rank):
+    def __init__(self, spec, M, dev, rank, fused=False):
         self.spec, self.M, self.dev = spec, M, dev
+        self.fused = fused  # activation quant inside the GEMM launch (8-bit routes)
         ops = torch.ops.b200q
         g = torch.Generator(device=dev)
         g.manual_seed(spec["seed"])
@@ -163,11 +164,19 @@ class B200Block:
         h = None
         for i, (l, (w, s, b)) in enumerate(zip(spec["layers"], self.weights)):
             x = inputs[spec["inputs"][i]] if i < len(spec["inputs"]) else h
-            if spec["route"] == "fp8":
+            if spec["route"] == "fp8" and self.fused:
+                ev = self._ev(record)
+                y = ops.fp8_linear(x, w, s, b, torch.bfloat16, l.act or "none")
+                self._ev_end(ev, record, l)
+            elif spec["route"] == "fp8":
                 xq, xs = ops.fp8_quant_tensorwise(x)
                 ev = self._ev(record)
                 y = ops.fp8_scaled_mm(xq, w, xs.reshape(1), s, None, b, torch.bfloat16,
                                       l.act or "none")
+                self._ev_end(ev, record, l)
+            elif spec["route"] == "int8" and self.fused:
+                ev = self._ev(record)
+                y = ops.i8_linear(x, w, s, b, torch.bfloat16, l.act or "none")
                 self._ev_end(ev, record, l)
             elif spec["route"] == "int8":
                 xq, xs = ops.quant_rowwise_i8(x)
@@ -203,7 +212,11 @@ class B200Block:
             x = inputs[spec["inputs"][i]] if i < len(spec["inputs"]) else h
             flops = 2.0 * self.M * l.K * l.N
             act = l.act or "none"
-            if spec["route"] == "fp8":
+            if spec["route"] == "fp8" and self.fused:
+                g, y = capture(lambda: ops.fp8_linear(x, w, s, b, torch.bfloat16, act))
+            elif spec["route"] == "int8" and self.fused:
+                g, y = capture(lambda: ops.i8_linear(x, w, s, b, torch.bfloat16, act))
+            elif spec["route"] == "fp8":
                 g, (xq, xs) = capture(lambda: ops.fp8_quant_tensorwise(x))
                 seq.append((g, 0.0))
                 g, y = capture(lambda: ops.fp8_scaled_mm(xq, w, xs.reshape(1), s, None, b,
@@ -299,7 +312,7 @@ def run_b200q(args):
 
     spec = _workload_spec(args.workload, args.m)
     start, M = _split_rows(spec["M"], world, rank)
-    blk = B200Block(spec, M, dev, rank)
+    blk = B200Block(spec, M, dev, rank, fused=args.prologue == "fused")
     flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
 
     def barrier():
@@ -401,6 +414,10 @@ def run_b200q(args):
                        "M_per_rank": M, "layers": [(l.name, l.K, l.N, l.act) for l in spec["layers"]],
                        "parallelism": f"token-rows split over {world} rank(s), weights replicated, no collective",
                        "l2": "flushed (256 MB write) between timed steps, outside the events",
+                       "activation_quant": ({"fused": "inside each GEMM launch (quant prologue; fp8: "
+                                                      "+1 amax-reduction launch per linear)",
+                                             "separate": "own launch(es) before each GEMM"}[args.prologue]
+                                            if spec["route"] != "w8a16" else "none (weight-only)"),
                        "launch": ("each op of the step captured once as a CUDA graph, replayed per step"
                                   if args.launch == "graph" else "eager torch.ops calls")},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1) if achieved else None,
@@ -524,6 +541,9 @@ def main():
     ap.add_argument("--m", type=int, default=None, help="override the workload's total token count M")
     ap.add_argument("--launch", default="graph", choices=["graph", "eager"],
                     help="replay per-op CUDA graphs (default) or call the torch ops eagerly")
+    ap.add_argument("--prologue", default="separate", choices=["fused", "separate"],
+                    help="8-bit routes: activation quant in its own launch before each GEMM "
+                         "(default, currently faster), or inside the GEMM launch")
     ap.add_argument("--impl", default="b200q", choices=["b200q", "reference"])
     ap.add_argument("--cpu-rows", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")

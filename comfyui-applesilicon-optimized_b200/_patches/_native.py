@@ -16,7 +16,10 @@ _patches/fp8_ext/fp8_matmul2d.mm:355-360, _patches/fp8s_ext/w8a16_gemm.mm:316-32
   i8_matmul_nt_fused(a, w, row_scale, bias) -> bf16 [M,N]       (i8_matmul2d_nt_fused)
   i8_matmul_nt_fused_cs(a, w, row_scale, col_scale, bias, out_dtype) (i8_matmul2d_nt_fused_cs)
   i8_linear(x, w, w_scale, bias, out_dtype) -> quant + GEMM + dequant epilogue
+                                               (B200Q_FUSED_PROLOGUE=1: quant inside the GEMM)
   fp8_quant_tensorwise(x)                   -> (q e4m3 [M,K], scale f32 [])
+  fp8_linear(x, w, w_scale, bias, out_dtype, act, scale_result)
+                                            -> per-tensor e4m3 quant fused into fp8_scaled_mm
   fp8_scaled_mm(a, w_nk, scale_a, scale_b, scale_result, bias, out_dtype, act)
   w8a16_linear(x, w_nk e4m3, w_scale, bias, act, out_dtype)
   fp8_decode(t, out_dtype)
@@ -57,6 +60,11 @@ _SIGNATURES = {
     "b200q_fp8_scaled_mm": ([_vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _int, _int, _vp,
                              _int, _i64, _i64, _i64, _i64, _vp], _int),
     "b200q_fp8_quant_tensorwise": ([_vp, _int, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp], _int),
+    "b200q_prologue_sync_bytes": ([_i64], _sz),
+    "b200q_i8_linear_fused": ([_vp, _int, _i64, _vp, _i64, _vp, _i64, _vp, _int, _vp, _int, _i64,
+                               _i64, _i64, _i64, _vp, _vp, _vp, _sz, _vp], _int),
+    "b200q_fp8_linear_fused": ([_vp, _int, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _int, _int, _vp,
+                                _int, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _sz, _vp], _int),
     "b200q_w8a16_workspace_size": ([_i64, _i64, _i64], _sz),
     "b200q_w8a16_linear": ([_vp, _int, _i64, _vp, _i64, _vp, _vp, _int, _int, _vp, _int, _i64, _i64,
                             _i64, _i64, _vp, _sz, _vp], _int),
@@ -206,8 +214,40 @@ def i8_matmul_nt_fused(a, w, row_scale, bias=None):
     return i8_matmul_nt_fused_cs(a, w, row_scale, one, bias, torch.bfloat16)
 
 
+# Sync words of the fused-prologue launches (b200q_prologue_sync_bytes): one
+# zero-initialised buffer per (device, stream), reused by every call ordered on
+# that stream (each launch leaves it zeroed).  Buffers are never freed while the
+# process runs: a CUDA graph captured with one keeps using its address.
+_SYNC = {}
+_SYNC_RETIRED = []
+_SYNC_MIN_BYTES = 64 << 10
+
+
+def _sync_buffer(t, M):
+    need = int(lib().b200q_prologue_sync_bytes(M))
+    key = (t.device.index, torch.cuda.current_stream(t.device).cuda_stream)
+    buf = _SYNC.get(key)
+    if buf is None or buf.numel() < need:
+        if buf is not None:
+            _SYNC_RETIRED.append(buf)
+        buf = torch.zeros((max(need, _SYNC_MIN_BYTES),), dtype=torch.uint8, device=t.device)
+        _SYNC[key] = buf
+    return buf
+
+
+def fused_prologue_enabled():
+    """B200Q_FUSED_PROLOGUE=1 selects the one-launch route (quant inside the GEMM).
+
+    Off by default: with two quantizer warps per SM the in-kernel quant is
+    issue-bound and measured slower than its own launch on the BASELINE shapes."""
+    return os.environ.get("B200Q_FUSED_PROLOGUE", "0") == "1"
+
+
 def i8_linear(x, w, w_scale, bias=None, out_dtype=torch.bfloat16, act=None):
-    """Per-token quant + INT8 GEMM + reference dequant epilogue; x [..., K]."""
+    """Per-token quant + INT8 GEMM + reference dequant epilogue; x [..., K].
+
+    With B200Q_FUSED_PROLOGUE=1 the quantization runs inside the GEMM launch
+    (b200q_i8_linear_fused); otherwise it is its own launch (b200q_i8_linear)."""
     _require_cuda(x, w, w_scale, bias)
     shp = x.shape
     x2 = _rows_2d(x.reshape(-1, shp[-1]), "x")
@@ -223,9 +263,16 @@ def i8_linear(x, w, w_scale, bias=None, out_dtype=torch.bfloat16, act=None):
     q = torch.empty((M, K), dtype=torch.int8, device=x.device)
     s = torch.empty((M,), dtype=torch.float32, device=x.device)
     out = torch.empty((M, N), dtype=out_dtype, device=x.device)
-    _check(lib().b200q_i8_linear(_p(x2), _DT[x2.dtype], x2.stride(0), _p(w), w.stride(0), _p(ws),
-                                 ws.numel(), _p(bias), ACTS[act], _p(out), code, N, M, N, K, _p(q),
-                                 _p(s), _stream(x2)))
+    if fused_prologue_enabled():
+        sync = _sync_buffer(x2, M)
+        _check(lib().b200q_i8_linear_fused(_p(x2), _DT[x2.dtype], x2.stride(0), _p(w), w.stride(0),
+                                           _p(ws), ws.numel(), _p(bias), ACTS[act], _p(out), code,
+                                           N, M, N, K, _p(q), _p(s), _p(sync), sync.numel(),
+                                           _stream(x2)))
+    else:
+        _check(lib().b200q_i8_linear(_p(x2), _DT[x2.dtype], x2.stride(0), _p(w), w.stride(0),
+                                     _p(ws), ws.numel(), _p(bias), ACTS[act], _p(out), code, N, M,
+                                     N, K, _p(q), _p(s), _stream(x2)))
     return out.reshape(*shp[:-1], N)
 
 
@@ -275,6 +322,49 @@ def fp8_scaled_mm(a, w, scale_a=None, scale_b=None, scale_result=None, bias=None
                                      nb, _p(sr), _p(bias), bdt, ACTS[act], _p(out), code, N, M, N,
                                      K, _stream(a)))
     return out
+
+
+def fp8_linear(x, w, w_scale=None, bias=None, out_dtype=torch.bfloat16, act=None,
+               scale_result=None):
+    """bf16/f16 x [..., K] -> per-tensor e4m3 quant -> FP8 scaled GEMM with w [N,K] e4m3.
+
+    Same result as fp8_quant_tensorwise(x) followed by fp8_scaled_mm(q, w, scale,
+    w_scale, scale_result, bias, out_dtype, act).  With B200Q_FUSED_PROLOGUE=1 the
+    quantization runs inside the GEMM launch after one amax-reduction launch
+    (b200q_fp8_linear_fused)."""
+    _require_cuda(x, w, w_scale, bias, scale_result)
+    shp = x.shape
+    x2 = _rows_2d(x.reshape(-1, shp[-1]), "x")
+    if x2.dtype not in (torch.bfloat16, torch.float16):
+        raise RuntimeError(f"{TAG} fp8_linear expects bf16/f16 activations, got {x2.dtype}")
+    w = _rows_2d(w, "w")
+    M, K = x2.shape
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise RuntimeError(f"{TAG} K mismatch")
+    sb, nb = _scale_arg(w_scale, (1, N))
+    sr, _ = _scale_arg(scale_result, (1,))
+    out_dtype = out_dtype or torch.bfloat16
+    code = _out_dtype_code(out_dtype, (torch.bfloat16, torch.float16, torch.float32))
+    bdt = BIAS_NONE
+    if bias is not None:
+        bias = bias.contiguous()
+        if bias.dtype not in _BIAS_DT:
+            bias = bias.float()
+        bdt = _BIAS_DT[bias.dtype]
+    if not fused_prologue_enabled():
+        q, xs = fp8_quant_tensorwise(x2)
+        out = fp8_scaled_mm(q, w, xs.reshape(1), w_scale, scale_result, bias, out_dtype, act)
+        return out.reshape(*shp[:-1], N)
+    q = torch.empty((M, K), dtype=torch.float8_e4m3fn, device=x.device)
+    xs = torch.empty((1,), dtype=torch.float32, device=x.device)
+    out = torch.empty((M, N), dtype=out_dtype, device=x.device)
+    sync = _sync_buffer(x2, M)
+    _check(lib().b200q_fp8_linear_fused(_p(x2), _DT[x2.dtype], x2.stride(0), _p(w), w.stride(0),
+                                        _p(sb), nb, _p(sr), _p(bias), bdt, ACTS[act], _p(out), code,
+                                        N, M, N, K, _p(q), _p(xs), _p(sync), sync.numel(),
+                                        _stream(x2)))
+    return out.reshape(*shp[:-1], N)
 
 
 def w8a16_linear(x, w, w_scale=None, bias=None, act=None, out_dtype=None):
@@ -339,6 +429,8 @@ def _register_ops():
     L.define("i8_linear(Tensor x, Tensor w, Tensor w_scale, Tensor? bias=None, "
              "ScalarType out_dtype=15, str act='none') -> Tensor")
     L.define("fp8_quant_tensorwise(Tensor x) -> (Tensor, Tensor)")
+    L.define("fp8_linear(Tensor x, Tensor w, Tensor? w_scale=None, Tensor? bias=None, "
+             "ScalarType out_dtype=15, str act='none', Tensor? scale_result=None) -> Tensor")
     L.define("fp8_scaled_mm(Tensor a, Tensor w, Tensor? scale_a=None, Tensor? scale_b=None, "
              "Tensor? scale_result=None, Tensor? bias=None, ScalarType out_dtype=15, "
              "str act='none') -> Tensor")
@@ -354,6 +446,7 @@ def _register_ops():
         "i8_matmul_nt_fused_cs": i8_matmul_nt_fused_cs,
         "i8_linear": i8_linear,
         "fp8_quant_tensorwise": fp8_quant_tensorwise,
+        "fp8_linear": fp8_linear,
         "fp8_scaled_mm": lambda a, w, sa=None, sb=None, sr=None, b=None, od=torch.bfloat16,
         act="none": fp8_scaled_mm(a, w, sa, sb, sr, b, od, act),
         "w8a16_linear": w8a16_linear,
@@ -382,6 +475,8 @@ def _register_ops():
                                            x.new_empty((), dtype=torch.float32)),
         "fp8_scaled_mm": lambda a, w, sa=None, sb=None, sr=None, b=None, od=torch.bfloat16,
         act="none": a.new_empty((a.shape[0], w.shape[0]), dtype=od),
+        "fp8_linear": lambda x, w, ws=None, b=None, od=torch.bfloat16, act="none", sr=None:
+        x.new_empty((*x.shape[:-1], w.shape[0]), dtype=od),
         "w8a16_linear": lambda x, w, ws=None, b=None, act="none", od=None: x.new_empty(
             (*x.shape[:-1], w.shape[0]), dtype=od or x.dtype),
         "fp8_decode": lambda t, od=torch.float32: t.new_empty(t.shape, dtype=od),

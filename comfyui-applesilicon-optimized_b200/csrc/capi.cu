@@ -117,36 +117,38 @@ int raster_group_m(int64_t lda, int64_t ldw, int64_t M, int64_t N, int64_t K) {
 }
 
 // ------------------------------------------------------------ 8-bit GEMM dispatch
-template <MmaKind KIND, int BN, int STAGES, int EPI>
+template <MmaKind KIND, int BN, int STAGES, int EPI, int PRO>
 int launch_gemm8_tc(const DeviceInfo* d, const void* a, int64_t lda, const void* w, int64_t ldw,
-                    int M, int N, int K, const EpiArgs& ep, cudaStream_t st) {
+                    int M, int N, int K, const EpiArgs& ep, const Prologue& pro, cudaStream_t st) {
   CUtensorMap ta, tb;
   if (!make_tmap(&ta, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M, lda, kGemmBK, kGemmBM,
                  CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_tmap(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldw, kGemmBK, BN,
                  CU_TENSOR_MAP_SWIZZLE_128B))
     return B200Q_ERR_CUDA;
-  auto kern = gemm8_tc_kernel<KIND, BN, STAGES, EPI>;
-  constexpr int smem = Gemm8Layout<BN, STAGES>::kSmemBytes;
+  auto kern = gemm8_tc_kernel<KIND, BN, STAGES, EPI, PRO>;
+  constexpr int smem = PRO != kProNone ? Gemm8Layout<BN, STAGES>::kSmemBytesPro
+                                       : Gemm8Layout<BN, STAGES>::kSmemBytes;
   if (!set_smem(kern, smem)) return B200Q_ERR_CUDA;
   const int64_t tiles = int64_t((M + kGemmBM - 1) / kGemmBM) * ((N + BN - 1) / BN);
   const int grid = static_cast<int>(tiles < d->num_sms ? tiles : d->num_sms);
-  kern<<<grid, kGemmThreads, smem, st>>>(ta, tb, M, N, K, raster_group_m(lda, ldw, M, N, K), ep);
+  kern<<<grid, kGemmThreads, smem, st>>>(ta, tb, M, N, K, raster_group_m(lda, ldw, M, N, K), ep, pro);
   return finish_launch();
 }
 
 // CTA-pair kernel: clusters of 2, grid = 2 x min(tiles, SMs / 2).
-template <MmaKind KIND, int STAGES, int EPI>
+template <MmaKind KIND, int STAGES, int EPI, int PRO>
 int launch_gemm8_tc2(const DeviceInfo* d, const void* a, int64_t lda, const void* w, int64_t ldw,
-                     int M, int N, int K, const EpiArgs& ep, cudaStream_t st) {
+                     int M, int N, int K, const EpiArgs& ep, const Prologue& pro, cudaStream_t st) {
   CUtensorMap ta, tb;
   if (!make_tmap(&ta, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M, lda, kGemmBK, 128,
                  CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_tmap(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldw, kGemmBK, 128,
                  CU_TENSOR_MAP_SWIZZLE_128B))
     return B200Q_ERR_CUDA;
-  auto kern = gemm8_tc2_kernel<KIND, STAGES, EPI>;
-  constexpr int smem = Gemm8PairLayout<STAGES>::kSmemBytes;
+  auto kern = gemm8_tc2_kernel<KIND, STAGES, EPI, PRO>;
+  constexpr int smem = PRO != kProNone ? Gemm8PairLayout<STAGES>::kSmemBytesPro
+                                       : Gemm8PairLayout<STAGES>::kSmemBytes;
   if (!set_smem(kern, smem)) return B200Q_ERR_CUDA;
   const int64_t tiles = int64_t((M + 255) / 256) * ((N + 255) / 256);
   const int64_t pairs = tiles < d->num_sms / 2 ? tiles : d->num_sms / 2;
@@ -162,9 +164,13 @@ int launch_gemm8_tc2(const DeviceInfo* d, const void* a, int64_t lda, const void
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, raster_group_m(lda, ldw, M, N, K), ep) !=
-      cudaSuccess)
-    return finish_launch();
+  const cudaError_t le =
+      cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, raster_group_m(lda, ldw, M, N, K), ep, pro);
+  if (le != cudaSuccess) {
+    cudaGetLastError();
+    fprintf(stderr, "[b200q] cluster launch failed: %s\n", cudaGetErrorString(le));
+    return B200Q_ERR_CUDA;
+  }
   return finish_launch();
 }
 
@@ -188,21 +194,28 @@ bool pair_kernels_enabled() {
   return on;
 }
 
-template <MmaKind KIND, int EPI>
+bool gemm8_tc_eligible(const void* a, int64_t lda, const void* w, int64_t ldw, int64_t K) {
+  return K > 0 && (K % 16 == 0) && (lda % 16 == 0) && (ldw % 16 == 0) && aligned16(a) && aligned16(w);
+}
+
+// Tensor-core dispatch; PRO != kProNone means `a` is the code buffer that the
+// launch's own quant prologue fills (gemm8_tc_eligible must hold).
+template <MmaKind KIND, int EPI, int PRO = kProNone>
 int gemm8(const void* a, int64_t lda, const void* w, int64_t ldw, int64_t M, int64_t N, int64_t K,
-          const EpiArgs& ep, cudaStream_t st) {
+          const EpiArgs& ep, cudaStream_t st, const Prologue& pro = Prologue{}) {
   const DeviceInfo* d = current_device();
   if (!d) return B200Q_ERR_UNSUPPORTED;
   if (M == 0 || N == 0) return B200Q_OK;
-  const bool tc = K > 0 && (K % 16 == 0) && (lda % 16 == 0) && (ldw % 16 == 0) && aligned16(a) &&
-                  aligned16(w);
   constexpr bool kFp8 = KIND == MmaKind::F8F6F4;
-  if (!tc) return launch_gemm8_simt<kFp8, EPI>(a, lda, w, ldw, int(M), int(N), int(K), ep, st);
+  if (!gemm8_tc_eligible(a, lda, w, ldw, K)) {
+    if constexpr (PRO != kProNone) return B200Q_ERR_INVALID;
+    else return launch_gemm8_simt<kFp8, EPI>(a, lda, w, ldw, int(M), int(N), int(K), ep, st);
+  }
   if (N <= 128)
-    return launch_gemm8_tc<KIND, 128, 6, EPI>(d, a, lda, w, ldw, int(M), int(N), int(K), ep, st);
+    return launch_gemm8_tc<KIND, 128, 6, EPI, PRO>(d, a, lda, w, ldw, int(M), int(N), int(K), ep, pro, st);
   if (M >= 256 && pair_kernels_enabled())
-    return launch_gemm8_tc2<KIND, 6, EPI>(d, a, lda, w, ldw, int(M), int(N), int(K), ep, st);
-  return launch_gemm8_tc<KIND, 256, 4, EPI>(d, a, lda, w, ldw, int(M), int(N), int(K), ep, st);
+    return launch_gemm8_tc2<KIND, 6, EPI, PRO>(d, a, lda, w, ldw, int(M), int(N), int(K), ep, pro, st);
+  return launch_gemm8_tc<KIND, 256, 4, EPI, PRO>(d, a, lda, w, ldw, int(M), int(N), int(K), ep, pro, st);
 }
 
 EpiArgs make_epi(void* out, int64_t ldo, int out_dtype, int64_t M, int64_t N) {
@@ -316,6 +329,17 @@ int dispatch_w8a16_tc(const DeviceInfo* d, int bt, const void* x, int64_t ldx, c
   }
 }
 
+// The prologue's bulk-copy quantizer reads 16-byte row segments of x.
+bool ring_ok(const void* x, int64_t ldx, int64_t K) {
+  return aligned16(x) && K % 8 == 0 && ldx % 8 == 0;
+}
+
+// Sync words of a fused-prologue launch: 16-byte aligned, large enough for M rows.
+bool sync_ok(const unsigned int* sync, size_t sync_bytes, int64_t M) {
+  return sync && (reinterpret_cast<uintptr_t>(sync) & 15) == 0 &&
+         sync_bytes >= b200q_prologue_sync_bytes(M);
+}
+
 int grid_for(int64_t work, int per_block, const DeviceInfo* d) {
   int64_t g = (work + per_block - 1) / per_block;
   const int64_t cap = int64_t(d->num_sms) * 8;
@@ -422,6 +446,107 @@ int b200q_i8_linear(const void* x, int x_dtype, int64_t ldx, const int8_t* w, in
   return b200q_i8_matmul_nt_dequant(q_scratch, K, w, ldw, scale_scratch, col_scale,
                                     col_scale_numel, bias, act, out, out_dtype, ldo, M, N, K,
                                     stream);
+}
+
+size_t b200q_prologue_sync_bytes(int64_t M) {
+  const int64_t bands = M > 0 ? (M + kBandRows - 1) / kBandRows : 0;
+  return static_cast<size_t>(((kSyncBands + bands) * 4 + 255) & ~int64_t(255));
+}
+
+int b200q_i8_linear_fused(const void* x, int x_dtype, int64_t ldx, const int8_t* w, int64_t ldw,
+                          const float* col_scale, int64_t col_scale_numel, const void* bias,
+                          int act, void* out, int out_dtype, int64_t ldo, int64_t M, int64_t N,
+                          int64_t K, int8_t* q_scratch, float* scale_scratch, unsigned int* sync,
+                          size_t sync_bytes, void* stream) {
+  if (!x || !w || !out || !col_scale || !q_scratch || !scale_scratch || !valid_dims(M, N, K) ||
+      K == 0 || ldx < K || ldw < K || ldo < N || (col_scale_numel != 1 && col_scale_numel != N) ||
+      (x_dtype != B200Q_BF16 && x_dtype != B200Q_F16) ||
+      (out_dtype != B200Q_BF16 && out_dtype != B200Q_F16) || act < B200Q_ACT_NONE ||
+      act > B200Q_ACT_GELU_ERF)
+    return B200Q_ERR_INVALID;
+  if (!sync_ok(sync, sync_bytes, M)) return B200Q_ERR_WORKSPACE;
+  const DeviceInfo* d = current_device();
+  if (!d) return B200Q_ERR_UNSUPPORTED;
+  if (M == 0 || N == 0) return B200Q_OK;
+  // Shapes the TMA path cannot take run as quant launch + SIMT GEMM.
+  if (!gemm8_tc_eligible(q_scratch, K, w, ldw, K))
+    return b200q_i8_linear(x, x_dtype, ldx, w, ldw, col_scale, col_scale_numel, bias, act, out,
+                           out_dtype, ldo, M, N, K, q_scratch, scale_scratch, stream);
+  EpiArgs ep = make_epi(out, ldo, out_dtype, M, N);
+  ep.row_scale = scale_scratch;
+  ep.row_scale_vec = 1;
+  ep.col_scale = col_scale;
+  ep.col_scale_vec = col_scale_numel == N && N != 1 ? 1 : 0;
+  ep.bias = bias;
+  ep.bias_dtype = bias ? (out_dtype == B200Q_BF16 ? kBiasBF16 : kBiasF16) : kBiasNone;
+  ep.act = act;
+  Prologue pro{};
+  pro.x = x;
+  pro.ldx = ldx;
+  pro.q = reinterpret_cast<uint8_t*>(q_scratch);
+  pro.scales = scale_scratch;
+  pro.sync = sync;
+  pro.x_f16 = x_dtype == B200Q_F16 ? 1 : 0;
+  pro.nbands = static_cast<int>((M + kBandRows - 1) / kBandRows);
+  pro.ring = ring_ok(x, ldx, K) ? 1 : 0;
+  return gemm8<MmaKind::I8, kEpiI8Dequant, kProInt8Row>(q_scratch, K, w, ldw, M, N, K, ep,
+                                                        static_cast<cudaStream_t>(stream), pro);
+}
+
+int b200q_fp8_linear_fused(const void* x, int x_dtype, int64_t ldx, const uint8_t* w, int64_t ldw,
+                           const float* scale_b, int64_t scale_b_numel, const float* scale_result,
+                           const void* bias, int bias_dtype, int act, void* out, int out_dtype,
+                           int64_t ldo, int64_t M, int64_t N, int64_t K, uint8_t* q_scratch,
+                           float* scale_out, unsigned int* sync, size_t sync_bytes, void* stream) {
+  if (!x || !w || !out || !q_scratch || !scale_out || !valid_dims(M, N, K) || K == 0 || ldx < K ||
+      ldw < K || ldo < N || (scale_b && scale_b_numel != 1 && scale_b_numel != N) ||
+      (x_dtype != B200Q_BF16 && x_dtype != B200Q_F16) ||
+      (out_dtype != B200Q_BF16 && out_dtype != B200Q_F16 && out_dtype != B200Q_F32) ||
+      bias_dtype < B200Q_BIAS_NONE || bias_dtype > B200Q_BIAS_F32 ||
+      (bias_dtype != B200Q_BIAS_NONE && !bias) || act < B200Q_ACT_NONE || act > B200Q_ACT_GELU_ERF)
+    return B200Q_ERR_INVALID;
+  if (!sync_ok(sync, sync_bytes, M)) return B200Q_ERR_WORKSPACE;
+  const DeviceInfo* d = current_device();
+  if (!d) return B200Q_ERR_UNSUPPORTED;
+  if (M == 0) return B200Q_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  unsigned int* amax = sync + kSyncAmax;
+  if (N == 0 || !gemm8_tc_eligible(q_scratch, K, w, ldw, K)) {
+    // Two-launch route; the quant's amax word is cleared again afterwards so
+    // the sync buffer stays all-zero between calls.
+    int s = b200q_fp8_quant_tensorwise(x, x_dtype, M, K, ldx, q_scratch, K, scale_out, amax, stream);
+    if (s == B200Q_OK && N > 0)
+      s = b200q_fp8_scaled_mm(q_scratch, K, w, ldw, scale_out, 1, scale_b, scale_b_numel,
+                              scale_result, bias, bias_dtype, act, out, out_dtype, ldo, M, N, K,
+                              stream);
+    if (cudaMemsetAsync(amax, 0, sizeof(unsigned int), st) != cudaSuccess && s == B200Q_OK)
+      s = B200Q_ERR_CUDA;
+    return s;
+  }
+  const int grid = grid_for(M * K / 8 + 1, 256, d);
+  if (x_dtype == B200Q_BF16)
+    absmax_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), ldx, M, int(K), amax);
+  else
+    absmax_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(x), ldx, M, int(K), amax);
+  const int s = finish_launch();
+  if (s != B200Q_OK) return s;
+  EpiArgs ep = make_epi(out, ldo, out_dtype, M, N);
+  ep.col_scale = scale_b;
+  ep.col_scale_vec = scale_b && scale_b_numel == N && N != 1 ? 1 : 0;
+  ep.extra_scale = scale_result;
+  ep.bias = bias;
+  ep.bias_dtype = bias ? bias_dtype : kBiasNone;
+  ep.act = act;
+  Prologue pro{};
+  pro.x = x;
+  pro.ldx = ldx;
+  pro.q = q_scratch;
+  pro.scales = scale_out;
+  pro.sync = sync;
+  pro.x_f16 = x_dtype == B200Q_F16 ? 1 : 0;
+  pro.nbands = static_cast<int>((M + kBandRows - 1) / kBandRows);
+  pro.ring = ring_ok(x, ldx, K) ? 1 : 0;
+  return gemm8<MmaKind::F8F6F4, kEpiScaled, kProFp8Tensor>(q_scratch, K, w, ldw, M, N, K, ep, st, pro);
 }
 
 int b200q_fp8_scaled_mm(const uint8_t* a, int64_t lda, const uint8_t* w, int64_t ldw,

@@ -17,11 +17,15 @@
 //               before the TMEM wait; element math (raw int32 / reference
 //               two-rounding INT8 dequant / FP8 scaled + bias + GELU) and
 //               16-byte global stores.
+// With a quant prologue (PRO != kProNone, prologue.cuh) warps 2 and 3 quantize
+// activation rows (bulk-copied into their shared-memory rings) while the tensor
+// cores work, and the producer waits for a band's rows before loading it.
 // Tiles are walked in groups of 16 M-tiles so the ~148 concurrently running
 // tiles share A row panels and W column panels in L2.
 #pragma once
 
 #include "numerics.cuh"
+#include "prologue.cuh"
 #include "ptx.cuh"
 
 namespace b200q {
@@ -42,6 +46,9 @@ struct Gemm8Layout {
   // full[S], empty[S], acc_full[2], acc_empty[2], tmem slot, abort flag
   static constexpr int kBarBytes = (2 * STAGES + 4) * 8 + 16;
   static constexpr int kSmemBytes = kBarOffset + kBarBytes + 1024;  // + alignment slack
+  // Quant-prologue launches: the quantizer warps' bulk-copy rings follow.
+  static constexpr int kQuantOffset = (kBarOffset + kBarBytes + 127) & ~127;
+  static constexpr int kSmemBytesPro = kQuantOffset + kQSmemBytes + 1024;
   static constexpr uint32_t kTmemCols = 2 * BN;
 };
 
@@ -213,10 +220,10 @@ __device__ __forceinline__ void epilogue_math(const uint32_t (&r)[32], const flo
   }
 }
 
-template <MmaKind KIND, int BN, int STAGES, int EPI>
+template <MmaKind KIND, int BN, int STAGES, int EPI, int PRO>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    int M, int N, int K, int group_m, EpiArgs ep) {
+                    int M, int N, int K, int group_m, EpiArgs ep, Prologue pro) {
   using L = Gemm8Layout<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -229,6 +236,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* exit_flag = reinterpret_cast<int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -247,6 +255,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&acc_empty[b], 8 * 32);
     }
     *abort_flag = 0;
+    if constexpr (PRO != kProNone) {
+      uint64_t* qfull = reinterpret_cast<uint64_t*>(smem + L::kQuantOffset + kQWarps * kQSlots * kQSlotBytes);
+      for (int i = 0; i < kQWarps * kQSlots; ++i) mbar_init(&qfull[i], 1);
+    }
     fence_mbarrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -261,6 +273,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  float pro_s = 1.0f;  // per-tensor activation scale of the fp8 prologue
+  if constexpr (PRO == kProFp8Tensor) {
+    pro_s = pro_fp8_scale(pro);
+    if (blockIdx.x == 0 && threadIdx.x == 0) pro.scales[0] = pro_s;
+  }
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -268,9 +285,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      int ready_band = -1;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         int mb, nb;
         gemm_tile_coords(tile, num_m, num_n, group_m, mb, nb);
+        if constexpr (PRO != kProNone) {
+          if (mb != ready_band) {
+            if (!pro_band_wait(pro, mb, M, abort_flag)) break;
+            ready_band = mb;
+          }
+        }
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
@@ -314,6 +338,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
     __syncwarp();
+  } else if (warp == 2 || warp == 3) {
+    // ------------------------------------------------------------ quantizer warps
+    if constexpr (PRO != kProNone) {
+      if (pro.ring) {
+        uint8_t* ring = smem + L::kQuantOffset + (warp - 2) * kQSlots * kQSlotBytes;
+        uint64_t* qfull = reinterpret_cast<uint64_t*>(smem + L::kQuantOffset + kQWarps * kQSlots * kQSlotBytes) +
+                          (warp - 2) * kQSlots;
+        if (pro.x_f16) pro_ring_worker<PRO, __half>(pro, M, K, pro_s, ring, qfull, abort_flag);
+        else pro_ring_worker<PRO, __nv_bfloat16>(pro, M, K, pro_s, ring, qfull, abort_flag);
+      } else {
+        pro_worker<PRO>(pro, M, K, pro_s);
+      }
+    }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue
     // 8 warps: warp w reads TMEM lane quarter (w % 4) and column half (w - 4) / 4.
@@ -333,8 +370,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const int64_t m = static_cast<int64_t>(mb) * kGemmBM + row_local;
       const bool row_ok = m < M;
+      if constexpr (PRO == kProInt8Row) {
+        // Row scales come from the quantizers: acquire the band before reading them.
+        if (!__all_sync(0xffffffffu, pro_band_wait(pro, mb, M, abort_flag))) break;
+      }
       float rs = 1.0f;
-      if (EPI != kEpiInt32 && ep.row_scale && row_ok) rs = __ldg(ep.row_scale + (ep.row_scale_vec ? m : 0));
+      if constexpr (PRO == kProFp8Tensor) {
+        rs = pro_s;
+      } else {
+        if (EPI != kEpiInt32 && ep.row_scale && row_ok) rs = __ldcg(ep.row_scale + (ep.row_scale_vec ? m : 0));
+      }
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
 #pragma unroll 1
       for (int c = half * kChunks; c < (half + 1) * kChunks; ++c) {
@@ -364,6 +409,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 2) tmem_dealloc(tmem_base, L::kTmemCols);
+  if constexpr (PRO != kProNone) pro_exit(pro, exit_flag);
 }
 
 // ---------------------------------------------------------------------------
@@ -384,13 +430,15 @@ struct Gemm8PairLayout {
   static constexpr int kBarOffset = STAGES * kStageBytes;
   static constexpr int kBarBytes = (2 * STAGES + 4) * 8 + 16;
   static constexpr int kSmemBytes = kBarOffset + kBarBytes + 1024;
+  static constexpr int kQuantOffset = (kBarOffset + kBarBytes + 127) & ~127;
+  static constexpr int kSmemBytesPro = kQuantOffset + kQSmemBytes + 1024;
   static constexpr uint32_t kTmemCols = 512;  // 2 x 256-column accumulators
 };
 
-template <MmaKind KIND, int STAGES, int EPI>
+template <MmaKind KIND, int STAGES, int EPI, int PRO>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm8_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     int M, int N, int K, int group_m, EpiArgs ep) {
+                     int M, int N, int K, int group_m, EpiArgs ep, Prologue pro) {
   using L = Gemm8PairLayout<STAGES>;
   constexpr int BM = 256, BN = 256;
   extern __shared__ uint8_t smem_raw[];
@@ -404,6 +452,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* exit_flag = reinterpret_cast<int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -426,6 +475,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&acc_empty[b], 2 * 8);  // 8 epilogue warps in each CTA
     }
     *abort_flag = 0;
+    if constexpr (PRO != kProNone) {
+      uint64_t* qfull = reinterpret_cast<uint64_t*>(smem + L::kQuantOffset + kQWarps * kQSlots * kQSlotBytes);
+      for (int i = 0; i < kQWarps * kQSlots; ++i) mbar_init(&qfull[i], 1);
+    }
     fence_mbarrier_init();
   }
   if (warp == 0 && lane == 0) {
@@ -440,6 +493,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  float pro_s = 1.0f;  // per-tensor activation scale of the fp8 prologue
+  if constexpr (PRO == kProFp8Tensor) {
+    pro_s = pro_fp8_scale(pro);
+    if (blockIdx.x == 0 && threadIdx.x == 0) pro.scales[0] = pro_s;
+  }
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer (both CTAs)
@@ -448,11 +506,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      int ready_band = -1;
       for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
         int mb, nb;
         gemm_tile_coords(tile, num_m, num_n, group_m, mb, nb);
         const int a_row = mb * BM + static_cast<int>(rank) * 128;
         const int b_row = nb * BN + static_cast<int>(rank) * 128;
+        if constexpr (PRO != kProNone) {
+          const int band = a_row / kBandRows;
+          if (band != ready_band) {
+            if (!pro_band_wait(pro, band, M, abort_flag)) break;
+            ready_band = band;
+          }
+        }
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * L::kStageBytes);
@@ -502,6 +568,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
     }
     __syncwarp();
+  } else if (warp == 2 || warp == 3) {
+    // ------------------------------------------------------------ quantizer warps
+    if constexpr (PRO != kProNone) {
+      if (pro.ring) {
+        uint8_t* ring = smem + L::kQuantOffset + (warp - 2) * kQSlots * kQSlotBytes;
+        uint64_t* qfull = reinterpret_cast<uint64_t*>(smem + L::kQuantOffset + kQWarps * kQSlots * kQSlotBytes) +
+                          (warp - 2) * kQSlots;
+        if (pro.x_f16) pro_ring_worker<PRO, __half>(pro, M, K, pro_s, ring, qfull, abort_flag);
+        else pro_ring_worker<PRO, __nv_bfloat16>(pro, M, K, pro_s, ring, qfull, abort_flag);
+      } else {
+        pro_worker<PRO>(pro, M, K, pro_s);
+      }
+    }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int q = warp & 3;
@@ -521,8 +600,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const int64_t m = static_cast<int64_t>(mb) * BM + static_cast<int64_t>(rank) * 128 + row_local;
       const bool row_ok = m < M;
+      if constexpr (PRO == kProInt8Row) {
+        const int band = (mb * BM) / kBandRows + static_cast<int>(rank);
+        if (!__all_sync(0xffffffffu, pro_band_wait(pro, band, M, abort_flag))) break;
+      }
       float rs = 1.0f;
-      if (EPI != kEpiInt32 && ep.row_scale && row_ok) rs = __ldg(ep.row_scale + (ep.row_scale_vec ? m : 0));
+      if constexpr (PRO == kProFp8Tensor) {
+        rs = pro_s;
+      } else {
+        if (EPI != kEpiInt32 && ep.row_scale && row_ok) rs = __ldcg(ep.row_scale + (ep.row_scale_vec ? m : 0));
+      }
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
 #pragma unroll 1
       for (int c = half * kChunks; c < (half + 1) * kChunks; ++c) {
@@ -553,6 +640,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   cluster_sync();  // the peer's shared memory and barriers stay alive until both are done
   tc_fence_after();
   if (warp == 2) tmem_dealloc_pair(tmem_base, L::kTmemCols);
+  if constexpr (PRO != kProNone) pro_exit(pro, exit_flag);
 }
 
 template <int EPI>

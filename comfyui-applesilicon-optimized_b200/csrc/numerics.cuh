@@ -57,12 +57,16 @@ __device__ __forceinline__ uint32_t e4m3x2_to_bf16x2(uint16_t two) {
   return *reinterpret_cast<uint32_t*>(&b);
 }
 
-// GELU with the tanh approximation (torch approximate="tanh") and exact erf GELU.
+// GELU with the tanh approximation (torch approximate="tanh") and exact erf GELU,
+// written without cancellation: for negative x the textbook forms
+// 0.5 x (1 + tanh(u)) and 0.5 x (1 + erf(x / sqrt 2)) subtract two numbers close
+// to 1 and lose most of fp32's digits (several fp16 ULPs at x ~ -4).  Identities
+// used: 1 + tanh(u) = 2 / (1 + exp(-2u)) and 1 + erf(z) = erfc(-z).
 __device__ __forceinline__ float gelu_tanh(float x) {
   const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
   const float k1 = 0.044715f;
-  float inner = k0 * (x + k1 * x * x * x);
-  return 0.5f * x * (1.0f + tanhf(inner));
+  const float u = k0 * (x + k1 * x * x * x);
+  return __fdividef(x, 1.0f + expf(-2.0f * u));
 }
 __device__ __forceinline__ float gelu_erf(float x) {
   return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f));

@@ -9,7 +9,9 @@
 //      q      = int8(clamp(rint(T(x / s)), -128, 127))   (T = input dtype, RNE)
 //    One CTA of 256 threads per row, 16-byte loads; the row stays in registers
 //    between the absmax and the quantize pass (K <= 16384 for bf16/fp16), so HBM
-//    sees one read of x and one write of q.
+//    sees one read of x and one write of q.  x / s is formed as x * RN(1/s) with
+//    an exact-divide fallback near rounding ties (quotients8 below), which gives
+//    the divide's result bit for bit at a fraction of its cost.
 //
 //  * fp8 per-tensor quant (the activation side of the FP8 W8A8 route):
 //      amax = max|x| over the tensor; scale = max(amax / 448, 1e-30)
@@ -66,21 +68,94 @@ __device__ __forceinline__ int quant_code(float x, float s_math) {
   return static_cast<int>(d);
 }
 
-template <typename T>
-__device__ __forceinline__ uint2 quant8(const uint4& v, float s_math) {
-  const T* e = reinterpret_cast<const T*>(&v);
-  uint32_t lo = 0, hi = 0;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) lo |= (static_cast<uint32_t>(quant_code<T>(to_float<T>(e[i]), s_math)) & 0xFFu) << (8 * i);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) hi |= (static_cast<uint32_t>(quant_code<T>(to_float<T>(e[i + 4]), s_math)) & 0xFFu) << (8 * i);
-  return make_uint2(lo, hi);
-}
 
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
+}
+
+// ---------------------------------------------------------------------------
+// Quotients without a divide per element.
+//
+// The reference computes q = round(x / s) with a correctly rounded fp32 divide
+// and then rounds that quotient to a coarser format F (bf16/fp16 before rint
+// for int8, e4m3 for fp8).  Here y = RN(x * r) with r = RN(1/s):
+//   y = (x/s)(1+d1)(1+d2), |d1|,|d2| <= 2^-24   =>   |y - RN(x/s)| <= 3 ulp.
+// Rounding to F drops the low bits of the fp32 pattern and only changes
+// outcome where those bits cross the tie pattern 100..0.  So when the dropped
+// bits of y are more than 4 ulps away from the tie, y and RN(x/s) round to the
+// same F value and y is used; otherwise (about 9 in 2^16 values for bf16) the
+// exact __fdiv_rn quotient is taken.  The result is therefore identical to
+// round_F(__fdiv_rn(x, s)) for every input.
+//
+// Range notes: for fp16 the 13-bit rule is only the tie rule in fp16's normal
+// range; below it (|y| < 2^-14) rint gives 0 whichever way the quotient
+// rounds, so the code is unaffected.  For e4m3 the 20-bit rule holds in the
+// normal range (|y| >= 2^-6); nonzero quotients below it take the exact path.
+template <typename T>
+struct TieBits;
+template <>
+struct TieBits<__nv_bfloat16> {
+  static constexpr uint32_t kMask = 0xFFFFu, kTie = 0x8000u;
+};
+template <>
+struct TieBits<__half> {
+  static constexpr uint32_t kMask = 0x1FFFu, kTie = 0x1000u;
+};
+
+template <typename T>
+__device__ __forceinline__ bool near_tie(float y) {
+  return (__float_as_uint(y) & TieBits<T>::kMask) - (TieBits<T>::kTie - 4u) <= 8u;
+}
+
+__device__ __forceinline__ bool near_tie_e4m3(float y) {
+  const uint32_t b = __float_as_uint(y);
+  const uint32_t mag = b & 0x7FFFFFFFu;
+  return (mag < 0x3C800000u && mag != 0u) || (b & 0xFFFFFu) - (0x80000u - 4u) <= 8u;
+}
+
+// Eight quotients x[i] / s, each equal to __fdiv_rn(x[i], s) wherever the
+// rounding to F could tell them apart (F = T, or e4m3 when E4M3 is true).  The
+// exact divides sit in one rarely taken branch after the straight-line path.
+template <typename T, bool E4M3>
+__device__ __forceinline__ void quotients8(const uint4& v, float s, float r, float (&y)[8]) {
+  const T* e = reinterpret_cast<const T*>(&v);
+  uint32_t slow = 0u;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    y[i] = __fmul_rn(to_float<T>(e[i]), r);
+    const bool t = E4M3 ? near_tie_e4m3(y[i]) : near_tie<T>(y[i]);
+    slow |= t ? (1u << i) : 0u;
+  }
+  if (slow) {  // fully unrolled: a runtime index would move y[] to local memory
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if ((slow >> i) & 1u) y[i] = __fdiv_rn(to_float<T>(e[i]), s);
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ uint2 quant8_fast(const uint4& v, float s, float r) {
+  float y[8];
+  quotients8<T, false>(v, s, r, y);
+  uint32_t w[2] = {0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float d = fminf(fmaxf(rintf(round_to<T>(y[i])), -128.0f), 127.0f);
+    w[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(d)) & 0xFFu) << (8 * (i & 3));
+  }
+  return make_uint2(w[0], w[1]);
+}
+
+template <typename T>
+__device__ __forceinline__ uint2 fp8_quant8_fast(const uint4& v, float s, float r) {
+  float y[8];
+  quotients8<T, true>(v, s, r, y);
+  uint32_t w[2] = {0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) w[i >> 2] |= static_cast<uint32_t>(encode_e4m3_sat(y[i])) << (8 * (i & 3));
+  return make_uint2(w[0], w[1]);
 }
 
 // Row scale from the row's absmax; writes scales[row], returns s_math.
@@ -130,13 +205,14 @@ __global__ void __launch_bounds__(kQuantThreads)
     for (int idx = threadIdx.x + kQuantMaxVec * kQuantThreads; idx < nvec; idx += kQuantThreads)
       amax = fmaxf(amax, absmax8<T>(xr[idx]));
     const float s_math = row_scale_from_absmax<T>(amax, red, &bcast, scales, row);
+    const float r_math = __frcp_rn(s_math);
 #pragma unroll
     for (int i = 0; i < kQuantMaxVec; ++i) {
       const int idx = threadIdx.x + i * kQuantThreads;
-      if (idx < nvec) qr[idx] = quant8<T>(v[i], s_math);
+      if (idx < nvec) qr[idx] = quant8_fast<T>(v[i], s_math, r_math);
     }
     for (int idx = threadIdx.x + kQuantMaxVec * kQuantThreads; idx < nvec; idx += kQuantThreads)
-      qr[idx] = quant8<T>(xr[idx], s_math);
+      qr[idx] = quant8_fast<T>(xr[idx], s_math, r_math);
     __syncthreads();  // red/bcast are reused by the next row
   }
 }
@@ -211,16 +287,6 @@ __device__ __forceinline__ float fp8_scale_from_amax(unsigned int bits) {
   return fmaxf(__fdiv_rn(__uint_as_float(bits), 448.0f), 1e-30f);
 }
 
-template <typename T>
-__device__ __forceinline__ uint2 fp8_quant8(const uint4& v, float s) {
-  const T* e = reinterpret_cast<const T*>(&v);
-  uint32_t lo = 0, hi = 0;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) lo |= static_cast<uint32_t>(encode_e4m3_sat(__fdiv_rn(to_float<T>(e[j]), s))) << (8 * j);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) hi |= static_cast<uint32_t>(encode_e4m3_sat(__fdiv_rn(to_float<T>(e[j + 4]), s))) << (8 * j);
-  return make_uint2(lo, hi);
-}
 
 template <typename T>
 __global__ void __launch_bounds__(256)
@@ -228,6 +294,7 @@ __global__ void __launch_bounds__(256)
                         const unsigned int* __restrict__ amax_bits, uint8_t* __restrict__ q,
                         int64_t ldq, float* __restrict__ scale_out) {
   const float s = fp8_scale_from_amax(*amax_bits);
+  const float r = __frcp_rn(s);
   if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = s;
   const bool vec = (K % 8 == 0) && (ldx % 8 == 0) && (ldq % 8 == 0) &&
                    (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
@@ -240,17 +307,18 @@ __global__ void __launch_bounds__(256)
     int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     for (; i + stride < nvec; i += 2 * stride) {
       const uint4 a = __ldcs(xv + i), b = __ldcs(xv + i + stride);
-      qv[i] = fp8_quant8<T>(a, s);
-      qv[i + stride] = fp8_quant8<T>(b, s);
+      qv[i] = fp8_quant8_fast<T>(a, s, r);
+      qv[i + stride] = fp8_quant8_fast<T>(b, s, r);
     }
-    if (i < nvec) qv[i] = fp8_quant8<T>(__ldcs(xv + i), s);
+    if (i < nvec) qv[i] = fp8_quant8_fast<T>(__ldcs(xv + i), s, r);
   } else {
     for (int64_t r = blockIdx.x; r < M; r += gridDim.x) {
       const T* xr = x + r * ldx;
       uint8_t* qr = q + r * ldq;
       if (vec) {
         for (int c = threadIdx.x; c < (K >> 3); c += blockDim.x)
-          reinterpret_cast<uint2*>(qr)[c] = fp8_quant8<T>(__ldcs(reinterpret_cast<const uint4*>(xr) + c), s);
+          reinterpret_cast<uint2*>(qr)[c] =
+              fp8_quant8_fast<T>(__ldcs(reinterpret_cast<const uint4*>(xr) + c), s, r);
       } else {
         for (int c = threadIdx.x; c < K; c += blockDim.x)
           qr[c] = encode_e4m3_sat(__fdiv_rn(to_float<T>(xr[c]), s));

@@ -118,6 +118,45 @@ B200Q_API int b200q_fp8_quant_tensorwise(const void* x, int x_dtype, int64_t M, 
                                uint8_t* q, int64_t ldq, float* scale, unsigned int* amax_scratch,
                                void* stream);
 
+/* Fused quant prologue: the activation quantization runs inside the GEMM launch
+ * (idle warps quantize 128-row bands while the tensor cores work; the TMA
+ * producer waits for a band's rows before loading them), so there is no separate
+ * quant kernel and no kernel boundary between quant and GEMM.
+ *
+ * `sync` is a caller-owned device buffer of at least b200q_prologue_sync_bytes(M)
+ * bytes, 16-byte aligned, ALL ZERO before the first call.  Every call leaves it
+ * all zero again when its kernels finish, so calls ordered on one stream (and
+ * CUDA-graph replays) can reuse it; calls that may overlap on the GPU need
+ * separate buffers. */
+B200Q_API size_t b200q_prologue_sync_bytes(int64_t M);
+
+/* b200q_i8_linear with the per-token quant fused into the GEMM launch (one
+ * launch).  Same arguments and results as b200q_i8_linear (q_scratch and
+ * scale_scratch receive the codes and scales), plus the sync buffer.  Replaces
+ * _int8_linear_kernel (_patches/int8_linear_kernel_mps.py:218-263): the
+ * reference's i8_quant_rowwise (_patches/int8_ext/int8_gemm.mm:2332) followed by
+ * i8_matmul2d_nt_fused_cs (:1823).  Shapes the TMA path cannot take (K % 16 != 0,
+ * unaligned weight) fall back to the two-launch route inside the call. */
+B200Q_API int b200q_i8_linear_fused(const void* x, int x_dtype, int64_t ldx, const int8_t* w,
+                                    int64_t ldw, const float* col_scale, int64_t col_scale_numel,
+                                    const void* bias, int act, void* out, int out_dtype,
+                                    int64_t ldo, int64_t M, int64_t N, int64_t K,
+                                    int8_t* q_scratch, float* scale_scratch, unsigned int* sync,
+                                    size_t sync_bytes, void* stream);
+
+/* FP8 W8A8 linear from a bf16/f16 activation: per-tensor e4m3 quant of x
+ * (b200q_fp8_quant_tensorwise semantics) fused into b200q_fp8_scaled_mm with
+ * scale_a = the activation scale.  Two launches: an amax reduction over x, then
+ * the GEMM whose prologue quantizes.  q_scratch [M,K] receives the codes and
+ * scale_out (one fp32) the activation scale.  Replaces the activation-quant +
+ * torch._scaled_mm pair that reaches _mps_scaled_mm (_patches/scaled_mm_fp8.py:149). */
+B200Q_API int b200q_fp8_linear_fused(const void* x, int x_dtype, int64_t ldx, const uint8_t* w,
+                                     int64_t ldw, const float* scale_b, int64_t scale_b_numel,
+                                     const float* scale_result, const void* bias, int bias_dtype,
+                                     int act, void* out, int out_dtype, int64_t ldo, int64_t M,
+                                     int64_t N, int64_t K, uint8_t* q_scratch, float* scale_out,
+                                     unsigned int* sync, size_t sync_bytes, void* stream);
+
 /* Bytes of device workspace b200q_w8a16_linear needs for this shape (0 = none). */
 B200Q_API size_t b200q_w8a16_workspace_size(int64_t M, int64_t N, int64_t K);
 
