@@ -398,6 +398,15 @@ def run_b200q(args):
     eight_bit = spec["route"] in ("fp8", "int8")
     peak = (2.0 if eight_bit else 1.0) * peaks["bf16_sustained"]
     achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None
+    # W8A16 with <= 256 tokens is bound by the FP8 weight stream (the
+    # HBM roofline), so its roofline is bytes moved per launch / launch time.
+    hbm_bound = spec["route"] == "w8a16" and M <= 256
+    achieved_gbs, bytes_per_launch = None, 0
+    if hbm_bound and n_gemm:
+        l0 = spec["layers"][0]
+        bytes_per_launch = (l0.N * l0.K + M * l0.K * 2 + M * l0.N * 2 + l0.N * 2) * len(spec["layers"])
+        achieved_gbs = bytes_per_launch * n_gemm / (gemm_ms / 1e3) / 1e9 / len(spec["layers"]) \
+            if gemm_ms > 0 else None
     traffic, traffic_src = _committed_traffic(args.workload) if args.m is None else (None, None)
 
     if rank == 0:
@@ -420,7 +429,18 @@ def run_b200q(args):
                                             if spec["route"] != "w8a16" else "none (weight-only)"),
                        "launch": ("each op of the step captured once as a CUDA graph, replayed per step"
                                   if args.launch == "graph" else "eager torch.ops calls")},
-            "roofline": {"bound": "tensor", "achieved": round(achieved, 1) if achieved else None,
+            "roofline": ({"bound": "hbm", "achieved": round(achieved_gbs, 1) if achieved_gbs else None,
+                          "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                          "frac": round(achieved_gbs / peaks["hbm_gbs"], 4) if achieved_gbs else None,
+                          "traffic": None, "traffic_source": None,
+                          "algorithmic_bytes_per_launch": bytes_per_launch // len(spec["layers"]),
+                          "kernel": "w8a16_gemv_kernel" if M <= 32 else (
+                              "w8a16_stream_kernel" if M <= 64 else "w8a16_tc_kernel"),
+                          "peak_source": f"hbm_gbs of {peaks['source']} MEASURED_PEAKS.json",
+                          "timing": "CUDA events around each launch (includes ~6 us launch latency "
+                                    "measured for an empty kernel on this path)",
+                          "gemm_launches_timed": n_gemm} if hbm_bound else
+                         {"bound": "tensor", "achieved": round(achieved, 1) if achieved else None,
                          "peak": round(peak, 1), "unit": "TFLOP/s",
                          "frac": round(achieved / peak, 4) if achieved else None,
                          "traffic": traffic, "traffic_source": traffic_src,
@@ -429,7 +449,7 @@ def run_b200q(args):
                          "peak_source": (f"{'2 x ' if eight_bit else ''}bf16_tflops_sustained of "
                                          f"{peaks['source']} MEASURED_PEAKS.json"
                                          + (" (dense FP8/INT8 rate = 2 x BF16 on B200)" if eight_bit else "")),
-                         "gemm_launches_timed": n_gemm},
+                         "gemm_launches_timed": n_gemm}),
             "e2e": {"value": round(e2e, 3), "unit": "TFLOP/s" if spec["route"] != "int8" else "TOP/s",
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                     "steps": e2e_steps},

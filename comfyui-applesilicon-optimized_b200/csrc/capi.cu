@@ -247,9 +247,9 @@ W16Plan w8a16_plan(int num_sms, int64_t M, int64_t N, int64_t K) {
   const int64_t num_kb = (K + kW16BK - 1) / kW16BK;
   int best = 1;
   double best_eff = 0.0;
-  // Token tiles of <= 64 run the streaming kernel, whose per-SM rate is bound by
-  // its MMA issue rate (measured on B200: ~80 ns per 128 x N x 16 MMA at N <= 64),
-  // not by how many SMs stream; split-K only adds partial traffic there.
+  // Token tiles of <= 64 run the streaming kernel as one tile per CTA: its
+  // split-K fix-up (one dependent L2 round trip per 4 tokens) cost more than the
+  // idle SMs it would fill (measured: S = 2 turned 34 us into 74 us at M = 64).
   const int max_splits = p.bt <= 64 ? 1 : kW16MaxSplits;
   for (int s = 1; s <= max_splits; ++s) {
     if (s > 1 && s * 4 > num_kb) break;
@@ -332,6 +332,31 @@ int dispatch_w8a16_tc(const DeviceInfo* d, int bt, const void* x, int64_t ldx, c
 // The prologue's bulk-copy quantizer reads 16-byte row segments of x.
 bool ring_ok(const void* x, int64_t ldx, int64_t K) {
   return aligned16(x) && K % 8 == 0 && ldx % 8 == 0;
+}
+
+template <int MT, bool XF16>
+int launch_w8a16_gemv(const void* x, int64_t ldx, const uint8_t* w, int64_t ldw, int64_t M,
+                      int64_t N, int64_t K, const EpiArgs& ep, cudaStream_t st) {
+  CUtensorMap tw;
+  if (!make_tmap(&tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldw, 128, kGvRows,
+                 CU_TENSOR_MAP_SWIZZLE_128B))
+    return B200Q_ERR_CUDA;
+  auto kern = w8a16_gemv_kernel<MT, XF16>;
+  if (!set_smem(kern, kGvSmemBytes)) return B200Q_ERR_CUDA;
+  const dim3 grid(static_cast<unsigned>((N + kGvRows - 1) / kGvRows));
+  kern<<<grid, kGvThreads, kGvSmemBytes, st>>>(tw, static_cast<const uint16_t*>(x), ldx, int(M),
+                                               int(N), int(K), ep);
+  return finish_launch();
+}
+
+// W8A16 with <= 32 tokens takes the weight-streaming GEMV when the operands are
+// 16-byte aligned (the caller checks).  B200Q_W8A16_GEMV=0 turns it off (A/B runs).
+bool w8a16_gemv_selected(int64_t M) {
+  static const bool on = [] {
+    const char* e = getenv("B200Q_W8A16_GEMV");
+    return !(e && e[0] == '0');
+  }();
+  return on && M <= 32;
 }
 
 // Sync words of a fused-prologue launch: 16-byte aligned, large enough for M rows.
@@ -605,6 +630,7 @@ size_t b200q_w8a16_workspace_size(int64_t M, int64_t N, int64_t K) {
   const DeviceInfo* d = current_device();
   const int sms = d ? d->num_sms : 148;
   if (M <= 0 || N <= 0 || K <= 0) return 0;
+  if (w8a16_gemv_selected(M)) return 0;
   const W16Plan p = w8a16_plan(sms, M, N, K);
   if (p.splits <= 1) return 0;
   return ((p.partial_bytes + 255) & ~size_t(255)) + p.counter_bytes;
@@ -638,6 +664,13 @@ int b200q_w8a16_linear(const void* x, int x_dtype, int64_t ldx, const uint8_t* w
     else
       w8a16_simt_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(x), ldx, w, ldw, int(M), int(N), int(K), ep);
     return finish_launch();
+  }
+  if (w8a16_gemv_selected(M)) {
+    if (M <= 16)
+      return x_dtype == B200Q_F16 ? launch_w8a16_gemv<1, true>(x, ldx, w, ldw, M, N, K, ep, st)
+                                  : launch_w8a16_gemv<1, false>(x, ldx, w, ldw, M, N, K, ep, st);
+    return x_dtype == B200Q_F16 ? launch_w8a16_gemv<2, true>(x, ldx, w, ldw, M, N, K, ep, st)
+                                : launch_w8a16_gemv<2, false>(x, ldx, w, ldw, M, N, K, ep, st);
   }
   const W16Plan p = w8a16_plan(d->num_sms, M, N, K);
   W8A16Args args{};

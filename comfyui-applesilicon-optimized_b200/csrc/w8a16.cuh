@@ -360,21 +360,21 @@ __global__ void __launch_bounds__(kW16Threads, 1)
 //   warps 4..11 converters: warp w owns TMEM lane quarter w % 4 (the rows it may
 //            access) and half of the block's K; one thread per weight row
 //   warp 1   MMA: 8 x kind::f16 (bf16 x bf16 -> fp32), K=16 each, A from TMEM,
-//            rotated over kNacc independent accumulators: with N = 16..32 tokens an
-//            MMA is tiny and a single accumulator serializes them on latency
-//            (measured ~80 ns each); the epilogue sums the accumulators in order
+//            into one accumulator (back-to-back 128 x 16 x 16 MMAs on one
+//            accumulator run at the tensor pipe's ~27 ns each, measured)
 //   warps 12..15 epilogue (split-K protocol as in w8a16_tc_kernel)
 constexpr int kWsBK = 128;
 constexpr int kWsThreads = 512;
 constexpr int kWsConv = 256;
-constexpr int kWsABufs = 4;
-constexpr int kWsACols = kWsBK / 2;  // 128 bf16 per row = 64 32-bit columns
+constexpr int kWsSB = 2 * kWsBK;    // K per converter -> MMA handoff ("step": two blocks)
+constexpr int kWsABufs = 3;          // TMEM A buffers, one step each
+constexpr int kWsACols = kWsSB / 2;  // 256 bf16 per row = 128 32-bit columns
 
 template <int BT>
 struct W8A16StreamLayout {
   static constexpr int kRawSlot = kW16BM * kWsBK;        // 16 KB e4m3
-  static constexpr int kXSlot = BT * kWsBK * 2;          // bf16 activations (two atoms)
-  static constexpr int kXSlots = BT <= 16 ? 6 : BT <= 32 ? 5 : 4;
+  static constexpr int kXSlot = BT * kWsSB * 2;          // bf16 activations of one step (four atoms)
+  static constexpr int kXSlots = BT <= 16 ? 4 : BT <= 32 ? 3 : 2;
   static constexpr int kFree = 204 * 1024 - kXSlots * kXSlot;
   static constexpr int kRawSlots = kFree / kRawSlot > 10 ? 10 : kFree / kRawSlot;
   static constexpr int kXOff = 0;
@@ -383,9 +383,9 @@ struct W8A16StreamLayout {
   // wfull/wempty[RS], xfull/xempty[RX], afull/aempty[4], acc_full/acc_empty[2], slot, abort, last
   static constexpr int kBarBytes = (2 * kRawSlots + 2 * kXSlots + 2 * kWsABufs + 4) * 8 + 16;
   static constexpr int kSmemBytes = kBarOff + kBarBytes + 1024;
-  static constexpr int kNacc = BT <= 16 ? 4 : BT <= 32 ? 2 : 1;
+  static constexpr int kNacc = 1;
   static constexpr uint32_t kAccCols = 2 * kNacc * BT;
-  static constexpr uint32_t kTmemCols = 512;  // accumulators + 4 x 64 A columns
+  static constexpr uint32_t kTmemCols = 512;  // accumulators + 3 x 128 A columns
 };
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
@@ -511,12 +511,13 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         int nt, tt, sp;
         w16_unit_coords(u, S, num_t, nt, tt, sp);
         const int kb0 = sp * num_kb / S, kb1 = (sp + 1) * num_kb / S;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int kb = kb0; kb < kb1; kb += 2) {
+          const int nblk = min(2, kb1 - kb);  // 128-K blocks in this step
           if (!mbar_wait(&xempty[xs], xph ^ 1u, abort_flag)) { ok = false; break; }
-          mbar_arrive_expect_tx(&xfull[xs], L::kXSlot);
+          mbar_arrive_expect_tx(&xfull[xs], static_cast<uint32_t>(nblk) * (L::kXSlot / 2));
           uint8_t* dst = sX + xs * L::kXSlot;
-          tma_load_2d(&tmX, &xfull[xs], dst, kb * kWsBK, tt * BT);
-          tma_load_2d(&tmX, &xfull[xs], dst + L::kXSlot / 2, kb * kWsBK + 64, tt * BT);
+          for (int at = 0; at < 2 * nblk; ++at)  // 64-K swizzle atoms of BT rows
+            tma_load_2d(&tmX, &xfull[xs], dst + at * (L::kXSlot / 4), kb * kWsBK + at * 64, tt * BT);
           if (++xs == RX) { xs = 0; xph ^= 1u; }
         }
       }
@@ -540,19 +541,20 @@ __global__ void __launch_bounds__(kWsThreads, 1)
         if (!mbar_wait(&acc_empty[buf], acc_phase ^ 1u, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + buf * L::kNacc * BT;
-        int mi = 0;  // MMA index within the unit (selects the accumulator)
-        for (int kb = kb0; kb < kb1; ++kb) {
+        uint32_t acc = 0u;  // 0 for the unit's first MMA (overwrite), then accumulate
+        for (int kb = kb0; kb < kb1; kb += 2) {
+          const int nblk = min(2, kb1 - kb);
           if (!mbar_wait(&afull[ab], aph, abort_flag)) { ok = false; break; }
           if (!mbar_wait(&xfull[xs], xph, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_tmem = tmem_a0 + ab * kWsACols;
+          for (int atom = 0; atom < 2 * nblk; ++atom) {
+            const uint64_t bdesc = make_sw128_desc(smem_u32(sX + xs * L::kXSlot + atom * (L::kXSlot / 4)));
 #pragma unroll
-          for (int atom = 0; atom < 2; ++atom) {
-            const uint64_t bdesc = make_sw128_desc(smem_u32(sX + xs * L::kXSlot + atom * (L::kXSlot / 2)));
-#pragma unroll
-            for (int k = 0; k < 4; ++k, ++mi)  // K=16 per MMA = 8 TMEM columns of A, +32 B of B
-              umma_ts_f16(d_tmem + (mi % L::kNacc) * BT, a_tmem + (atom * 4 + k) * 8, bdesc + 2 * k,
-                          kIdesc, mi >= L::kNacc ? 1u : 0u);
+            for (int k = 0; k < 4; ++k) {  // K=16 per MMA = 8 TMEM columns of A, +32 B of B
+              umma_ts_f16(d_tmem, a_tmem + (atom * 4 + k) * 8, bdesc + 2 * k, kIdesc, acc);
+              acc = 1u;
+            }
           }
           umma_commit(&aempty[ab]);
           umma_commit(&xempty[xs]);
@@ -577,36 +579,40 @@ __global__ void __launch_bounds__(kWsThreads, 1)
       int nt, tt, sp;
       w16_unit_coords(u, S, num_t, nt, tt, sp);
       const int kb0 = sp * num_kb / S, kb1 = (sp + 1) * num_kb / S;
-      for (int kb = kb0; kb < kb1; ++kb) {
-        if (!mbar_wait_warp(&wfull[rs], rph, abort_flag)) { ok = false; break; }
+      for (int kb = kb0; kb < kb1; kb += 2) {
+        const int nblk = min(2, kb1 - kb);
         if (!mbar_wait_warp(&aempty[ab], aph ^ 1u, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        // Row r's 64 bytes: 16-byte chunks c = half*4 .. half*4+3, stored at chunk
-        // position c ^ (r & 7) by the 128-byte TMA swizzle.
-        const uint8_t* row = sW + rs * L::kRawSlot + r * kWsBK;
-        uint32_t v[32];
+        for (int b = 0; b < nblk; ++b) {
+          if (!mbar_wait_warp(&wfull[rs], rph, abort_flag)) { ok = false; break; }
+          // Row r's 64 bytes: 16-byte chunks c = half*4 .. half*4+3, stored at chunk
+          // position c ^ (r & 7) by the 128-byte TMA swizzle.
+          const uint8_t* row = sW + rs * L::kRawSlot + r * kWsBK;
+          uint32_t v[32];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int c = half * 4 + j;
-          const uint4 w = *reinterpret_cast<const uint4*>(row + ((c ^ (r & 7)) << 4));
-          const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
+          for (int j = 0; j < 4; ++j) {
+            const int c = half * 4 + j;
+            const uint4 w = *reinterpret_cast<const uint4*>(row + ((c ^ (r & 7)) << 4));
+            const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            if constexpr (X_F16) {
-              v[j * 8 + 2 * k] = e4m3x2_to_f16x2(static_cast<uint16_t>(wd[k] & 0xFFFFu));
-              v[j * 8 + 2 * k + 1] = e4m3x2_to_f16x2(static_cast<uint16_t>(wd[k] >> 16));
-            } else {
-              v[j * 8 + 2 * k] = e4m3x2_to_bf16x2(static_cast<uint16_t>(wd[k] & 0xFFFFu));
-              v[j * 8 + 2 * k + 1] = e4m3x2_to_bf16x2(static_cast<uint16_t>(wd[k] >> 16));
+            for (int k = 0; k < 4; ++k) {
+              if constexpr (X_F16) {
+                v[j * 8 + 2 * k] = e4m3x2_to_f16x2(static_cast<uint16_t>(wd[k] & 0xFFFFu));
+                v[j * 8 + 2 * k + 1] = e4m3x2_to_f16x2(static_cast<uint16_t>(wd[k] >> 16));
+              } else {
+                v[j * 8 + 2 * k] = e4m3x2_to_bf16x2(static_cast<uint16_t>(wd[k] & 0xFFFFu));
+                v[j * 8 + 2 * k + 1] = e4m3x2_to_bf16x2(static_cast<uint16_t>(wd[k] >> 16));
+              }
             }
           }
+          tmem_st32(tmem_a0 + lane_off + ab * kWsACols + b * (kWsBK / 2) + half * 32, v);
+          mbar_arrive(&wempty[rs]);  // the raw slot's bytes are in registers / in flight to TMEM
+          if (++rs == RS) { rs = 0; rph ^= 1u; }
         }
-        tmem_st32(tmem_a0 + lane_off + ab * kWsACols + half * 32, v);
+        if (!ok) break;
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(&wempty[rs]);
         mbar_arrive(&afull[ab]);
-        if (++rs == RS) { rs = 0; rph ^= 1u; }
         if (++ab == AB) { ab = 0; aph ^= 1u; }
       }
     }
@@ -685,6 +691,214 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 2) tmem_dealloc(tmem_base, L::kTmemCols);
+}
+
+// ---------------------------------------------------------------------------
+// Weight-streaming GEMV for M <= 32 tokens: the HBM-bound regime, where every
+// SM must pull its share of the FP8 weight (~44 GB/s per SM on B200) and the
+// arithmetic is tiny.  A 128-row tcgen05 tile fed by one issuing thread cannot
+// keep that pace at N = 16 tokens (a 2 KB weight step per MMA plus its
+// barrier hand-offs, measured ~25 GB/s per SM), so here every warp converts
+// e4m3 -> bf16/fp16 in registers and multiplies with warp-level m16n8k16 MMAs
+// (fp32 accumulation), while TMA keeps the weight stream in flight.
+//
+// CTA = 8 warps on 32 weight rows (4 groups of 8), three CTAs per SM.  One
+// thread streams the rows' K in stages of 512 bytes (4 TMA boxes of 32 rows x
+// 128 B, 128-byte swizzle) through a kGvStages-deep shared-memory ring; in each
+// stage warp w takes K [64w, 64w + 64).  The warps' partial sums are reduced
+// through shared memory in warp order (deterministic).  Within a warp's 64-K
+// slice, lane (g = lane/4, q = lane%4) reads W[row g of a group][16q .. 16q+15];
+// byte 4t+j of that vector feeds MMA t (t = 0..3) at logical k = 2q + (j & 1)
+// + 8 (j >> 1).  The activation operand uses the same per-lane permutation of K
+// (X[m][16q + 4t + j], read from global memory through L1, one stage ahead), so
+// the dot product is unchanged and no shuffles are needed.
+// Measured alternatives that were slower on B200 (C2, 12288 x 3072): one
+// persistent CTA per SM with a 12-16 stage ring (24.6 us per call vs 18.4 us),
+// the same with 16 warps (22.5 us); the 3-CTA form keeps more warps resident to
+// hide the activation loads and the per-warp MMA chain.
+constexpr int kGvRows = 32;
+constexpr int kGvWarps = 8;
+constexpr int kGvThreads = kGvWarps * 32;
+constexpr int kGvStageK = 64 * kGvWarps;              // 512 K bytes per stage
+constexpr int kGvStageBytes = kGvRows * kGvStageK;    // 16 KB
+constexpr int kGvStages = 3;
+constexpr int kGvSmemBytes = kGvStages * kGvStageBytes + 2 * kGvStages * 8 + 16 + 1024;
+
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                          uint32_t b1, bool f16) {
+  if (f16) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+
+// MT = 16-token tiles (1: M <= 16, 2: M <= 32).  Requires K % 16 == 0, ldx % 8 == 0
+// and a 16-byte-aligned X (the host checks; W goes through the tensor map).
+template <int MT, bool X_F16>
+__global__ void __launch_bounds__(kGvThreads, MT == 1 ? 3 : 2)
+    w8a16_gemv_kernel(const __grid_constant__ CUtensorMap tmW, const uint16_t* __restrict__ X,
+                      int64_t ldx, int M, int N, int K, EpiArgs ep) {
+  __shared__ float red[kGvWarps][MT * 16][kGvRows + 1];
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + kGvStages * kGvStageBytes);
+  uint64_t* empty = full + kGvStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kGvStages);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int n0 = blockIdx.x * kGvRows;
+  const int nst = (K + kGvStageK - 1) / kGvStageK;
+
+  if (threadIdx.x == 0) {
+    for (int s2 = 0; s2 < kGvStages; ++s2) {
+      mbar_init(&full[s2], 1);
+      mbar_init(&empty[s2], kGvWarps);
+    }
+    *abort_flag = 0;
+    fence_mbarrier_init();
+    tma_prefetch_desc(&tmW);
+  }
+  __syncthreads();
+  auto issue = [&](int st) {  // thread 0: stage st into slot st % kGvStages
+    const int slot = st % kGvStages;
+    uint8_t* dst = ring + slot * kGvStageBytes;
+    mbar_arrive_expect_tx(&full[slot], kGvStageBytes);
+#pragma unroll
+    for (int b = 0; b < kGvStageK / 128; ++b)
+      tma_load_2d(&tmW, &full[slot], dst + b * (kGvRows * 128), st * kGvStageK + b * 128, n0);
+  };
+  if (threadIdx.x == 0)
+    for (int st = 0; st < kGvStages && st < nst; ++st) issue(st);
+
+  float acc[MT][4][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int gr = 0; gr < 4; ++gr)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[mt][gr][i] = 0.0f;
+  // Activation rows of this lane: tokens g + 8h + 16mt; rows past M are zero.
+  const uint16_t* xrow[MT][2];
+  bool xok[MT][2];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int m = 16 * mt + 8 * h + g;
+      xok[mt][h] = m < M;
+      xrow[mt][h] = X + static_cast<int64_t>(m < M ? m : 0) * ldx + 16 * q;
+    }
+  // Activation fragments are loaded one stage ahead, so their L2 round trip
+  // overlaps the wait for the stage's weights.
+  uint4 xa[MT][2][2], xn[MT][2][2];
+  auto load_x = [&](int st, uint4 (&dst)[MT][2][2]) {
+    const int k0 = st * kGvStageK + 64 * warp;
+    const bool kin = st < nst && k0 + 16 * q < K;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int p = 0; p < 2; ++p)
+          dst[mt][h][p] = (xok[mt][h] && kin)
+                              ? __ldg(reinterpret_cast<const uint4*>(xrow[mt][h] + k0) + p)
+                              : make_uint4(0u, 0u, 0u, 0u);
+  };
+  load_x(0, xn);
+  // This warp's 16-byte chunk of each row inside the stage's box: box warp/2,
+  // chunk (warp & 1) * 4 + q, stored at chunk ^ (row & 7) by the 128-byte swizzle.
+  const int box = warp >> 1;
+  const int chunk = (warp & 1) * 4 + q;
+
+  bool ok = true;
+  for (int st = 0; st < nst && ok; ++st) {
+    const int slot = st % kGvStages;
+    const uint32_t ph = (st / kGvStages) & 1u;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int p = 0; p < 2; ++p) xa[mt][h][p] = xn[mt][h][p];
+    load_x(st + 1, xn);
+    if (!mbar_wait_warp(&full[slot], ph, abort_flag)) { ok = false; break; }
+    const int k0 = st * kGvStageK + 64 * warp;
+    if (k0 < K) {
+      const uint8_t* sb = ring + slot * kGvStageBytes + box * (kGvRows * 128);
+      uint4 wv[4];
+#pragma unroll
+      for (int gr = 0; gr < 4; ++gr) {
+        const int r = 8 * gr + g;
+        wv[gr] = *reinterpret_cast<const uint4*>(sb + r * 128 + ((chunk ^ (r & 7)) << 4));
+      }
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        uint32_t a[MT][4];
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          const uint32_t* r0 = reinterpret_cast<const uint32_t*>(&xa[mt][0][t >> 1]);
+          const uint32_t* r1 = reinterpret_cast<const uint32_t*>(&xa[mt][1][t >> 1]);
+          a[mt][0] = r0[(t & 1) * 2];
+          a[mt][1] = r1[(t & 1) * 2];
+          a[mt][2] = r0[(t & 1) * 2 + 1];
+          a[mt][3] = r1[(t & 1) * 2 + 1];
+        }
+#pragma unroll
+        for (int gr = 0; gr < 4; ++gr) {
+          const uint32_t wd = (t == 0) ? wv[gr].x : (t == 1) ? wv[gr].y : (t == 2) ? wv[gr].z : wv[gr].w;
+          const uint16_t lo = static_cast<uint16_t>(wd & 0xFFFFu), hi = static_cast<uint16_t>(wd >> 16);
+          const uint32_t b0 = X_F16 ? e4m3x2_to_f16x2(lo) : e4m3x2_to_bf16x2(lo);
+          const uint32_t b1 = X_F16 ? e4m3x2_to_f16x2(hi) : e4m3x2_to_bf16x2(hi);
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) mma_16816(acc[mt][gr], a[mt], b0, b1, X_F16);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+    if (threadIdx.x == 0 && st + kGvStages < nst) {
+      // Refill this slot once every warp has released it.
+      if (!mbar_wait(&empty[slot], ph, abort_flag)) { ok = false; break; }
+      issue(st + kGvStages);
+    }
+  }
+  if (!ok && threadIdx.x == 0) {
+    // Let this CTA's in-flight stages land before its shared memory is released.
+    for (int s2 = 0; s2 < kGvStages; ++s2) mbar_wait_drain(&full[s2], 0);
+  }
+
+  // D fragment: acc[mt][gr][i] is token 16mt + g + 8(i >> 1), row 8gr + 2q + (i & 1).
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int gr = 0; gr < 4; ++gr)
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        red[warp][16 * mt + g + 8 * (i >> 1)][8 * gr + 2 * q + (i & 1)] = acc[mt][gr][i];
+  __syncthreads();
+  if (*abort_flag) return;
+  const float xs = ep.extra_scale ? __ldg(ep.extra_scale) : 1.0f;
+  for (int e = threadIdx.x; e < MT * 16 * kGvRows; e += kGvThreads) {
+    const int tok = e / kGvRows, r = e % kGvRows;
+    const int n = n0 + r;
+    if (tok >= M || n >= N) continue;
+    float v = red[0][tok][r];
+#pragma unroll
+    for (int w2 = 1; w2 < kGvWarps; ++w2) v = __fadd_rn(v, red[w2][tok][r]);
+    if (ep.extra_scale) v = __fmul_rn(v, xs);
+    if (ep.bias_dtype != kBiasNone) v = __fadd_rn(v, load_bias(ep.bias, ep.bias_dtype, n));
+    store_out(ep, tok, n, apply_act(v, ep.act));
+  }
 }
 
 // SIMT fallback (K % 16 != 0 or unaligned operands): one thread per output
