@@ -240,6 +240,10 @@ struct W16Plan {
 
 W16Plan w8a16_plan(int num_sms, int64_t M, int64_t N, int64_t K) {
   W16Plan p{};
+  // Token tiles up to 64 run the TMEM-operand streaming kernel; larger M runs the
+  // shared-memory-operand kernel (128- or 256-token tiles).  A 128-token
+  // streaming tile was measured no faster at M = 128..256 (its X stream and
+  // the single MMA issuer bind first).
   p.bt = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
   const int64_t num_n = (N + kW16BM - 1) / kW16BM;
   const int64_t num_t = (M + p.bt - 1) / p.bt;

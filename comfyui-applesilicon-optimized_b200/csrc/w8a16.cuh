@@ -367,7 +367,6 @@ constexpr int kWsBK = 128;
 constexpr int kWsThreads = 512;
 constexpr int kWsConv = 256;
 constexpr int kWsSB = 2 * kWsBK;    // K per converter -> MMA handoff ("step": two blocks)
-constexpr int kWsABufs = 3;          // TMEM A buffers, one step each
 constexpr int kWsACols = kWsSB / 2;  // 256 bf16 per row = 128 32-bit columns
 
 template <int BT>
@@ -381,11 +380,14 @@ struct W8A16StreamLayout {
   static constexpr int kRawOff = kXSlots * kXSlot;
   static constexpr int kBarOff = kRawOff + kRawSlots * kRawSlot;
   // wfull/wempty[RS], xfull/xempty[RX], afull/aempty[4], acc_full/acc_empty[2], slot, abort, last
-  static constexpr int kBarBytes = (2 * kRawSlots + 2 * kXSlots + 2 * kWsABufs + 4) * 8 + 16;
+  // TMEM: double-buffered accumulators (2 x BT columns), then as many A buffers
+  // of one step (128 columns) as fit in the 512 columns.
+  static constexpr int kABufs = (512 - 2 * BT) / 128 > 3 ? 3 : (512 - 2 * BT) / 128;
+  static constexpr int kBarBytes = (2 * kRawSlots + 2 * kXSlots + 2 * kABufs + 4) * 8 + 16;
   static constexpr int kSmemBytes = kBarOff + kBarBytes + 1024;
   static constexpr int kNacc = 1;
   static constexpr uint32_t kAccCols = 2 * kNacc * BT;
-  static constexpr uint32_t kTmemCols = 512;  // accumulators + 3 x 128 A columns
+  static constexpr uint32_t kTmemCols = 512;  // accumulators + kABufs x 128 A columns
 };
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
@@ -421,7 +423,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
   using L = W8A16StreamLayout<BT>;
   constexpr int RS = L::kRawSlots;
   constexpr int RX = L::kXSlots;
-  constexpr int AB = kWsABufs;
+  constexpr int AB = L::kABufs;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));

@@ -50,7 +50,7 @@ def _call_noalloc(L, x, w, ws, bias, out):
 
 def test_noalloc_matches_workspace_entry_point_twice(native, abi):
     g = torch.Generator().manual_seed(31)
-    M, K, N = 100, 12288, 3072  # a split-K plan: the call needs scratch
+    M, K, N = 300, 12288, 3072  # a split-K plan (256-token tiles): the call needs scratch
     assert 0 < abi.b200q_w8a16_workspace_size(M, N, K) <= B200Q_NOALLOC_SCRATCH_BYTES
     x = torch.randn(M, K, generator=g).to(torch.bfloat16).cuda()
     w = (torch.randn(N, K, generator=g) * 100).clamp(-448, 448).to(torch.float8_e4m3fn).cuda()
@@ -77,7 +77,7 @@ def test_noalloc_matches_workspace_entry_point_twice(native, abi):
 
 
 def test_noalloc_rejects_shapes_beyond_the_static_scratch(native, abi):
-    M, K, N = 128, 49152, 12288
+    M, K, N = 300, 49152, 12288
     need = abi.b200q_w8a16_workspace_size(M, N, K)
     assert need > B200Q_NOALLOC_SCRATCH_BYTES
     x = torch.empty(M, K, dtype=torch.bfloat16, device="cuda")
