@@ -11,6 +11,7 @@ functions (pybind in the reference: _patches/int8_ext/int8_gemm.mm:2626-2715,
 _patches/fp8_ext/fp8_matmul2d.mm:355-360, _patches/fp8s_ext/w8a16_gemm.mm:316-329):
 
   quant_rowwise_i8(x)                       -> (q int8 [M,K], scale f32 [M,1])
+  quant_rowwise_i8_convrot(x, groupsize)    -> the same for the convrot-rotated rows
   int_mm(a [M,K] i8, b [K,N] i8)            -> int32 [M,N]      (torch._int_mm contract)
   i8_matmul_nt(a [M,K], w [N,K])            -> int32 [M,N]      (i8_matmul2d_nt)
   i8_matmul_nt_fused(a, w, row_scale, bias) -> bf16 [M,N]       (i8_matmul2d_nt_fused)
@@ -52,6 +53,8 @@ _SIGNATURES = {
     "b200q_launch_count": ([], ctypes.c_uint64),
     "b200q_get_device_status": ([_vp, _int], _int),
     "b200q_quant_rowwise_i8": ([_vp, _int, _i64, _i64, _i64, _vp, _i64, _vp, _vp], _int),
+    "b200q_quant_rowwise_i8_convrot": ([_vp, _int, _i64, _i64, _i64, _int, _vp, _i64, _vp, _vp],
+                                       _int),
     "b200q_i8_matmul_nt": ([_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp], _int),
     "b200q_i8_matmul_nt_dequant": ([_vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _int, _vp, _int,
                                     _i64, _i64, _i64, _i64, _vp], _int),
@@ -149,6 +152,24 @@ def quant_rowwise_i8(x):
     s = torch.empty((M, 1), dtype=torch.float32, device=x.device)
     _check(lib().b200q_quant_rowwise_i8(_p(x), _DT[x.dtype], M, K, x.stride(0), _p(q), K, _p(s),
                                         _stream(x)))
+    return q, s
+
+
+CONVROT_MAX_K = 28672  # B200Q_CONVROT_MAX_K
+
+
+def quant_rowwise_i8_convrot(x, groupsize=256):
+    """Convrot (256-wide Hadamard) rotation fused into the per-token INT8 quant:
+    x [M,K] bf16/f16 -> (q int8 [M,K], scale f32 [M,1]) of the rotated rows."""
+    _require_cuda(x)
+    x = _rows_2d(x, "x")
+    if x.dtype not in (torch.bfloat16, torch.float16):
+        raise RuntimeError(f"{TAG} quant_rowwise_i8_convrot expects bf16/f16, got {x.dtype}")
+    M, K = x.shape
+    q = torch.empty((M, K), dtype=torch.int8, device=x.device)
+    s = torch.empty((M, 1), dtype=torch.float32, device=x.device)
+    _check(lib().b200q_quant_rowwise_i8_convrot(_p(x), _DT[x.dtype], M, K, x.stride(0), int(groupsize),
+                                                _p(q), K, _p(s), _stream(x)))
     return q, s
 
 
@@ -421,6 +442,7 @@ def _register_ops():
         return
     L = torch.library.Library("b200q", "DEF")
     L.define("quant_rowwise_i8(Tensor x) -> (Tensor, Tensor)")
+    L.define("quant_rowwise_i8_convrot(Tensor x, int groupsize=256) -> (Tensor, Tensor)")
     L.define("int_mm(Tensor a, Tensor b) -> Tensor")
     L.define("i8_matmul_nt(Tensor a, Tensor w) -> Tensor")
     L.define("i8_matmul_nt_fused(Tensor a, Tensor w, Tensor row_scale, Tensor? bias=None) -> Tensor")
@@ -440,6 +462,7 @@ def _register_ops():
 
     impls = {
         "quant_rowwise_i8": quant_rowwise_i8,
+        "quant_rowwise_i8_convrot": quant_rowwise_i8_convrot,
         "int_mm": int_mm,
         "i8_matmul_nt": i8_matmul_nt,
         "i8_matmul_nt_fused": i8_matmul_nt_fused,
@@ -462,6 +485,7 @@ def _register_ops():
 
     fakes = {
         "quant_rowwise_i8": fake_quant,
+        "quant_rowwise_i8_convrot": lambda x, groupsize=256: fake_quant(x),
         "int_mm": lambda a, b: a.new_empty((a.shape[0], b.shape[1]), dtype=torch.int32),
         "i8_matmul_nt": lambda a, w: a.new_empty((a.shape[0], w.shape[0]), dtype=torch.int32),
         "i8_matmul_nt_fused": lambda a, w, rs, bias=None: a.new_empty((a.shape[0], w.shape[0]),

@@ -74,6 +74,16 @@ def _int8_linear_bounded(x, weight, weight_scale, bias, out_dtype, convrot, conv
     return output.reshape(*x.shape[:-1], weight.shape[0])
 
 
+def _fused_convrot_ok(groupsize, K):
+    """The fused rotate+quant kernel covers groupsize 256 (the only size the
+    reference's fused kernels handle).  B200Q_CONVROT_FUSED=0 keeps comfy's eager
+    bf16 Hadamard matmul instead (bit-identical to the eager path; the fused
+    kernel may flip a rotated value's last bf16 ulp on rare ties)."""
+    from . import _native
+    return (os.environ.get("B200Q_CONVROT_FUSED", "1") != "0" and groupsize == 256
+            and K % 256 == 0 and K <= _native.CONVROT_MAX_K)
+
+
 def _quant_cached(x, convrot, convrot_groupsize):
     """Rotate (convrot) + rowwise quant, reusing the previous result for the same
     live tensor object and settings (int8_linear_kernel_mps.py:97-140)."""
@@ -81,13 +91,17 @@ def _quant_cached(x, convrot, convrot_groupsize):
     c = _act_cache
     if c is not None and c[0]() is x and c[1] == convrot and c[2] == convrot_groupsize:
         return c[3], c[4]
-    xr = x
-    if convrot:
-        from comfy_kitchen.tensor.int8_utils import _build_hadamard, _rotate_activation
-        h = _build_hadamard(convrot_groupsize, device=x.device, dtype=x.dtype)
-        xr = _rotate_activation(xr, h, convrot_groupsize)
-    x_2d = xr.reshape(-1, xr.shape[-1])
-    x_8, x_scale = _kernel.i8_quant_rowwise(x_2d)
+    K = x.shape[-1]
+    if convrot and _fused_convrot_ok(convrot_groupsize, K):
+        # One pass: Hadamard rotation + rowwise quant (int8_gemm.mm:1409-1505 numerics).
+        x_8, x_scale = torch.ops.b200q.quant_rowwise_i8_convrot(x.reshape(-1, K), convrot_groupsize)
+    else:
+        xr = x
+        if convrot:
+            from comfy_kitchen.tensor.int8_utils import _build_hadamard, _rotate_activation
+            h = _build_hadamard(convrot_groupsize, device=x.device, dtype=x.dtype)
+            xr = _rotate_activation(xr, h, convrot_groupsize)
+        x_8, x_scale = _kernel.i8_quant_rowwise(xr.reshape(-1, K))
     if os.environ.get("ASFP8_INT8_ACT_CACHE", "1") != "0":
         try:
             _act_cache = (weakref.ref(x), convrot, convrot_groupsize, x_8, x_scale)

@@ -436,6 +436,32 @@ int b200q_quant_rowwise_i8(const void* x, int x_dtype, int64_t M, int64_t K, int
   return finish_launch();
 }
 
+int b200q_quant_rowwise_i8_convrot(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
+                                   int groupsize, int8_t* q, int64_t ldq, float* scales,
+                                   void* stream) {
+  if (!x || !q || !scales || M < 0 || K <= 0 || ldx < K || ldq < K || M >= (int64_t(1) << 31) ||
+      (x_dtype != B200Q_BF16 && x_dtype != B200Q_F16))
+    return B200Q_ERR_INVALID;
+  if (groupsize != kRotGroup || K % kRotGroup != 0 || K > B200Q_CONVROT_MAX_K)
+    return B200Q_ERR_UNSUPPORTED;
+  const DeviceInfo* d = current_device();
+  if (!d) return B200Q_ERR_UNSUPPORTED;
+  if (M == 0) return B200Q_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int smem = static_cast<int>(2 * K * sizeof(float));
+  const int grid = static_cast<int>(M < int64_t(d->num_sms) * 8 ? M : int64_t(d->num_sms) * 8);
+  if (x_dtype == B200Q_BF16) {
+    auto kern = quant_rowwise_i8_rot_kernel<__nv_bfloat16>;
+    if (!set_smem(kern, smem)) return B200Q_ERR_CUDA;
+    kern<<<grid, kQuantThreads, smem, st>>>(static_cast<const __nv_bfloat16*>(x), ldx, q, ldq, scales, int(M), int(K));
+  } else {
+    auto kern = quant_rowwise_i8_rot_kernel<__half>;
+    if (!set_smem(kern, smem)) return B200Q_ERR_CUDA;
+    kern<<<grid, kQuantThreads, smem, st>>>(static_cast<const __half*>(x), ldx, q, ldq, scales, int(M), int(K));
+  }
+  return finish_launch();
+}
+
 int b200q_i8_matmul_nt(const int8_t* a, int64_t lda, const int8_t* w, int64_t ldw, int32_t* c,
                        int64_t ldc, int64_t M, int64_t N, int64_t K, void* stream) {
   if (!a || !w || !c || !valid_dims(M, N, K) || K == 0 || lda < K || ldw < K || ldc < N)

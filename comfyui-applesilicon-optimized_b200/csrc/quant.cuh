@@ -236,6 +236,100 @@ __global__ void __launch_bounds__(kQuantThreads)
   }
 }
 
+// ------------------------------------------------------------ convrot + INT8
+// Convrot rotation fused into the per-token quant (the _quant_cached path with
+// convrot, _patches/int8_linear_kernel_mps.py:97-140; the reference's fused
+// form is i8_merge_rot_quant, _patches/int8_ext/int8_gemm.mm:1409-1505).
+// Each 256-wide group of a row is multiplied by the regular Hadamard
+// H = H4 (x) H4 (x) H4 (x) H4 / 16, H4 = [[1,1,1,-1],[1,1,-1,1],[1,-1,1,1],
+// [-1,1,1,1]], as four radix-4 butterfly stages in fp32 (strides 1, 4, 16, 64,
+// each output the row of H4 selected by its base-4 digit, evaluated in the
+// reference's term order), then * 2^-4 (exact) and one rounding to the input
+// dtype.  The rotated row stays in shared memory for the absmax and the
+// quantize pass, which follow quant_rowwise_i8 exactly.  All groups of a row
+// advance through a stage together (ping-pong buffers of K floats), so a row
+// costs four block barriers whatever its width.
+constexpr int kRotGroup = 256;
+
+template <typename T>
+__global__ void __launch_bounds__(kQuantThreads)
+    quant_rowwise_i8_rot_kernel(const T* __restrict__ x, int64_t ldx, int8_t* __restrict__ q,
+                                int64_t ldq, float* __restrict__ scales, int M, int K) {
+  extern __shared__ float rot_smem[];
+  float* bufa = rot_smem;
+  float* bufb = rot_smem + K;
+  __shared__ float red[kQuantThreads / 32];
+  __shared__ float bcast;
+  const int t = threadIdx.x;  // position inside every 256-wide group
+  const bool vec = (K % 8 == 0) && (ldx % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
+  for (int row = blockIdx.x; row < M; row += gridDim.x) {
+    const T* xr = x + static_cast<int64_t>(row) * ldx;
+    if (vec) {
+      for (int i = t; i < (K >> 3); i += kQuantThreads) {
+        const uint4 v = __ldcs(reinterpret_cast<const uint4*>(xr) + i);
+        const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) bufa[8 * i + j] = to_float<T>(e[j]);
+      }
+    } else {
+      for (int i = t; i < K; i += kQuantThreads) bufa[i] = to_float<T>(xr[i]);
+    }
+    __syncthreads();
+    float* src = bufa;
+    float* dst = bufb;
+#pragma unroll
+    for (int stride = 1; stride <= 64; stride *= 4) {
+      const int digit = (t / stride) & 3;
+      const int base = t - digit * stride;
+      for (int g0 = 0; g0 < K; g0 += kRotGroup) {
+        const float a0 = src[g0 + base];
+        const float a1 = src[g0 + base + stride];
+        const float a2 = src[g0 + base + 2 * stride];
+        const float a3 = src[g0 + base + 3 * stride];
+        float y;
+        if (digit == 0) y = __fsub_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3);
+        else if (digit == 1) y = __fadd_rn(__fsub_rn(__fadd_rn(a0, a1), a2), a3);
+        else if (digit == 2) y = __fadd_rn(__fadd_rn(__fsub_rn(a0, a1), a2), a3);
+        else y = __fadd_rn(__fadd_rn(__fsub_rn(a1, a0), a2), a3);
+        dst[g0 + t] = y;
+      }
+      __syncthreads();
+      float* tmp = src;
+      src = dst;
+      dst = tmp;
+    }
+    // src holds the unscaled rotation; scale by 2^-4 (exact), round to T once.
+    float amax = 0.0f;
+    for (int i = t; i < K; i += kQuantThreads) {
+      const float r = round_to<T>(src[i] * 0.0625f);
+      src[i] = r;
+      amax = fmaxf(amax, fabsf(r));
+    }
+    const float s_math = row_scale_from_absmax<T>(amax, red, &bcast, scales, row);
+    const float r_math = __frcp_rn(s_math);
+    int8_t* qr = q + static_cast<int64_t>(row) * ldq;
+    if (vec && (ldq % 8 == 0) && (reinterpret_cast<uintptr_t>(q) % 8 == 0)) {
+      for (int i = t; i < (K >> 3); i += kQuantThreads) {
+        float y[8];
+        uint32_t w[2] = {0u, 0u};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) y[j] = src[8 * i + j];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float d = __fmul_rn(y[j], r_math);
+          if (near_tie<T>(d)) d = __fdiv_rn(y[j], s_math);
+          d = fminf(fmaxf(rintf(round_to<T>(d)), -128.0f), 127.0f);
+          w[j >> 2] |= (static_cast<uint32_t>(static_cast<int>(d)) & 0xFFu) << (8 * (j & 3));
+        }
+        reinterpret_cast<uint2*>(qr)[i] = make_uint2(w[0], w[1]);
+      }
+    } else {
+      for (int i = t; i < K; i += kQuantThreads) qr[i] = static_cast<int8_t>(quant_code<T>(src[i], s_math));
+    }
+    __syncthreads();  // buffers and red/bcast are reused by the next row
+  }
+}
+
 // ------------------------------------------------------------ FP8 per-tensor
 // Two addressing modes, chosen per launch: contiguous tensors (ldx == K) are
 // walked as one flat array of 16-byte vectors; strided ones row by row (one

@@ -70,6 +70,21 @@ B200Q_API int b200q_get_device_status(unsigned int* status, int reset);
 B200Q_API int b200q_quant_rowwise_i8(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
                            int8_t* q, int64_t ldq, float* scales, void* stream);
 
+/* Convrot rotation fused into the per-token INT8 quant: each 256-wide group of a
+ * row is multiplied by comfy_kitchen's regular Hadamard (H4 (x) H4 (x) H4 (x) H4
+ * / 16), rounded once to x's dtype, then quantized exactly as
+ * b200q_quant_rowwise_i8.  Replaces the convrot branch of _quant_cached
+ * (_patches/int8_linear_kernel_mps.py:97-140: _build_hadamard + _rotate_activation
+ * + i8_quant_rowwise) and the rotation of i8_merge_rot_quant
+ * (_patches/int8_ext/int8_gemm.mm:1409-1505).  The fp32 butterfly order follows
+ * the latter, so like it the result can differ from the eager bf16 Hadamard
+ * matmul by a last-ulp rotation flip on rare ties.  groupsize must be 256 and
+ * K a multiple of it, K <= B200Q_CONVROT_MAX_K (B200Q_ERR_UNSUPPORTED otherwise). */
+#define B200Q_CONVROT_MAX_K 28672
+B200Q_API int b200q_quant_rowwise_i8_convrot(const void* x, int x_dtype, int64_t M, int64_t K,
+                                             int64_t ldx, int groupsize, int8_t* q, int64_t ldq,
+                                             float* scales, void* stream);
+
 /* Exact int8 x int8 -> int32 NT GEMM, C[M,N] = A[M,K] . W[N,K]^T.
  * Replaces i8_matmul2d_nt (_patches/int8_ext/int8_gemm.mm:1655) and the
  * torch._int_mm seam (_patches/int_mm_mps.py:90). */

@@ -11,7 +11,11 @@ against the reference's own Python code run in this container
 (``tests/golden/make_golden.py`` -> ``tests/golden/*.npz``).  The INT8 rowwise
 quant lives in comfy_kitchen (absent here); it is pinned through the
 reference's restatement (int8_gemm.mm:1337-1381) and the known-answer cases of
-its tests (zero and 1e-30 rows, corner codes, ragged K).
+its tests (zero and 1e-30 rows, corner codes, ragged K).  The convrot Hadamard
+is likewise comfy_kitchen's; it is restated from the reference's fused kernel
+(int8_gemm.mm:1417-1480) and checked for the properties that kernel relies on
+(orthonormal, symmetric, entries +-2^-4) -- parity unpinned against
+comfy_kitchen itself.
 
 Reference citations are paths inside luix93/ComfyUI-AppleSilicon-Optimized.
 """
@@ -78,6 +82,48 @@ def quantize_int8_rowwise(x):
     d = rnd((xf / s[:, None]).astype(np.float32))
     q = np.clip(np.rint(d), -128, 127).astype(np.int8)
     return torch.from_numpy(q), torch.from_numpy(scale.reshape(-1, 1))
+
+
+# ------------------------------------------------------------------ convrot
+def hadamard_convrot(groupsize=256):
+    """The convrot rotation matrix for groupsize 256, as the reference restates
+    comfy_kitchen's _build_hadamard (absent here) in its fused kernel
+    (_patches/int8_ext/int8_gemm.mm:1417-1480): the regular Hadamard
+    H = H4 (x) H4 (x) H4 (x) H4 with H4 = [[1,1,1,-1],[1,1,-1,1],[1,-1,1,1],
+    [-1,1,1,1]], scaled by 2^-4 (entries exactly +-1/16; symmetric; H @ H = I).
+    Element (i, j) is the product over the four base-4 digits of i and j of
+    H4[digit_i][digit_j]; the digit order is immaterial (each factor is the
+    same symmetric matrix)."""
+    if groupsize != 256:
+        raise ValueError("convrot groupsize 256 only (the reference's fused kernels)")
+    h4 = np.array([[1, 1, 1, -1], [1, 1, -1, 1], [1, -1, 1, 1], [-1, 1, 1, 1]], np.float64)
+    h = np.ones((1, 1))
+    for _ in range(4):
+        h = np.kron(h, h4)
+    return h / 16.0
+
+
+def rotate_convrot(x, groupsize=256):
+    """x [..., K] (K % 256 == 0) rotated group by group: x_g @ H, computed exactly
+    (float64: bf16/fp16 values times +-2^-4, 256-term sums) and rounded once to
+    x.dtype -- the value comfy's bf16 Hadamard matmul (_patches/
+    int8_linear_kernel_mps.py:119-121) and the reference's fused FWHT
+    (int8_gemm.mm:1479) both approximate, up to fp32 summation order."""
+    rnd, _ = _rounder(x.dtype)
+    shp = x.shape
+    xf = to_f32(x.reshape(-1, shp[-1])).astype(np.float64)
+    K = xf.shape[1]
+    if K % groupsize:
+        raise ValueError("K must be a multiple of the convrot groupsize")
+    h = hadamard_convrot(groupsize)
+    y = (xf.reshape(-1, K // groupsize, groupsize) @ h).reshape(-1, K)
+    return from_f32(rnd(y.astype(np.float32)), x.dtype).reshape(shp)
+
+
+def quantize_int8_rowwise_convrot(x, groupsize=256):
+    """Convrot rotation then per-token INT8 quant (_quant_cached,
+    _patches/int8_linear_kernel_mps.py:97-140)."""
+    return quantize_int8_rowwise(rotate_convrot(x, groupsize))
 
 
 def int_mm(a, b):
