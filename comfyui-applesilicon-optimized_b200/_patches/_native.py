@@ -16,6 +16,9 @@ _patches/fp8_ext/fp8_matmul2d.mm:355-360, _patches/fp8s_ext/w8a16_gemm.mm:316-32
   i8_matmul_nt(a [M,K], w [N,K])            -> int32 [M,N]      (i8_matmul2d_nt)
   i8_matmul_nt_fused(a, w, row_scale, bias) -> bf16 [M,N]       (i8_matmul2d_nt_fused)
   i8_matmul_nt_fused_cs(a, w, row_scale, col_scale, bias, out_dtype) (i8_matmul2d_nt_fused_cs)
+  i8_matmul_nt_fused_cs_qkv(a, w, rs, cs, bias, heads, head_dim, batch)
+                                            -> q, k, v in [B, H, S, D] (i8_matmul2d_nt_fused_cs_qkv)
+  rms_rope_partial_(q, k, freqs, qw, kw, eps) -> in-place RMSNorm + split-half RoPE
   i8_linear(x, w, w_scale, bias, out_dtype) -> quant + GEMM + dequant epilogue
                                                (B200Q_FUSED_PROLOGUE=1: quant inside the GEMM)
   fp8_quant_tensorwise(x)                   -> (q e4m3 [M,K], scale f32 [])
@@ -56,6 +59,10 @@ _SIGNATURES = {
     "b200q_quant_rowwise_i8_convrot": ([_vp, _int, _i64, _i64, _i64, _int, _vp, _i64, _vp, _vp],
                                        _int),
     "b200q_i8_matmul_nt": ([_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _vp], _int),
+    "b200q_i8_matmul_nt_dequant_qkv": ([_vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _vp, _vp,
+                                       _int, _i64, _i64, _i64, _i64, _i64, _i64, _vp], _int),
+    "b200q_rms_rope_partial": ([_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
+                               ctypes.c_float, _vp], _int),
     "b200q_i8_matmul_nt_dequant": ([_vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _int, _vp, _int,
                                     _i64, _i64, _i64, _i64, _vp], _int),
     "b200q_i8_linear": ([_vp, _int, _i64, _vp, _i64, _vp, _i64, _vp, _int, _vp, _int, _i64, _i64,
@@ -227,6 +234,51 @@ def i8_matmul_nt_fused_cs(a, w, row_scale, col_scale, bias=None, out_dtype=torch
                                             _p(col_scale), col_scale.numel(), _p(bias),
                                             ACTS[act], _p(out), code, N, M, N, K, _stream(a)))
     return out
+
+
+def i8_matmul_nt_fused_cs_qkv(a, w, row_scale, col_scale, bias=None, heads=1, head_dim=128,
+                              batch=1, out_dtype=torch.bfloat16):
+    """INT8 QKV projection straight into attention layout: returns q, k, v, each
+    [batch, heads, M // batch, head_dim] (i8_matmul2d_nt_fused_cs_qkv, batch 1)."""
+    _require_cuda(a, w, row_scale, col_scale, bias)
+    a, w = _rows_2d(a, "a"), _rows_2d(w, "w")
+    M, K = a.shape
+    N = w.shape[0]
+    if w.shape[1] != K or N != 3 * heads * head_dim or M % batch:
+        raise RuntimeError(f"{TAG} qkv shapes: M={M} K={K} N={N} heads={heads} head_dim={head_dim} "
+                           f"batch={batch}")
+    row_scale = row_scale.reshape(-1).float().contiguous()
+    col_scale = col_scale.reshape(-1).float().contiguous()
+    code = _out_dtype_code(out_dtype, (torch.bfloat16, torch.float16))
+    if bias is not None:
+        bias = bias.to(out_dtype).contiguous()
+    S = M // batch
+    outs = [torch.empty((batch, heads, S, head_dim), dtype=out_dtype, device=a.device) for _ in range(3)]
+    _check(lib().b200q_i8_matmul_nt_dequant_qkv(
+        _p(a), a.stride(0), _p(w), w.stride(0), _p(row_scale), _p(col_scale), col_scale.numel(),
+        _p(bias), _p(outs[0]), _p(outs[1]), _p(outs[2]), code, heads, head_dim, batch, M, N, K,
+        _stream(a)))
+    return tuple(outs)
+
+
+def rms_rope_partial_(q, k, freqs, q_weight, k_weight, eps=1e-6):
+    """In place: RMSNorm (fp32 weights) + split-half RoPE on the first 2R dims of
+    bf16 q, k [B, H, S, D]; freqs [B*S, R, 2, 2] bf16 (any leading shape with that
+    element count).  rms_rope_attention_partial (dit_kernels.mm:825-874, 1677)."""
+    _require_cuda(q, k, freqs, q_weight, k_weight)
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or q.shape != k.shape or q.dim() != 4:
+        raise RuntimeError(f"{TAG} rms_rope_partial_ expects bf16 q/k of one [B,H,S,D] shape")
+    if not (q.is_contiguous() and k.is_contiguous()):
+        raise RuntimeError(f"{TAG} rms_rope_partial_ works in place on contiguous q/k")
+    B, H, S, D = q.shape
+    fr = freqs.to(torch.bfloat16).contiguous()
+    R = fr.shape[-3] if fr.dim() >= 3 else 0
+    if fr.numel() != B * S * R * 4:
+        raise RuntimeError(f"{TAG} freqs must hold [B*S, R, 2, 2] = {B * S} x R x 4 values")
+    qw = q_weight.float().contiguous()
+    kw = k_weight.float().contiguous()
+    _check(lib().b200q_rms_rope_partial(_p(q), _p(k), _p(fr), _p(qw), _p(kw), B, H, S, D, R,
+                                        float(eps), _stream(q)))
 
 
 def i8_matmul_nt_fused(a, w, row_scale, bias=None):
@@ -448,6 +500,11 @@ def _register_ops():
     L.define("i8_matmul_nt_fused(Tensor a, Tensor w, Tensor row_scale, Tensor? bias=None) -> Tensor")
     L.define("i8_matmul_nt_fused_cs(Tensor a, Tensor w, Tensor row_scale, Tensor col_scale, "
              "Tensor? bias=None, ScalarType out_dtype=15, str act='none') -> Tensor")
+    L.define("i8_matmul_nt_fused_cs_qkv(Tensor a, Tensor w, Tensor row_scale, Tensor col_scale, "
+             "Tensor? bias, int heads, int head_dim, int batch=1, ScalarType out_dtype=15) "
+             "-> (Tensor, Tensor, Tensor)")
+    L.define("rms_rope_partial_(Tensor(a!) q, Tensor(b!) k, Tensor freqs, Tensor q_weight, "
+             "Tensor k_weight, float eps=1e-06) -> ()")
     L.define("i8_linear(Tensor x, Tensor w, Tensor w_scale, Tensor? bias=None, "
              "ScalarType out_dtype=15, str act='none') -> Tensor")
     L.define("fp8_quant_tensorwise(Tensor x) -> (Tensor, Tensor)")
@@ -468,6 +525,8 @@ def _register_ops():
         "i8_matmul_nt_fused": i8_matmul_nt_fused,
         "i8_matmul_nt_fused_cs": i8_matmul_nt_fused_cs,
         "i8_linear": i8_linear,
+        "i8_matmul_nt_fused_cs_qkv": i8_matmul_nt_fused_cs_qkv,
+        "rms_rope_partial_": rms_rope_partial_,
         "fp8_quant_tensorwise": fp8_quant_tensorwise,
         "fp8_linear": fp8_linear,
         "fp8_scaled_mm": lambda a, w, sa=None, sb=None, sr=None, b=None, od=torch.bfloat16,
@@ -492,6 +551,10 @@ def _register_ops():
                                                                       dtype=torch.bfloat16),
         "i8_matmul_nt_fused_cs": lambda a, w, rs, cs, bias=None, od=torch.bfloat16, act="none":
         a.new_empty((a.shape[0], w.shape[0]), dtype=od),
+        "i8_matmul_nt_fused_cs_qkv": lambda a, w, rs, cs, bias, heads, head_dim, batch=1,
+        od=torch.bfloat16: tuple(a.new_empty((batch, heads, a.shape[0] // batch, head_dim), dtype=od)
+                                 for _ in range(3)),
+        "rms_rope_partial_": lambda q, k, fr, qw, kw, eps=1e-6: None,
         "i8_linear": lambda x, w, ws, bias=None, od=torch.bfloat16, act="none": x.new_empty(
             (*x.shape[:-1], w.shape[0]), dtype=od),
         "fp8_quant_tensorwise": lambda x: (x.new_empty((x.numel() // x.shape[-1], x.shape[-1]),

@@ -13,6 +13,7 @@
 
 #include "../../include/b200q.h"
 #include "gemm8.cuh"
+#include "qkv_rope.cuh"
 #include "quant.cuh"
 #include "w8a16.cuh"
 
@@ -501,6 +502,58 @@ int b200q_i8_linear(const void* x, int x_dtype, int64_t ldx, const int8_t* w, in
   return b200q_i8_matmul_nt_dequant(q_scratch, K, w, ldw, scale_scratch, col_scale,
                                     col_scale_numel, bias, act, out, out_dtype, ldo, M, N, K,
                                     stream);
+}
+
+int b200q_i8_matmul_nt_dequant_qkv(const int8_t* a, int64_t lda, const int8_t* w, int64_t ldw,
+                                   const float* row_scale, const float* col_scale,
+                                   int64_t col_scale_numel, const void* bias, void* q_out,
+                                   void* k_out, void* v_out, int out_dtype, int64_t heads,
+                                   int64_t head_dim, int64_t batch, int64_t M, int64_t N, int64_t K,
+                                   void* stream) {
+  if (!a || !w || !row_scale || !col_scale || !q_out || !k_out || !v_out || !valid_dims(M, N, K) ||
+      K == 0 || lda < K || ldw < K || heads <= 0 || head_dim <= 0 || head_dim % 32 != 0 ||
+      batch <= 0 || M % batch != 0 || N != 3 * heads * head_dim ||
+      (col_scale_numel != 1 && col_scale_numel != N) ||
+      (out_dtype != B200Q_BF16 && out_dtype != B200Q_F16) || !aligned16(q_out) ||
+      !aligned16(k_out) || !aligned16(v_out))
+    return B200Q_ERR_INVALID;
+  EpiArgs ep = make_epi(q_out, N, out_dtype, M, N);
+  ep.row_scale = row_scale;
+  ep.row_scale_vec = 1;
+  ep.col_scale = col_scale;
+  ep.col_scale_vec = col_scale_numel == N && N != 1 ? 1 : 0;
+  ep.bias = bias;
+  ep.bias_dtype = bias ? (out_dtype == B200Q_BF16 ? kBiasBF16 : kBiasF16) : kBiasNone;
+  ep.qkv[0] = q_out;
+  ep.qkv[1] = k_out;
+  ep.qkv[2] = v_out;
+  ep.qkv_heads = static_cast<int>(heads);
+  ep.qkv_dim = static_cast<int>(head_dim);
+  ep.qkv_seq = static_cast<int>(M / batch);
+  return gemm8<MmaKind::I8, kEpiI8Dequant>(a, lda, w, ldw, M, N, K, ep, static_cast<cudaStream_t>(stream));
+}
+
+int b200q_rms_rope_partial(void* q, void* k, const void* freqs, const float* q_weight,
+                           const float* k_weight, int64_t batch, int64_t heads, int64_t seq,
+                           int64_t head_dim, int64_t rot_half, float eps, void* stream) {
+  if (!q || !k || !q_weight || !k_weight || batch <= 0 || heads <= 0 || seq <= 0 ||
+      head_dim <= 0 || head_dim % 32 != 0 || head_dim > 256 || rot_half < 0 ||
+      2 * rot_half > head_dim || (rot_half > 0 && !freqs) ||
+      batch * heads * seq >= (int64_t(1) << 30))
+    return B200Q_ERR_INVALID;
+  const DeviceInfo* d = current_device();
+  if (!d) return B200Q_ERR_UNSUPPORTED;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t warps = 2 * batch * heads * seq;
+  const dim3 grid(static_cast<unsigned>((warps + kRrWarps - 1) / kRrWarps));
+  auto* qp = static_cast<__nv_bfloat16*>(q);
+  auto* kp = static_cast<__nv_bfloat16*>(k);
+  auto* fp = static_cast<const __nv_bfloat16*>(freqs);
+  if (head_dim <= 128)
+    rms_rope_partial_kernel<1><<<grid, kRrWarps * 32, 0, st>>>(qp, kp, fp, q_weight, k_weight, int(batch), int(heads), int(seq), int(head_dim), int(rot_half), eps);
+  else
+    rms_rope_partial_kernel<2><<<grid, kRrWarps * 32, 0, st>>>(qp, kp, fp, q_weight, k_weight, int(batch), int(heads), int(seq), int(head_dim), int(rot_half), eps);
+  return finish_launch();
 }
 
 size_t b200q_prologue_sync_bytes(int64_t M) {

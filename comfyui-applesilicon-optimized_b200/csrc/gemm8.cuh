@@ -134,8 +134,9 @@ __device__ __forceinline__ bool load_col_params(const EpiArgs& e, int n0, float 
 __device__ __forceinline__ void store_chunk(const EpiArgs& e, int64_t m, int n0, const float (&v)[32]) {
   const bool full = n0 + 32 <= e.N;
   if (e.out_dtype == kOutBF16 || e.out_dtype == kOutF16) {
-    if (full && ((e.ldo & 7) == 0) && ((reinterpret_cast<uintptr_t>(e.out) & 15) == 0)) {
-      uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(e.out) + m * e.ldo + n0);
+    uint16_t* p16 = out_ptr16(e, m, n0);
+    if (full && (e.qkv_heads > 0 || (e.ldo & 7) == 0) && ((reinterpret_cast<uintptr_t>(p16) & 15) == 0)) {
+      uint4* o = reinterpret_cast<uint4*>(p16);
       if (e.out_dtype == kOutBF16) {
 #pragma unroll
         for (int j = 0; j < 4; ++j)

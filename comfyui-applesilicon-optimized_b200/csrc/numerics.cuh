@@ -99,7 +99,29 @@ struct EpiArgs {
   int bias_dtype;
   int act;
   int M, N;
+  // Attention-layout scatter (qkv_heads > 0): columns [kind*H*D + h*D + d] of
+  // row m = b*S + s go to qkv[kind][((b*H + h)*S + s)*D + d] (kind 0/1/2 = Q/K/V),
+  // instead of out[m*ldo + n].  Requires N == 3*H*D and D % 32 == 0.
+  void* qkv[3];
+  int qkv_heads, qkv_dim, qkv_seq;
 };
+
+// Element pointer of output (m, n) for 16-bit outputs, in either layout.
+__device__ __forceinline__ uint16_t* out_ptr16(const EpiArgs& e, int64_t m, int n) {
+  if (e.qkv_heads > 0) {
+    const int W = e.qkv_heads * e.qkv_dim;
+    const int kind = n / W;
+    const int inner = n - kind * W;
+    const int h = inner / e.qkv_dim;
+    const int d = inner - h * e.qkv_dim;
+    const int64_t b = m / e.qkv_seq;
+    const int64_t s = m - b * e.qkv_seq;
+    // a select, not qkv[kind]: a runtime index would copy EpiArgs to local memory
+    void* base = kind == 0 ? e.qkv[0] : (kind == 1 ? e.qkv[1] : e.qkv[2]);
+    return static_cast<uint16_t*>(base) + ((b * e.qkv_heads + h) * e.qkv_seq + s) * e.qkv_dim + d;
+  }
+  return static_cast<uint16_t*>(e.out) + m * e.ldo + n;
+}
 
 // The INT8 W8A8 dequant epilogue of the reference (int8_gemm.mm:417-443 and the
 // eager chunked path int8_linear_kernel_mps.py:203-215):
@@ -141,10 +163,10 @@ __device__ __forceinline__ void store_out(const EpiArgs& e, int64_t m, int n, fl
   const int64_t off = m * e.ldo + n;
   switch (e.out_dtype) {
     case kOutBF16:
-      static_cast<__nv_bfloat16*>(e.out)[off] = __float2bfloat16_rn(v);
+      *reinterpret_cast<__nv_bfloat16*>(out_ptr16(e, m, n)) = __float2bfloat16_rn(v);
       break;
     case kOutF16:
-      static_cast<__half*>(e.out)[off] = __float2half_rn(v);
+      *reinterpret_cast<__half*>(out_ptr16(e, m, n)) = __float2half_rn(v);
       break;
     default:
       static_cast<float*>(e.out)[off] = v;

@@ -133,6 +133,33 @@ B200Q_API int b200q_fp8_quant_tensorwise(const void* x, int x_dtype, int64_t M, 
                                uint8_t* q, int64_t ldq, float* scale, unsigned int* amax_scratch,
                                void* stream);
 
+/* INT8 GEMM + dequant epilogue (as b200q_i8_matmul_nt_dequant, no activation)
+ * storing straight into attention layout: column kind*H*D + h*D + d of token
+ * row m = b*S + s (S = M / batch) goes to {q,k,v}_out[((b*H + h)*S + s)*D + d]
+ * (kind 0/1/2), i.e. three [batch, H, S, D] tensors instead of one [M, 3*H*D].
+ * N must be 3*heads*head_dim, head_dim % 32 == 0, outputs 16-byte aligned.
+ * Replaces i8_matmul2d_nt_fused_cs_qkv (_patches/int8_ext/int8_gemm.mm:2028,
+ * epilogue :445-474), whose layout is the batch = 1 case. */
+B200Q_API int b200q_i8_matmul_nt_dequant_qkv(const int8_t* a, int64_t lda, const int8_t* w,
+                                             int64_t ldw, const float* row_scale,
+                                             const float* col_scale, int64_t col_scale_numel,
+                                             const void* bias, void* q_out, void* k_out,
+                                             void* v_out, int out_dtype, int64_t heads,
+                                             int64_t head_dim, int64_t batch, int64_t M,
+                                             int64_t N, int64_t K, void* stream);
+
+/* In place on bf16 q, k [batch, heads, seq, head_dim] (contiguous): per row
+ * RMSNorm y = bf16((x * rsqrt(sum(x^2)/D + eps)) * w) with fp32 weights
+ * q_weight/k_weight [D], then split-half RoPE on the first 2*rot_half dims with
+ * the bf16 rotation-matrix table freqs [batch*seq, rot_half, 2, 2] (diagonal
+ * product rounded, then the off-diagonal product added with one rounding).
+ * head_dim % 32 == 0, <= 256; rot_half = 0 skips RoPE.  Replaces
+ * rms_rope_attention_partial (_patches/dit_ext/dit_kernels.mm:825-874, 1677). */
+B200Q_API int b200q_rms_rope_partial(void* q, void* k, const void* freqs, const float* q_weight,
+                                     const float* k_weight, int64_t batch, int64_t heads,
+                                     int64_t seq, int64_t head_dim, int64_t rot_half, float eps,
+                                     void* stream);
+
 /* Fused quant prologue: the activation quantization runs inside the GEMM launch
  * (idle warps quantize 128-row bands while the tensor cores work; the TMA
  * producer waits for a band's rows before loading them), so there is no separate

@@ -326,3 +326,81 @@ def bf16_ulp_diff(a, b):
         return np.where(i & 0x8000, 0x8000 - (i & 0x7FFF), 0x8000 + i)
 
     return int(np.abs(ordered(ia) - ordered(ib)).max()) if ia.size else 0
+
+
+# ------------------------------------------------------------------ QKV layout, RMSNorm, RoPE
+def qkv_scatter(dense, heads, head_dim, batch=1):
+    """[M, 3*H*D] -> three [B, H, S, D] attention-layout tensors (M = B*S): the
+    storage change of the reference's QKV epilogue (nax_frag_store_dequant_cs_qkv,
+    _patches/int8_ext/int8_gemm.mm:445-474, whose layout is the B = 1 case
+    [1, H, M, D]); values are untouched."""
+    M = dense.shape[0]
+    S = M // batch
+    return tuple(part.reshape(batch, S, heads, head_dim).permute(0, 2, 1, 3).contiguous()
+                 for part in dense.split(heads * head_dim, dim=-1))
+
+
+def _rms_sumsq_f32(x):
+    """Sum of squares of rows x [R, D] (float32) in the reduction order the
+    reference restates for native F.rms_norm (torch_rms_sumsq,
+    _patches/dit_ext/dit_kernels.mm:60-80): virtual thread vt sums elements
+    4vt..4vt+3 in order (fp32 multiply, then add); each group of 32 vt is
+    reduced across lanes, here by the xor butterfly (offsets 16, 8, 4, 2, 1);
+    the group totals are then reduced the same way (zero-padded to 32)."""
+    R, D = x.shape
+    vt_count = 32 * ((((D + 3) // 4) + 31) // 32)
+    acc = np.zeros((R, vt_count), np.float32)
+    for i in range(4):
+        idx = np.arange(vt_count) * 4 + i
+        ok = idx < D
+        v = np.zeros((R, vt_count), np.float32)
+        v[:, ok] = x[:, idx[ok]]
+        acc = (acc + (v * v).astype(np.float32)).astype(np.float32)
+
+    def butterfly(a):  # a [R, 32] -> every lane holds the xor-tree total; return lane 0
+        a = a.copy()
+        for o in (16, 8, 4, 2, 1):
+            a = (a + a[:, np.arange(32) ^ o]).astype(np.float32)
+        return a[:, 0]
+
+    groups = vt_count // 32
+    sums = np.zeros((R, 32), np.float32)
+    for gi in range(groups):
+        sums[:, gi] = butterfly(acc[:, 32 * gi:32 * gi + 32])
+    return butterfly(sums)
+
+
+def rms_rope_partial(q, k, freqs, q_weight, k_weight, eps):
+    """In-place semantics of rms_rope_attention_partial
+    (_patches/dit_ext/dit_kernels.mm:825-874), returned as new tensors:
+      y   = bf16((x * rsqrt(sumsq / D + eps)) * w[d])          per (b, h, s) row
+      d >= 2R: out = y;  d < 2R: i = d mod R, r = d >= R, m = freqs[row][i][r]
+      r = 0: bf16(bf16(m0 * y[i]) + m1 * y[i+R]);  r = 1: bf16(bf16(m1 * y[i+R]) + m0 * y[i])
+    q, k [B, H, S, D] bf16; freqs [B*S, R, 2, 2] bf16 (rotation matrix rows per
+    token row m = b*S + s); weights fp32 [D].  fp32 arithmetic throughout, the
+    rsqrt correctly rounded."""
+    B, H, S, D = q.shape
+    fr = to_f32(freqs).reshape(B * S, -1, 2, 2)
+    R = fr.shape[1]
+
+    def one(t, w):
+        x = to_f32(t).reshape(B, H, S, D)
+        rows = x.reshape(-1, D)
+        tot = _rms_sumsq_f32(rows)
+        mean = (tot.astype(np.float64) / D).astype(np.float32)
+        inv = (1.0 / np.sqrt((mean + np.float32(eps)).astype(np.float32).astype(np.float64))).astype(np.float32)
+        wv = np.asarray(w, np.float32).reshape(1, D)
+        y = round_bf16(((rows * inv[:, None]).astype(np.float32) * wv).astype(np.float32))
+        y = y.reshape(B, H, S, D)
+        out = y.copy()
+        m_idx = (np.arange(B)[:, None] * S + np.arange(S)[None, :])  # [B, S]
+        mat = fr[m_idx]  # [B, S, R, 2, 2]
+        yi = y[..., :R]          # [B, H, S, R]
+        yr = y[..., R:2 * R]
+        m00 = mat[:, None, :, :, 0, 0]; m01 = mat[:, None, :, :, 0, 1]
+        m10 = mat[:, None, :, :, 1, 0]; m11 = mat[:, None, :, :, 1, 1]
+        out[..., :R] = round_bf16((round_bf16((m00 * yi).astype(np.float32)) + (m01 * yr).astype(np.float32)).astype(np.float32))
+        out[..., R:2 * R] = round_bf16((round_bf16((m11 * yr).astype(np.float32)) + (m10 * yi).astype(np.float32)).astype(np.float32))
+        return from_f32(out, torch.bfloat16)
+
+    return one(q, q_weight), one(k, k_weight)
