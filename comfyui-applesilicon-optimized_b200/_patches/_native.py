@@ -19,6 +19,12 @@ _patches/fp8_ext/fp8_matmul2d.mm:355-360, _patches/fp8s_ext/w8a16_gemm.mm:316-32
   i8_matmul_nt_fused_cs_qkv(a, w, rs, cs, bias, heads, head_dim, batch)
                                             -> q, k, v in [B, H, S, D] (i8_matmul2d_nt_fused_cs_qkv)
   rms_rope_partial_(q, k, freqs, qw, kw, eps) -> in-place RMSNorm + split-half RoPE
+  silu_mul_split(x [M,2F] bf16)             -> act [M,F] = bf16(bf16(silu(gate)) * up)
+  i8_swiglu_rot(x [M,2F] bf16)              -> convrot(act) [M,F] bf16   (i8_swiglu_rot)
+  i8_swiglu_quant(x [M,2F], rotate)         -> (q int8 [M,F], scale [M,1]) of (rotated) act
+  i8_matmul_nt_fused_cs_swiglu(a, w [2F,K], rs, cs, bias) -> act [M,F]  (FC1 + SwiGLU epilogue)
+  i8_mlp_bridge_prequant(a, w1, rs, cs, bias, rotate, tile_rows)
+                                            -> (q, scale) FC2 input      (i8_mlp_bridge_prequant)
   i8_linear(x, w, w_scale, bias, out_dtype) -> quant + GEMM + dequant epilogue
                                                (B200Q_FUSED_PROLOGUE=1: quant inside the GEMM)
   fp8_quant_tensorwise(x)                   -> (q e4m3 [M,K], scale f32 [])
@@ -79,6 +85,13 @@ _SIGNATURES = {
     "b200q_w8a16_linear": ([_vp, _int, _i64, _vp, _i64, _vp, _vp, _int, _int, _vp, _int, _i64, _i64,
                             _i64, _i64, _vp, _sz, _vp], _int),
     "b200q_fp8_decode": ([_vp, _i64, _int, _vp, _int, _vp], _int),
+    "b200q_silu_mul_split": ([_vp, _i64, _i64, _i64, _vp, _i64, _vp], _int),
+    "b200q_i8_swiglu_rot": ([_vp, _i64, _i64, _i64, _vp, _i64, _vp], _int),
+    "b200q_i8_swiglu_quant": ([_vp, _i64, _i64, _i64, _int, _vp, _i64, _vp, _vp], _int),
+    "b200q_i8_matmul_nt_dequant_swiglu": ([_vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _vp, _i64,
+                                           _i64, _i64, _i64, _vp], _int),
+    "b200q_i8_mlp_bridge_prequant": ([_vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _i64,
+                                      _int, _i64, _vp, _vp, _i64, _vp, _vp], _int),
 }
 
 
@@ -279,6 +292,103 @@ def rms_rope_partial_(q, k, freqs, q_weight, k_weight, eps=1e-6):
     kw = k_weight.float().contiguous()
     _check(lib().b200q_rms_rope_partial(_p(q), _p(k), _p(fr), _p(qw), _p(kw), B, H, S, D, R,
                                         float(eps), _stream(q)))
+
+
+SWIGLU_MAX_F = 28672  # B200Q_SWIGLU_MAX_F
+
+
+def _wide_2d(x, name):
+    _require_cuda(x)
+    x = _rows_2d(x.reshape(-1, x.shape[-1]) if x.dim() != 2 else x, name)
+    if x.dtype != torch.bfloat16:
+        raise RuntimeError(f"{TAG} {name} must be bf16, got {x.dtype}")
+    if x.shape[1] % 2:
+        raise RuntimeError(f"{TAG} {name} width {x.shape[1]} is odd (expected [M, 2F])")
+    return x, x.shape[0], x.shape[1] // 2
+
+
+def silu_mul_split(x):
+    """SwiGLU of a split-half bf16 [..., 2F] tensor -> [..., F] (silu_mul_split)."""
+    shp = x.shape
+    x2, M, F = _wide_2d(x, "x")
+    out = torch.empty((M, F), dtype=torch.bfloat16, device=x.device)
+    _check(lib().b200q_silu_mul_split(_p(x2), x2.stride(0), M, F, _p(out), F, _stream(x2)))
+    return out.reshape(*shp[:-1], F)
+
+
+def i8_swiglu_rot(x):
+    """Convrot-rotated SwiGLU of a bf16 [M, 2F] tensor -> [M, F] bf16 (i8_swiglu_rot)."""
+    x2, M, F = _wide_2d(x, "x")
+    out = torch.empty((M, F), dtype=torch.bfloat16, device=x.device)
+    _check(lib().b200q_i8_swiglu_rot(_p(x2), x2.stride(0), M, F, _p(out), F, _stream(x2)))
+    return out
+
+
+def i8_swiglu_quant(x, rotate=True):
+    """Per-token INT8 quant of the (convrot-rotated) SwiGLU of a bf16 [M, 2F]
+    tensor, in one pass: (q int8 [M, F], scale f32 [M, 1])."""
+    x2, M, F = _wide_2d(x, "x")
+    q = torch.empty((M, F), dtype=torch.int8, device=x.device)
+    s = torch.empty((M, 1), dtype=torch.float32, device=x.device)
+    _check(lib().b200q_i8_swiglu_quant(_p(x2), x2.stride(0), M, F, int(bool(rotate)), _p(q), F,
+                                       _p(s), _stream(x2)))
+    return q, s
+
+
+def _fc1_args(a, w, row_scale, col_scale, bias):
+    _require_cuda(a, w, row_scale, col_scale, bias)
+    a, w = _rows_2d(a, "a"), _rows_2d(w, "w")
+    if a.dtype != torch.int8 or w.dtype != torch.int8:
+        raise RuntimeError(f"{TAG} FC1 operands must be int8")
+    M, K = a.shape
+    N2 = w.shape[0]
+    if w.shape[1] != K or N2 % 2:
+        raise RuntimeError(f"{TAG} FC1 shapes: a {tuple(a.shape)} w {tuple(w.shape)}")
+    row_scale = row_scale.reshape(-1).float().contiguous()
+    col_scale = col_scale.reshape(-1).float().contiguous()
+    if row_scale.numel() != M or col_scale.numel() not in (1, N2):
+        raise RuntimeError(f"{TAG} scale numel mismatch: row {row_scale.numel()} (M={M}), "
+                           f"col {col_scale.numel()} (2F={N2})")
+    if bias is not None:
+        bias = bias.to(torch.bfloat16).contiguous()
+        if bias.numel() != N2:
+            raise RuntimeError(f"{TAG} FC1 bias numel {bias.numel()} != 2F {N2}")
+    return a, w, row_scale, col_scale, bias, M, K, N2
+
+
+def i8_matmul_nt_fused_cs_swiglu(a, w, row_scale, col_scale, bias=None):
+    """FC1 (INT8 GEMM, channelwise two-rounding dequant + bias) with SwiGLU in the
+    epilogue: a [M,K] int8, w [2F,K] int8 (rows [gate; up]) -> act [M,F] bf16."""
+    a, w, rs, cs, bias, M, K, N2 = _fc1_args(a, w, row_scale, col_scale, bias)
+    out = torch.empty((M, N2 // 2), dtype=torch.bfloat16, device=a.device)
+    _check(lib().b200q_i8_matmul_nt_dequant_swiglu(_p(a), a.stride(0), _p(w), w.stride(0), _p(rs),
+                                                   _p(cs), cs.numel(), _p(bias), _p(out), N2 // 2,
+                                                   M, N2, K, _stream(a)))
+    return out
+
+
+BRIDGE_SCRATCH_BYTES = 1 << 30  # act scratch bound of the automatic row tiling
+
+
+def i8_mlp_bridge_prequant(a, w1, row_scale, col_scale, bias=None, rotate=True, tile_rows=-1):
+    """FC1 -> SwiGLU (-> convrot) -> per-token INT8 quant: the FC2 input
+    (q int8 [M,F], scale f32 [M,1]) without FC1's [M,2F] output
+    (i8_mlp_bridge_prequant).  tile_rows: rows per FC1 pass (0 = all rows,
+    -1 = all rows unless the [rows, F] bf16 scratch would exceed 1 GiB)."""
+    a, w1, rs, cs, bias, M, K, N2 = _fc1_args(a, w1, row_scale, col_scale, bias)
+    F = N2 // 2
+    if tile_rows < 0:
+        tile_rows = 0 if M * F * 2 <= BRIDGE_SCRATCH_BYTES else max(
+            256, (BRIDGE_SCRATCH_BYTES // (F * 2)) // 256 * 256)
+    rows = M if tile_rows == 0 else min(M, int(tile_rows))
+    scratch = torch.empty((max(rows, 1), F), dtype=torch.bfloat16, device=a.device)
+    q = torch.empty((M, F), dtype=torch.int8, device=a.device)
+    s = torch.empty((M, 1), dtype=torch.float32, device=a.device)
+    _check(lib().b200q_i8_mlp_bridge_prequant(_p(a), a.stride(0), _p(w1), w1.stride(0), _p(rs),
+                                              _p(cs), cs.numel(), _p(bias), M, N2, K,
+                                              int(bool(rotate)), int(tile_rows), _p(scratch),
+                                              _p(q), F, _p(s), _stream(a)))
+    return q, s
 
 
 def i8_matmul_nt_fused(a, w, row_scale, bias=None):
@@ -516,6 +626,13 @@ def _register_ops():
     L.define("w8a16_linear(Tensor x, Tensor w, Tensor? w_scale=None, Tensor? bias=None, "
              "str act='none', ScalarType? out_dtype=None) -> Tensor")
     L.define("fp8_decode(Tensor t, ScalarType out_dtype=6) -> Tensor")
+    L.define("silu_mul_split(Tensor x) -> Tensor")
+    L.define("i8_swiglu_rot(Tensor x) -> Tensor")
+    L.define("i8_swiglu_quant(Tensor x, bool rotate=True) -> (Tensor, Tensor)")
+    L.define("i8_matmul_nt_fused_cs_swiglu(Tensor a, Tensor w, Tensor row_scale, Tensor col_scale, "
+             "Tensor? bias=None) -> Tensor")
+    L.define("i8_mlp_bridge_prequant(Tensor a, Tensor w1, Tensor row_scale, Tensor col_scale, "
+             "Tensor? bias=None, bool rotate=True, int tile_rows=-1) -> (Tensor, Tensor)")
 
     impls = {
         "quant_rowwise_i8": quant_rowwise_i8,
@@ -533,6 +650,11 @@ def _register_ops():
         act="none": fp8_scaled_mm(a, w, sa, sb, sr, b, od, act),
         "w8a16_linear": w8a16_linear,
         "fp8_decode": fp8_decode,
+        "silu_mul_split": silu_mul_split,
+        "i8_swiglu_rot": i8_swiglu_rot,
+        "i8_swiglu_quant": i8_swiglu_quant,
+        "i8_matmul_nt_fused_cs_swiglu": i8_matmul_nt_fused_cs_swiglu,
+        "i8_mlp_bridge_prequant": i8_mlp_bridge_prequant,
     }
     for name, fn in impls.items():
         L.impl(name, fn, "CUDA")
@@ -567,6 +689,16 @@ def _register_ops():
         "w8a16_linear": lambda x, w, ws=None, b=None, act="none", od=None: x.new_empty(
             (*x.shape[:-1], w.shape[0]), dtype=od or x.dtype),
         "fp8_decode": lambda t, od=torch.float32: t.new_empty(t.shape, dtype=od),
+        "silu_mul_split": lambda x: x.new_empty((*x.shape[:-1], x.shape[-1] // 2)),
+        "i8_swiglu_rot": lambda x: x.new_empty((x.shape[0], x.shape[1] // 2)),
+        "i8_swiglu_quant": lambda x, rotate=True: (
+            x.new_empty((x.shape[0], x.shape[1] // 2), dtype=torch.int8),
+            x.new_empty((x.shape[0], 1), dtype=torch.float32)),
+        "i8_matmul_nt_fused_cs_swiglu": lambda a, w, rs, cs, bias=None: a.new_empty(
+            (a.shape[0], w.shape[0] // 2), dtype=torch.bfloat16),
+        "i8_mlp_bridge_prequant": lambda a, w1, rs, cs, bias=None, rotate=True, tile_rows=-1: (
+            a.new_empty((a.shape[0], w1.shape[0] // 2), dtype=torch.int8),
+            a.new_empty((a.shape[0], 1), dtype=torch.float32)),
     }
     for name, fn in fakes.items():
         torch.library.register_fake(f"b200q::{name}", fn, lib=L)

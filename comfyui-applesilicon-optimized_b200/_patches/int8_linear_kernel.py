@@ -12,8 +12,14 @@ comfy_kitchen's eager ``int8_linear`` (rowwise quant -> _int_mm -> chunked
 rescale -> + bias).  ``_kernel`` exposes the reference's native-module method
 names on top of ``torch.ops.b200q``.
 
-Convrot (Hadamard-rotated) checkpoints rotate with comfy_kitchen's own helpers
-before the quant, exactly as the reference does.  Opt-in: ASFP8_INT8_EXT=1.
+Convrot (Hadamard-rotated) checkpoints rotate inside the fused rotate+quant
+kernel (groupsize 256) or with comfy_kitchen's own helpers.
+
+SwiGLU MLPs (:538-776): ``int8_mlp_bridge(fc1, fc2, x)`` runs FC1 with SwiGLU in
+the GEMM epilogue, then the convrot quant of the [M, F] activation, then FC2 --
+FC1's [M, 2F] output is never formed; ``_try_int8_swiglu_forward(linear, x)``
+(the ``linear_input_act(..., "swiglu")`` route) quantizes the SwiGLU of an
+already materialised [M, 2F] tensor in one pass.  Opt-in: ASFP8_INT8_EXT=1.
 """
 import inspect
 import os
@@ -54,6 +60,17 @@ class _NativeInt8Kernel:
         # split_tail / long / moss are Apple tile schedules; the persistent tcgen05
         # kernel covers ragged M natively, and the bytes do not depend on them.
         return torch.ops.b200q.i8_matmul_nt_fused_cs(a, b, row_scale, col_scale, bias, out_dtype)
+
+    @staticmethod
+    def i8_swiglu_rot(x):
+        return torch.ops.b200q.i8_swiglu_rot(x)
+
+    @staticmethod
+    def i8_mlp_bridge_prequant(a_i8, fc1_weight, row_scale, fc1_col_scale, fc1_bias=None,
+                               long_schedule=True, tile_rows=-1):
+        # long_schedule is an Apple tile schedule; tile_rows bounds the act scratch.
+        return torch.ops.b200q.i8_mlp_bridge_prequant(a_i8, fc1_weight, row_scale, fc1_col_scale,
+                                                      fc1_bias, True, int(tile_rows))
 
     @staticmethod
     def warmup():
@@ -183,6 +200,110 @@ def _try_int8_kernel_forward(self, input):
                                getattr(params, "convrot_groupsize", 256))
 
 
+def _int8_layer_ok(layer):
+    """The weight / layer eligibility shared by the routes (:563-573, :726-737)."""
+    try:
+        from comfy_kitchen.tensor import QuantizedTensor
+    except Exception:
+        return False
+    w = getattr(layer, "weight", None)
+    if not isinstance(w, QuantizedTensor) or getattr(w, "_layout_cls", None) != "TensorWiseINT8Layout":
+        return False
+    if getattr(layer, "_full_precision_mm", False) or getattr(layer, "comfy_force_cast_weights", False):
+        return False
+    if len(getattr(layer, "weight_function", [])) or len(getattr(layer, "bias_function", [])):
+        return False
+    return not getattr(w._params, "transposed", False)
+
+
+def _swiglu_activation(x):
+    """Materialise SwiGLU once (int8_linear_kernel_mps.py:693-705): the b200q
+    silu_mul_split kernel for bf16 CUDA tensors, comfy's eager expression for
+    other dtypes (as the reference does for them)."""
+    wide = x.shape[-1]
+    half = wide // 2
+    if (_kernel is not None and x.device.type == "cuda" and x.dtype == torch.bfloat16
+            and os.environ.get("ASFP8_INT8_SWIGLU_EAGERACT") != "1"):
+        return torch.ops.b200q.silu_mul_split(x.reshape(-1, wide)).reshape(*x.shape[:-1], half)
+    return torch.nn.functional.silu(x[..., :half]) * x[..., half:]
+
+
+def _try_int8_swiglu_forward(linear, x):
+    """linear(swiglu(x)) for an INT8 ``linear`` (FC2) and a wide [..., 2F] x, or
+    None (int8_linear_kernel_mps.py:708-776).  bf16 input: SwiGLU (+ convrot for
+    convrot checkpoints) and the per-token quant in one kernel, then the INT8
+    GEMM; otherwise SwiGLU, then the ordinary INT8 route."""
+    if _kernel is None:
+        return None
+    try:
+        from comfy_kitchen.tensor import QuantizedTensor
+    except Exception:
+        return None
+    if not isinstance(x, torch.Tensor) or x.device.type != "cuda" or isinstance(x, QuantizedTensor):
+        return None
+    if not _int8_layer_ok(linear):
+        return None
+    w = linear.weight
+    params = w._params
+    wide = x.shape[-1]
+    if wide % 2:
+        return None
+    half = wide // 2
+    x2 = x.reshape(-1, wide)
+    convrot = getattr(params, "convrot", False)
+    groupsize = getattr(params, "convrot_groupsize", 256)
+    from . import _native
+    if (x.dtype == torch.bfloat16 and x2.is_contiguous() and half <= _native.SWIGLU_MAX_F
+            and (not convrot or (os.environ.get("ASFP8_INT8_SWIGLU_ROT", "1") == "1"
+                                 and groupsize == 256 and half % 256 == 0))):
+        x_8, x_scale = torch.ops.b200q.i8_swiglu_quant(x2, bool(convrot))
+        return _int8_linear_prequant(x_8, x_scale, w._qdata, params.scale, linear.bias, x.dtype,
+                                     x.shape)
+    act = _swiglu_activation(x)
+    return _int8_linear_kernel(act, w._qdata, params.scale, linear.bias, x.dtype, convrot, groupsize)
+
+
+def int8_mlp_bridge(fc1, fc2, x):
+    """FC2(SwiGLU(FC1(x))) for INT8 FC1/FC2 without FC1's [M, 2F] output, or None
+    (int8_mlp_bridge, int8_linear_kernel_mps.py:538-690).  Same eligibility:
+    bf16 contiguous 2-D x, both weights TensorWiseINT8Layout, FC2 convrot with
+    groupsize 256, FC1 rows a multiple of 512 and twice FC2's input width."""
+    if (_kernel is None
+            or os.environ.get("ASFP8_INT8_MLP_BRIDGE", "1") != "1"
+            or os.environ.get("ASFP8_INT8_SWIGLU", "1") != "1"
+            or os.environ.get("ASFP8_INT8_SWIGLU_ROT", "1") != "1"):
+        return None
+    try:
+        if (not isinstance(x, torch.Tensor) or x.dim() != 2 or x.device.type != "cuda"
+                or x.dtype != torch.bfloat16 or not x.is_contiguous()):
+            return None
+        if not (_int8_layer_ok(fc1) and _int8_layer_ok(fc2)):
+            return None
+        p1, p2 = fc1.weight._params, fc2.weight._params
+        if not getattr(p2, "convrot", False) or getattr(p2, "convrot_groupsize", 256) != 256:
+            return None
+        w1, w2 = fc1.weight._qdata, fc2.weight._qdata
+        if (w1.dim() != 2 or w2.dim() != 2 or w1.shape[0] % 512 or w1.shape[1] != x.shape[1]
+                or w2.shape[1] * 2 != w1.shape[0]):
+            return None
+        from . import _native
+        if w2.shape[1] > _native.CONVROT_MAX_K:
+            return None
+        s1, s2 = p1.scale.view(-1), p2.scale.view(-1)
+        if s1.numel() != w1.shape[0] or s2.numel() != w2.shape[0]:
+            return None
+        x_8, x_scale = _quant_cached(x, getattr(p1, "convrot", False),
+                                     getattr(p1, "convrot_groupsize", 256))
+        bias1 = fc1.bias.to(torch.bfloat16) if fc1.bias is not None else None
+        fc2_8, fc2_scale = _kernel.i8_mlp_bridge_prequant(
+            x_8.contiguous(), w1.contiguous(), x_scale.reshape(-1).float().contiguous(),
+            s1.float().contiguous(), bias1)
+        return _int8_linear_prequant(fc2_8, fc2_scale, w2, s2, fc2.bias, x.dtype, x.shape)
+    except Exception as e:
+        print(f"{TAG} MLP bridge fell back ({e!r})")
+        return None
+
+
 def _load_kernel():
     if not (_common.is_b200() and _common.native_ready()):
         print(f"{TAG} b200q library unavailable or device is not a B200; route not installed.")
@@ -244,11 +365,16 @@ def install():
             _orig_lia = ops.linear_input_act
 
             def linear_input_act_wrapped(linear, x, input_act, *args, **kwargs):
-                # Extended contracts (norm weights / residual epilogues) and the
-                # SwiGLU bridge stay on comfy's helper; a plain merged projection
-                # goes through Linear.forward, i.e. through this route.
+                # Extended contracts (norm weights / residual epilogues) stay on
+                # comfy's helper; the three-argument SwiGLU contract takes the
+                # fused SwiGLU-quant route; a plain merged projection goes
+                # through Linear.forward, i.e. through this route.
                 if args or kwargs:
                     return _orig_lia(linear, x, input_act, *args, **kwargs)
+                if input_act == "swiglu" and os.environ.get("ASFP8_INT8_SWIGLU", "1") == "1":
+                    res = _try_int8_swiglu_forward(linear, x)
+                    if res is not None:
+                        return res
                 if (input_act is None and isinstance(linear, torch.nn.Module)
                         and os.environ.get("ASFP8_INT8_PLAIN_LIA", "1") == "1"):
                     return linear(x)

@@ -124,8 +124,8 @@ int launch_gemm8_tc(const DeviceInfo* d, const void* a, int64_t lda, const void*
   CUtensorMap ta, tb;
   if (!make_tmap(&ta, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M, lda, kGemmBK, kGemmBM,
                  CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_tmap(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldw, kGemmBK, BN,
-                 CU_TENSOR_MAP_SWIZZLE_128B))
+      !make_tmap(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldw, kGemmBK,
+                 EPI == kEpiI8SwiGLU ? BN / 2 : BN, CU_TENSOR_MAP_SWIZZLE_128B))
     return B200Q_ERR_CUDA;
   auto kern = gemm8_tc_kernel<KIND, BN, STAGES, EPI, PRO>;
   constexpr int smem = PRO != kProNone ? Gemm8Layout<BN, STAGES>::kSmemBytesPro
@@ -217,6 +217,34 @@ int gemm8(const void* a, int64_t lda, const void* w, int64_t ldw, int64_t M, int
   if (M >= 256 && pair_kernels_enabled())
     return launch_gemm8_tc2<KIND, 6, EPI, PRO>(d, a, lda, w, ldw, int(M), int(N), int(K), ep, pro, st);
   return launch_gemm8_tc<KIND, 256, 4, EPI, PRO>(d, a, lda, w, ldw, int(M), int(N), int(K), ep, pro, st);
+}
+
+// FC1 with the SwiGLU epilogue: N2 = 2F weight rows [gate; up].  TMA path only
+// (both kernels split the B tile between the gate and up row ranges).
+int gemm8_swiglu(const void* a, int64_t lda, const void* w, int64_t ldw, int64_t M, int64_t N2,
+                 int64_t K, const EpiArgs& ep, cudaStream_t st) {
+  const DeviceInfo* d = current_device();
+  if (!d) return B200Q_ERR_UNSUPPORTED;
+  if (M == 0 || N2 == 0) return B200Q_OK;
+  if (!gemm8_tc_eligible(a, lda, w, ldw, K)) return B200Q_ERR_INVALID;
+  if (M >= 256 && pair_kernels_enabled())
+    return launch_gemm8_tc2<MmaKind::I8, 6, kEpiI8SwiGLU, kProNone>(d, a, lda, w, ldw, int(M), int(N2), int(K), ep, Prologue{}, st);
+  return launch_gemm8_tc<MmaKind::I8, 256, 4, kEpiI8SwiGLU, kProNone>(d, a, lda, w, ldw, int(M), int(N2), int(K), ep, Prologue{}, st);
+}
+
+template <bool ROT, bool QUANT>
+int launch_swiglu_rows(const DeviceInfo* d, const void* x, int64_t ldx, int64_t M, int64_t F,
+                       void* out, int64_t ldo, int8_t* q, int64_t ldq, float* scales,
+                       cudaStream_t st) {
+  auto kern = swiglu_rows_kernel<ROT, QUANT>;
+  const int smem = ROT ? static_cast<int>(2 * F * sizeof(float))
+                       : (QUANT ? static_cast<int>(F * sizeof(float)) : 0);
+  if (smem > 0 && !set_smem(kern, smem)) return B200Q_ERR_CUDA;
+  const int grid = static_cast<int>(M < int64_t(d->num_sms) * 8 ? M : int64_t(d->num_sms) * 8);
+  kern<<<grid, kQuantThreads, smem, st>>>(static_cast<const __nv_bfloat16*>(x), ldx, int(F),
+                                          static_cast<__nv_bfloat16*>(out), ldo, q, ldq, scales,
+                                          int(M));
+  return finish_launch();
 }
 
 EpiArgs make_epi(void* out, int64_t ldo, int out_dtype, int64_t M, int64_t N) {
@@ -531,6 +559,91 @@ int b200q_i8_matmul_nt_dequant_qkv(const int8_t* a, int64_t lda, const int8_t* w
   ep.qkv_dim = static_cast<int>(head_dim);
   ep.qkv_seq = static_cast<int>(M / batch);
   return gemm8<MmaKind::I8, kEpiI8Dequant>(a, lda, w, ldw, M, N, K, ep, static_cast<cudaStream_t>(stream));
+}
+
+int b200q_i8_matmul_nt_dequant_swiglu(const int8_t* a, int64_t lda, const int8_t* w, int64_t ldw,
+                                      const float* row_scale, const float* col_scale,
+                                      int64_t col_scale_numel, const void* bias, void* act_out,
+                                      int64_t ldo, int64_t M, int64_t N2, int64_t K, void* stream) {
+  if (!a || !w || !row_scale || !col_scale || !act_out || !valid_dims(M, N2, K) || K == 0 ||
+      lda < K || ldw < K || N2 <= 0 || N2 % 2 != 0 || ldo < N2 / 2 ||
+      (col_scale_numel != 1 && col_scale_numel != N2))
+    return B200Q_ERR_INVALID;
+  EpiArgs ep = make_epi(act_out, ldo, B200Q_BF16, M, N2);
+  ep.row_scale = row_scale;
+  ep.row_scale_vec = 1;
+  ep.col_scale = col_scale;
+  ep.col_scale_vec = col_scale_numel == N2 ? 1 : 0;
+  ep.bias = bias;
+  ep.bias_dtype = bias ? kBiasBF16 : kBiasNone;
+  return gemm8_swiglu(a, lda, w, ldw, M, N2, K, ep, static_cast<cudaStream_t>(stream));
+}
+
+static int swiglu_rows_args_ok(const void* x, int64_t ldx, int64_t M, int64_t F) {
+  return x && M >= 0 && M < (int64_t(1) << 31) && F > 0 && F <= B200Q_SWIGLU_MAX_F &&
+         ldx >= 2 * F;
+}
+
+int b200q_silu_mul_split(const void* x, int64_t ldx, int64_t M, int64_t F, void* out, int64_t ldo,
+                         void* stream) {
+  if (!swiglu_rows_args_ok(x, ldx, M, F) || !out || ldo < F) return B200Q_ERR_INVALID;
+  const DeviceInfo* d = current_device();
+  if (!d) return B200Q_ERR_UNSUPPORTED;
+  if (M == 0) return B200Q_OK;
+  return launch_swiglu_rows<false, false>(d, x, ldx, M, F, out, ldo, nullptr, 0, nullptr,
+                                          static_cast<cudaStream_t>(stream));
+}
+
+int b200q_i8_swiglu_rot(const void* x, int64_t ldx, int64_t M, int64_t F, void* out, int64_t ldo,
+                        void* stream) {
+  if (!swiglu_rows_args_ok(x, ldx, M, F) || !out || ldo < F) return B200Q_ERR_INVALID;
+  if (F % kRotGroup != 0) return B200Q_ERR_UNSUPPORTED;
+  const DeviceInfo* d = current_device();
+  if (!d) return B200Q_ERR_UNSUPPORTED;
+  if (M == 0) return B200Q_OK;
+  return launch_swiglu_rows<true, false>(d, x, ldx, M, F, out, ldo, nullptr, 0, nullptr,
+                                         static_cast<cudaStream_t>(stream));
+}
+
+int b200q_i8_swiglu_quant(const void* x, int64_t ldx, int64_t M, int64_t F, int rotate, int8_t* q,
+                          int64_t ldq, float* scales, void* stream) {
+  if (!swiglu_rows_args_ok(x, ldx, M, F) || !q || !scales || ldq < F) return B200Q_ERR_INVALID;
+  if (rotate && F % kRotGroup != 0) return B200Q_ERR_UNSUPPORTED;
+  const DeviceInfo* d = current_device();
+  if (!d) return B200Q_ERR_UNSUPPORTED;
+  if (M == 0) return B200Q_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (rotate) return launch_swiglu_rows<true, true>(d, x, ldx, M, F, nullptr, 0, q, ldq, scales, st);
+  return launch_swiglu_rows<false, true>(d, x, ldx, M, F, nullptr, 0, q, ldq, scales, st);
+}
+
+int b200q_i8_mlp_bridge_prequant(const int8_t* a, int64_t lda, const int8_t* w1, int64_t ldw,
+                                 const float* row_scale, const float* col_scale,
+                                 int64_t col_scale_numel, const void* bias, int64_t M, int64_t N2,
+                                 int64_t K, int rotate, int64_t tile_rows, void* act_scratch,
+                                 int8_t* q, int64_t ldq, float* scales, void* stream) {
+  const int64_t F = N2 / 2;
+  if (!a || !w1 || !row_scale || !col_scale || !act_scratch || !q || !scales ||
+      !valid_dims(M, N2, K) || K == 0 || lda < K || ldw < K || N2 <= 0 || N2 % 2 != 0 ||
+      ldq < F || tile_rows < 0 || (col_scale_numel != 1 && col_scale_numel != N2))
+    return B200Q_ERR_INVALID;
+  if (rotate && (F % kRotGroup != 0 || F > B200Q_CONVROT_MAX_K)) return B200Q_ERR_UNSUPPORTED;
+  if (M == 0) return B200Q_OK;
+  const int64_t rows = tile_rows == 0 || tile_rows > M ? M : tile_rows;
+  auto* act = static_cast<__nv_bfloat16*>(act_scratch);
+  for (int64_t r0 = 0; r0 < M; r0 += rows) {
+    const int64_t mr = M - r0 < rows ? M - r0 : rows;
+    int s = b200q_i8_matmul_nt_dequant_swiglu(a + r0 * lda, lda, w1, ldw, row_scale + r0,
+                                              col_scale, col_scale_numel, bias, act, F, mr, N2,
+                                              K, stream);
+    if (s != B200Q_OK) return s;
+    s = rotate ? b200q_quant_rowwise_i8_convrot(act, B200Q_BF16, mr, F, F, kRotGroup, q + r0 * ldq,
+                                                ldq, scales + r0, stream)
+               : b200q_quant_rowwise_i8(act, B200Q_BF16, mr, F, F, q + r0 * ldq, ldq,
+                                        scales + r0, stream);
+    if (s != B200Q_OK) return s;
+  }
+  return B200Q_OK;
 }
 
 int b200q_rms_rope_partial(void* q, void* k, const void* freqs, const float* q_weight,

@@ -35,7 +35,11 @@ constexpr int kGemmBK = 128;  // bytes = elements per k-block (one 128B swizzle 
 constexpr int kGemmThreads = 384;  // 4 control warps + 8 epilogue warps
 constexpr int kGemmGroupM = 16;
 
-enum EpiMode : int { kEpiInt32 = 0, kEpiI8Dequant = 1, kEpiScaled = 2 };
+// kEpiI8SwiGLU: the INT8 dequant epilogue on an FC1 whose N = 2F rows are
+// [gate; up]; each tile holds matching gate and up columns (the producer loads
+// the two row ranges into the two halves of the B tile) and the epilogue writes
+// act = swiglu(gate, up) [M, F] instead of the [M, 2F] output.
+enum EpiMode : int { kEpiInt32 = 0, kEpiI8Dequant = 1, kEpiScaled = 2, kEpiI8SwiGLU = 3 };
 
 template <int BN, int STAGES>
 struct Gemm8Layout {
@@ -129,10 +133,12 @@ __device__ __forceinline__ bool load_col_params(const EpiArgs& e, int n0, float 
   return true;
 }
 
-// Stores 32 values of row m at columns [n0, n0+32): 16-byte vector stores when
-// the chunk is whole and aligned, element stores on ragged edges.
-__device__ __forceinline__ void store_chunk(const EpiArgs& e, int64_t m, int n0, const float (&v)[32]) {
-  const bool full = n0 + 32 <= e.N;
+// Stores 32 values of row m at columns [n0, n0+32) (columns >= n_limit are
+// dropped): 16-byte vector stores when the chunk is whole and aligned, element
+// stores on ragged edges.
+__device__ __forceinline__ void store_chunk(const EpiArgs& e, int64_t m, int n0, const float (&v)[32],
+                                            int n_limit) {
+  const bool full = n0 + 32 <= n_limit;
   if (e.out_dtype == kOutBF16 || e.out_dtype == kOutF16) {
     uint16_t* p16 = out_ptr16(e, m, n0);
     if (full && (e.qkv_heads > 0 || (e.ldo & 7) == 0) && ((reinterpret_cast<uintptr_t>(p16) & 15) == 0)) {
@@ -158,7 +164,7 @@ __device__ __forceinline__ void store_chunk(const EpiArgs& e, int64_t m, int n0,
   }
 #pragma unroll
   for (int j = 0; j < 32; ++j)
-    if (n0 + j < e.N) store_out(e, m, n0 + j, v[j]);
+    if (n0 + j < n_limit) store_out(e, m, n0 + j, v[j]);
 }
 
 __device__ __forceinline__ void store_chunk_i32(const EpiArgs& e, int64_t m, int n0, const uint32_t (&r)[32]) {
@@ -181,7 +187,7 @@ template <int EPI, bool ACC_INT>
 __device__ __forceinline__ void epilogue_math(const uint32_t (&r)[32], const float (&cs)[32],
                                               const float (&bi)[32], bool has_bias, float rs,
                                               float xs, const EpiArgs& e, float (&v)[32]) {
-  if constexpr (EPI == kEpiI8Dequant) {
+  if constexpr (EPI == kEpiI8Dequant || EPI == kEpiI8SwiGLU) {
     // Reference order (int8_gemm.mm:417-443): s = cs*rs; T(C*s); T(r + bias).
     if (e.out_dtype == kOutF16) {
 #pragma unroll
@@ -221,6 +227,118 @@ __device__ __forceinline__ void epilogue_math(const uint32_t (&r)[32], const flo
   }
 }
 
+// Scale and bias of 8 consecutive columns n0.. (uniform loads; indices clamped
+// to the last column on a ragged edge).  Returns whether a bias is present.
+__device__ __forceinline__ bool load_col_params8(const EpiArgs& e, int n0, float (&cs)[8],
+                                                 float (&bi)[8]) {
+  const bool full = n0 + 8 <= e.N;
+  if (e.col_scale_vec) {
+    const float* p = e.col_scale + n0;
+    if (full && ((reinterpret_cast<uintptr_t>(p) & 15) == 0)) {
+      const float4 v0 = __ldg(reinterpret_cast<const float4*>(p));
+      const float4 v1 = __ldg(reinterpret_cast<const float4*>(p) + 1);
+      cs[0] = v0.x; cs[1] = v0.y; cs[2] = v0.z; cs[3] = v0.w;
+      cs[4] = v1.x; cs[5] = v1.y; cs[6] = v1.z; cs[7] = v1.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) cs[j] = __ldg(e.col_scale + min(n0 + j, e.N - 1));
+    }
+  } else {
+    const float c = __ldg(e.col_scale);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) cs[j] = c;
+  }
+  if (e.bias_dtype == kBiasNone) return false;
+  const uint16_t* p = static_cast<const uint16_t*>(e.bias) + n0;  // bf16
+  if (full && ((reinterpret_cast<uintptr_t>(p) & 15) == 0)) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      bi[2 * k] = __uint_as_float(w[k] << 16);
+      bi[2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      bi[j] = __uint_as_float(static_cast<uint32_t>(__ldg(p - n0 + min(n0 + j, e.N - 1))) << 16);
+  }
+  return true;
+}
+
+// SwiGLU epilogue of one accumulator tile for one epilogue warp.  The tile's BN
+// columns are BN/2 gate columns followed by the matching BN/2 up columns, both
+// for output columns [f_base, f_base + BN/2).  Warp half `half` takes BN/128 of
+// the 32-column gate chunks with their up partners, 8 columns at a time.  Each
+// side gets the reference's bf16 two-rounding dequant (+ bias) at its own
+// physical column (gate f, up F + f); then act = bf16(bf16(silu(gate)) * up).
+// The rare exact-silu fallback runs once per warp iteration for every lane that
+// still has one pending (a warp-uniform loop with a single inlined call site).
+template <int BN>
+__device__ __forceinline__ void swiglu_tile_epilogue(uint32_t taddr, int half, int f_base, int F,
+                                                     int64_t m, bool row_ok, float rs,
+                                                     const EpiArgs& ep) {
+  constexpr int kPairs = BN / 128;
+#pragma unroll 1
+  for (int c = half * kPairs; c < (half + 1) * kPairs; ++c) {
+    const int f0 = f_base + c * 32;
+    uint32_t packed[16];
+#pragma unroll
+    for (int sb = 0; sb < 4; ++sb) {
+      const int fs = f0 + sb * 8;
+      uint32_t rg[8], ru[8];
+      float csg[8], big[8], csu[8], biu[8];
+      tmem_ld8(taddr + c * 32 + sb * 8, rg);
+      tmem_ld8(taddr + BN / 2 + c * 32 + sb * 8, ru);
+      const bool hb = load_col_params8(ep, fs, csg, big);
+      load_col_params8(ep, F + fs, csu, biu);
+      tmem_ld_wait();
+      float g[8], u[8], a[8];
+      uint32_t slow = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        g[j] = round_bf16(__fmul_rn(__int2float_rn(static_cast<int32_t>(rg[j])), __fmul_rn(csg[j], rs)));
+        u[j] = round_bf16(__fmul_rn(__int2float_rn(static_cast<int32_t>(ru[j])), __fmul_rn(csu[j], rs)));
+        if (hb) {
+          g[j] = round_bf16(__fadd_rn(g[j], big[j]));
+          u[j] = round_bf16(__fadd_rn(u[j], biu[j]));
+        }
+        a[j] = silu_f32_fast(g[j]);
+        if (silu_needs_exact(a[j], g[j])) slow |= 1u << j;
+      }
+      while (__any_sync(0xffffffffu, slow != 0)) {
+        const int jj = slow ? __ffs(slow) - 1 : 0;
+        float gj = g[0];
+#pragma unroll
+        for (int j = 1; j < 8; ++j) gj = j == jj ? g[j] : gj;
+        const float e = silu_f32_exact_inl(gj);
+        if (slow) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) a[j] = j == jj ? e : a[j];
+          slow &= slow - 1;
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        packed[4 * sb + k] = pack_bf16x2(__fmul_rn(round_bf16(a[2 * k]), u[2 * k]),
+                                         __fmul_rn(round_bf16(a[2 * k + 1]), u[2 * k + 1]));
+    }
+    if (row_ok && f0 < F) {
+      uint16_t* p = static_cast<uint16_t*>(ep.out) + m * ep.ldo + f0;
+      if (f0 + 32 <= F && (ep.ldo & 7) == 0 && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          reinterpret_cast<uint4*>(p)[k] =
+              make_uint4(packed[4 * k], packed[4 * k + 1], packed[4 * k + 2], packed[4 * k + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (f0 + j < F) p[j] = static_cast<uint16_t>(packed[j >> 1] >> (16 * (j & 1)));
+      }
+    }
+  }
+}
+
 template <MmaKind KIND, int BN, int STAGES, int EPI, int PRO>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm8_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -241,8 +359,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  constexpr bool kSwiGLU = EPI == kEpiI8SwiGLU;
+  constexpr int kTileN = kSwiGLU ? BN / 2 : BN;  // output columns per tile
+  const int F = N >> 1;                          // SwiGLU: gate rows [0, F), up rows [F, 2F)
   const int num_m = (M + kGemmBM - 1) / kGemmBM;
-  const int num_n = (N + BN - 1) / BN;
+  const int num_n = ((kSwiGLU ? F : N) + kTileN - 1) / kTileN;
   const int num_tiles = num_m * num_n;
   const int num_kb = (K + kGemmBK - 1) / kGemmBK;
 
@@ -300,7 +421,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
           tma_load_2d(&tmA, &full[stage], sA + stage * L::kATile, kb * kGemmBK, mb * kGemmBM);
-          tma_load_2d(&tmB, &full[stage], sB + stage * L::kBTile, kb * kGemmBK, nb * BN);
+          if constexpr (kSwiGLU) {
+            // B tile = [gate rows; up rows] of this tile's columns (tensor map box = BN/2 rows).
+            tma_load_2d(&tmB, &full[stage], sB + stage * L::kBTile, kb * kGemmBK, nb * kTileN);
+            tma_load_2d(&tmB, &full[stage], sB + stage * L::kBTile + kTileN * kGemmBK, kb * kGemmBK,
+                        F + nb * kTileN);
+          } else {
+            tma_load_2d(&tmB, &full[stage], sB + stage * L::kBTile, kb * kGemmBK, nb * BN);
+          }
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
       }
@@ -382,22 +510,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (EPI != kEpiInt32 && ep.row_scale && row_ok) rs = __ldcg(ep.row_scale + (ep.row_scale_vec ? m : 0));
       }
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+      if constexpr (kSwiGLU) {
+        swiglu_tile_epilogue<BN>(taddr, half, nb * kTileN, F, m, row_ok, rs, ep);
+      } else {
 #pragma unroll 1
-      for (int c = half * kChunks; c < (half + 1) * kChunks; ++c) {
-        const int n0 = nb * BN + c * 32;
-        uint32_t r[32];
-        if constexpr (EPI == kEpiInt32) {
-          tmem_ld32(taddr + c * 32, r);
-          tmem_ld_wait();
-          if (row_ok && n0 < N) store_chunk_i32(ep, m, n0, r);
-        } else {
-          float cs[32], bi[32], v[32];
-          const bool has_bias = n0 < N ? load_col_params(ep, n0, cs, bi) : false;
-          tmem_ld32(taddr + c * 32, r);
-          tmem_ld_wait();
-          if (row_ok && n0 < N) {
-            epilogue_math<EPI, kAccInt>(r, cs, bi, has_bias, rs, xs, ep, v);
-            store_chunk(ep, m, n0, v);
+        for (int c = half * kChunks; c < (half + 1) * kChunks; ++c) {
+          const int n0 = nb * BN + c * 32;
+          uint32_t r[32];
+          if constexpr (EPI == kEpiInt32) {
+            tmem_ld32(taddr + c * 32, r);
+            tmem_ld_wait();
+            if (row_ok && n0 < N) store_chunk_i32(ep, m, n0, r);
+          } else {
+            float cs[32], bi[32], v[32];
+            const bool has_bias = n0 < N ? load_col_params(ep, n0, cs, bi) : false;
+            tmem_ld32(taddr + c * 32, r);
+            tmem_ld_wait();
+            if (row_ok && n0 < N) {
+              epilogue_math<EPI, kAccInt>(r, cs, bi, has_bias, rs, xs, ep, v);
+              store_chunk(ep, m, n0, v, N);
+            }
           }
         }
       }
@@ -461,8 +593,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t peer = rank ^ 1u;
   const int pair = blockIdx.x >> 1;
   const int num_pairs = gridDim.x >> 1;
+  constexpr bool kSwiGLU = EPI == kEpiI8SwiGLU;
+  constexpr int kTileN = kSwiGLU ? BN / 2 : BN;  // output columns per tile
+  const int F = N >> 1;                          // SwiGLU: gate rows [0, F), up rows [F, 2F)
   const int num_m = (M + BM - 1) / BM;
-  const int num_n = (N + BN - 1) / BN;
+  const int num_n = ((kSwiGLU ? F : N) + kTileN - 1) / kTileN;
   const int num_tiles = num_m * num_n;
   const int num_kb = (K + kGemmBK - 1) / kGemmBK;
 
@@ -512,7 +647,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         int mb, nb;
         gemm_tile_coords(tile, num_m, num_n, group_m, mb, nb);
         const int a_row = mb * BM + static_cast<int>(rank) * 128;
-        const int b_row = nb * BN + static_cast<int>(rank) * 128;
+        // SwiGLU: the even CTA loads the gate rows, the odd one the matching up
+        // rows, so accumulator columns [0,128) are gate and [128,256) up.
+        const int b_row = kSwiGLU ? (rank == 0 ? nb * kTileN : F + nb * kTileN)
+                                  : nb * BN + static_cast<int>(rank) * 128;
         if constexpr (PRO != kProNone) {
           const int band = a_row / kBandRows;
           if (band != ready_band) {
@@ -612,22 +750,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (EPI != kEpiInt32 && ep.row_scale && row_ok) rs = __ldcg(ep.row_scale + (ep.row_scale_vec ? m : 0));
       }
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+      if constexpr (kSwiGLU) {
+        swiglu_tile_epilogue<BN>(taddr, half, nb * kTileN, F, m, row_ok, rs, ep);
+      } else {
 #pragma unroll 1
-      for (int c = half * kChunks; c < (half + 1) * kChunks; ++c) {
-        const int n0 = nb * BN + c * 32;
-        uint32_t r[32];
-        if constexpr (EPI == kEpiInt32) {
-          tmem_ld32(taddr + c * 32, r);
-          tmem_ld_wait();
-          if (row_ok && n0 < N) store_chunk_i32(ep, m, n0, r);
-        } else {
-          float cs[32], bi[32], v[32];
-          const bool has_bias = n0 < N ? load_col_params(ep, n0, cs, bi) : false;
-          tmem_ld32(taddr + c * 32, r);
-          tmem_ld_wait();
-          if (row_ok && n0 < N) {
-            epilogue_math<EPI, kAccInt>(r, cs, bi, has_bias, rs, xs, ep, v);
-            store_chunk(ep, m, n0, v);
+        for (int c = half * kChunks; c < (half + 1) * kChunks; ++c) {
+          const int n0 = nb * BN + c * 32;
+          uint32_t r[32];
+          if constexpr (EPI == kEpiInt32) {
+            tmem_ld32(taddr + c * 32, r);
+            tmem_ld_wait();
+            if (row_ok && n0 < N) store_chunk_i32(ep, m, n0, r);
+          } else {
+            float cs[32], bi[32], v[32];
+            const bool has_bias = n0 < N ? load_col_params(ep, n0, cs, bi) : false;
+            tmem_ld32(taddr + c * 32, r);
+            tmem_ld_wait();
+            if (row_ok && n0 < N) {
+              epilogue_math<EPI, kAccInt>(r, cs, bi, has_bias, rs, xs, ep, v);
+              store_chunk(ep, m, n0, v, N);
+            }
           }
         }
       }

@@ -71,6 +71,39 @@ __device__ __forceinline__ float gelu_tanh(float x) {
 __device__ __forceinline__ float gelu_erf(float x) {
   return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f));
 }
+// SiLU of the reference's SwiGLU kernels (silu_mul_split_bf16,
+// dit_kernels.mm:724-737; i8_swiglu_rot_bf16, int8_gemm.mm:1521-1540):
+//   s = a / (1 + exp(-a)) in fp32, then rounded to bf16.
+// Defined here with exp correctly rounded to fp32 and the add and divide
+// correctly rounded, so the result is one well-defined number.  expf is within
+// 2 ulp, which moves s by at most ~10 fp32 ulp; that can change the bf16
+// rounding only when s lies within that distance of a bf16 tie (low 16 bits
+// near 0x8000), so those inputs, and the overflow edge a < -80, take the exact
+// route through a double-precision exp.
+__device__ __forceinline__ float silu_f32_exact_inl(float a) {
+  const float e = __double2float_rn(exp(-static_cast<double>(a)));
+  return __fdiv_rn(a, __fadd_rn(1.0f, e));
+}
+__device__ __noinline__ float silu_f32_exact(float a) { return silu_f32_exact_inl(a); }
+__device__ __forceinline__ float silu_f32_fast(float a) {
+  return __fdiv_rn(a, __fadd_rn(1.0f, expf(-a)));
+}
+// True when the fast s = silu_f32_fast(a) may round to a different bf16 than
+// the exact definition.
+__device__ __forceinline__ bool silu_needs_exact(float s, float a) {
+  const int lo = static_cast<int>(__float_as_uint(s) & 0xFFFFu);
+  return abs(lo - 0x8000) <= 32 || !(a > -80.0f);
+}
+__device__ __forceinline__ float silu_bf16(float a) {
+  float s = silu_f32_fast(a);
+  if (silu_needs_exact(s, a)) s = silu_f32_exact(a);
+  return round_bf16(s);
+}
+// act = bf16(bf16(silu(gate)) * up): the product of two bf16 values is exact in fp32.
+__device__ __forceinline__ float swiglu_bf16(float gate, float up) {
+  return round_bf16(__fmul_rn(silu_bf16(gate), up));
+}
+
 __device__ __forceinline__ float apply_act(float v, int act) {
   if (act == kActGeluTanh) return gelu_tanh(v);
   if (act == kActGeluErf) return gelu_erf(v);

@@ -251,6 +251,64 @@ __global__ void __launch_bounds__(kQuantThreads)
 // costs four block barriers whatever its width.
 constexpr int kRotGroup = 256;
 
+// Four radix-4 butterfly stages (strides 1, 4, 16, 64) of the unnormalised
+// 256-point Hadamard over every 256-wide group of src[0, K), ping-ponging with
+// dst; returns the buffer that holds the result.  Thread t owns position t of
+// every group (kQuantThreads == kRotGroup).  The caller synchronises after
+// filling src; the stages synchronise after each pass.
+__device__ __forceinline__ float* convrot_stages(float* src, float* dst, int K) {
+  const int t = threadIdx.x;
+#pragma unroll
+  for (int stride = 1; stride <= 64; stride *= 4) {
+    const int digit = (t / stride) & 3;
+    const int base = t - digit * stride;
+    for (int g0 = 0; g0 < K; g0 += kRotGroup) {
+      const float a0 = src[g0 + base];
+      const float a1 = src[g0 + base + stride];
+      const float a2 = src[g0 + base + 2 * stride];
+      const float a3 = src[g0 + base + 3 * stride];
+      float y;
+      if (digit == 0) y = __fsub_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3);
+      else if (digit == 1) y = __fadd_rn(__fsub_rn(__fadd_rn(a0, a1), a2), a3);
+      else if (digit == 2) y = __fadd_rn(__fadd_rn(__fsub_rn(a0, a1), a2), a3);
+      else y = __fadd_rn(__fadd_rn(__fsub_rn(a1, a0), a2), a3);
+      dst[g0 + t] = y;
+    }
+    __syncthreads();
+    float* tmp = src;
+    src = dst;
+    dst = tmp;
+  }
+  return src;
+}
+
+// Codes of one row whose values (already T-representable) sit in shared memory:
+// the divide-free quotient with the exact fallback near T's rounding ties.
+template <typename T>
+__device__ __forceinline__ void quant_row_smem(const float* src, int K, float s_math, int8_t* qr,
+                                               bool vec) {
+  const int t = threadIdx.x;
+  const float r_math = __frcp_rn(s_math);
+  if (vec && (reinterpret_cast<uintptr_t>(qr) % 8 == 0)) {
+    for (int i = t; i < (K >> 3); i += kQuantThreads) {
+      float y[8];
+      uint32_t w[2] = {0u, 0u};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) y[j] = src[8 * i + j];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float d = __fmul_rn(y[j], r_math);
+        if (near_tie<T>(d)) d = __fdiv_rn(y[j], s_math);
+        d = fminf(fmaxf(rintf(round_to<T>(d)), -128.0f), 127.0f);
+        w[j >> 2] |= (static_cast<uint32_t>(static_cast<int>(d)) & 0xFFu) << (8 * (j & 3));
+      }
+      reinterpret_cast<uint2*>(qr)[i] = make_uint2(w[0], w[1]);
+    }
+  } else {
+    for (int i = t; i < K; i += kQuantThreads) qr[i] = static_cast<int8_t>(quant_code<T>(src[i], s_math));
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kQuantThreads)
     quant_rowwise_i8_rot_kernel(const T* __restrict__ x, int64_t ldx, int8_t* __restrict__ q,
@@ -275,29 +333,7 @@ __global__ void __launch_bounds__(kQuantThreads)
       for (int i = t; i < K; i += kQuantThreads) bufa[i] = to_float<T>(xr[i]);
     }
     __syncthreads();
-    float* src = bufa;
-    float* dst = bufb;
-#pragma unroll
-    for (int stride = 1; stride <= 64; stride *= 4) {
-      const int digit = (t / stride) & 3;
-      const int base = t - digit * stride;
-      for (int g0 = 0; g0 < K; g0 += kRotGroup) {
-        const float a0 = src[g0 + base];
-        const float a1 = src[g0 + base + stride];
-        const float a2 = src[g0 + base + 2 * stride];
-        const float a3 = src[g0 + base + 3 * stride];
-        float y;
-        if (digit == 0) y = __fsub_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3);
-        else if (digit == 1) y = __fadd_rn(__fsub_rn(__fadd_rn(a0, a1), a2), a3);
-        else if (digit == 2) y = __fadd_rn(__fadd_rn(__fsub_rn(a0, a1), a2), a3);
-        else y = __fadd_rn(__fadd_rn(__fsub_rn(a1, a0), a2), a3);
-        dst[g0 + t] = y;
-      }
-      __syncthreads();
-      float* tmp = src;
-      src = dst;
-      dst = tmp;
-    }
+    float* src = convrot_stages(bufa, bufb, K);
     // src holds the unscaled rotation; scale by 2^-4 (exact), round to T once.
     float amax = 0.0f;
     for (int i = t; i < K; i += kQuantThreads) {
@@ -306,27 +342,85 @@ __global__ void __launch_bounds__(kQuantThreads)
       amax = fmaxf(amax, fabsf(r));
     }
     const float s_math = row_scale_from_absmax<T>(amax, red, &bcast, scales, row);
-    const float r_math = __frcp_rn(s_math);
-    int8_t* qr = q + static_cast<int64_t>(row) * ldq;
-    if (vec && (ldq % 8 == 0) && (reinterpret_cast<uintptr_t>(q) % 8 == 0)) {
-      for (int i = t; i < (K >> 3); i += kQuantThreads) {
-        float y[8];
-        uint32_t w[2] = {0u, 0u};
+    quant_row_smem<T>(src, K, s_math, q + static_cast<int64_t>(row) * ldq, vec && (ldq % 8 == 0));
+    __syncthreads();  // buffers and red/bcast are reused by the next row
+  }
+}
+
+// ------------------------------------------------------------ SwiGLU rows
+// One CTA per row (grid-stride) of a split-half [M, 2F] bf16 tensor x (gate =
+// columns [0, F), up = [F, 2F)):
+//   act = bf16(bf16(silu(gate)) * up)                       (silu_mul_split_bf16,
+//                                                            dit_kernels.mm:724-737)
+//   ROT:   act <- bf16(H256(act) * 2^-4) per 256-group     (i8_swiglu_rot_bf16,
+//                                                            int8_gemm.mm:1521-1555)
+//   QUANT: per-token INT8 codes + scale of act              (i8_quant_rowwise,
+//                                                            int8_gemm.mm:1337-1381)
+//   else:  act written to out [M, F] (bf16).
+// Shared memory: ROT 2F floats, QUANT without ROT F floats, neither none.
+template <bool ROT, bool QUANT>
+__global__ void __launch_bounds__(kQuantThreads)
+    swiglu_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int F,
+                       __nv_bfloat16* __restrict__ out, int64_t ldo, int8_t* __restrict__ q,
+                       int64_t ldq, float* __restrict__ scales, int M) {
+  extern __shared__ float rot_smem[];
+  float* bufa = rot_smem;
+  float* bufb = rot_smem + F;
+  __shared__ float red[kQuantThreads / 32];
+  __shared__ float bcast;
+  constexpr bool kSmem = ROT || QUANT;
+  const int t = threadIdx.x;
+  const bool vec = (F % 8 == 0) && (ldx % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
+  const bool vec_out = !kSmem && vec && (ldo % 8 == 0) && (reinterpret_cast<uintptr_t>(out) % 16 == 0);
+  for (int row = blockIdx.x; row < M; row += gridDim.x) {
+    const __nv_bfloat16* xr = x + static_cast<int64_t>(row) * ldx;
+    __nv_bfloat16* orow = out + static_cast<int64_t>(row) * ldo;
+    if (vec) {
+      for (int i = t; i < (F >> 3); i += kQuantThreads) {
+        const uint4 gv = __ldcs(reinterpret_cast<const uint4*>(xr) + i);
+        const uint4 uv = __ldcs(reinterpret_cast<const uint4*>(xr + F) + i);
+        const __nv_bfloat16* ge = reinterpret_cast<const __nv_bfloat16*>(&gv);
+        const __nv_bfloat16* ue = reinterpret_cast<const __nv_bfloat16*>(&uv);
+        float a[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) y[j] = src[8 * i + j];
+        for (int j = 0; j < 8; ++j) a[j] = swiglu_bf16(__bfloat162float(ge[j]), __bfloat162float(ue[j]));
+        if constexpr (kSmem) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          float d = __fmul_rn(y[j], r_math);
-          if (near_tie<T>(d)) d = __fdiv_rn(y[j], s_math);
-          d = fminf(fmaxf(rintf(round_to<T>(d)), -128.0f), 127.0f);
-          w[j >> 2] |= (static_cast<uint32_t>(static_cast<int>(d)) & 0xFFu) << (8 * (j & 3));
+          for (int j = 0; j < 8; ++j) bufa[8 * i + j] = a[j];
+        } else if (vec_out) {
+          reinterpret_cast<uint4*>(orow)[i] =
+              make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]), pack_bf16x2(a[4], a[5]),
+                         pack_bf16x2(a[6], a[7]));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) orow[8 * i + j] = __float2bfloat16_rn(a[j]);
         }
-        reinterpret_cast<uint2*>(qr)[i] = make_uint2(w[0], w[1]);
       }
     } else {
-      for (int i = t; i < K; i += kQuantThreads) qr[i] = static_cast<int8_t>(quant_code<T>(src[i], s_math));
+      for (int i = t; i < F; i += kQuantThreads) {
+        const float a = swiglu_bf16(__bfloat162float(xr[i]), __bfloat162float(xr[F + i]));
+        if constexpr (kSmem) bufa[i] = a;
+        else orow[i] = __float2bfloat16_rn(a);
+      }
     }
-    __syncthreads();  // buffers and red/bcast are reused by the next row
+    if constexpr (kSmem) {
+      __syncthreads();
+      float* src = bufa;
+      if constexpr (ROT) {
+        src = convrot_stages(bufa, bufb, F);
+        for (int i = t; i < F; i += kQuantThreads) src[i] = round_bf16(src[i] * 0.0625f);
+      }
+      if constexpr (QUANT) {
+        float amax = 0.0f;
+        for (int i = t; i < F; i += kQuantThreads) amax = fmaxf(amax, fabsf(src[i]));
+        const float s_math = row_scale_from_absmax<__nv_bfloat16>(amax, red, &bcast, scales, row);
+        quant_row_smem<__nv_bfloat16>(src, F, s_math, q + static_cast<int64_t>(row) * ldq,
+                                      (F % 8 == 0) && (ldq % 8 == 0));
+      } else {
+        for (int i = t; i < F; i += kQuantThreads) orow[i] = __float2bfloat16_rn(src[i]);
+      }
+      __syncthreads();  // buffers and red/bcast are reused by the next row
+    }
   }
 }
 

@@ -160,6 +160,59 @@ B200Q_API int b200q_rms_rope_partial(void* q, void* k, const void* freqs, const 
                                      int64_t seq, int64_t head_dim, int64_t rot_half, float eps,
                                      void* stream);
 
+/* ---- SwiGLU between FC1 and FC2 (bf16 only, as the reference).
+ * A "wide" tensor is [M, 2F] bf16 with gate = columns [0, F), up = [F, 2F);
+ * act = bf16(bf16(silu(gate)) * up), silu(a) = a / (1 + exp(-a)) in fp32 with
+ * exp correctly rounded.  The convrot variants rotate every 256-wide group of
+ * act (radix-4 Hadamard butterflies in fp32, then * 2^-4 and one bf16 rounding),
+ * exactly as b200q_quant_rowwise_i8_convrot does for a plain activation. */
+#define B200Q_SWIGLU_MAX_F 28672
+
+/* act [M, F] of a wide tensor (row stride ldx >= 2F).  Replaces silu_mul_split
+ * (_patches/dit_ext/dit_kernels.mm:724-737) behind _swiglu_activation
+ * (_patches/int8_linear_kernel_mps.py:693-705). */
+B200Q_API int b200q_silu_mul_split(const void* x, int64_t ldx, int64_t M, int64_t F, void* out,
+                                   int64_t ldo, void* stream);
+
+/* Rotated act [M, F] (F % 256 == 0).  Replaces i8_swiglu_rot
+ * (_patches/int8_ext/int8_gemm.mm:1521-1555, host :2593-2624). */
+B200Q_API int b200q_i8_swiglu_rot(const void* x, int64_t ldx, int64_t M, int64_t F, void* out,
+                                  int64_t ldo, void* stream);
+
+/* Per-token INT8 codes q [M, F] + scales [M] of act (rotate = 1: of the rotated
+ * act) in one pass, the rotated act never written.  Replaces the FC2 pre-pass
+ * i8_swiglu_rot -> i8_quant_rowwise of _try_int8_swiglu_forward
+ * (_patches/int8_linear_kernel_mps.py:757-766) and, with rotate = 0,
+ * _swiglu_activation -> rowwise quant (:771-773). */
+B200Q_API int b200q_i8_swiglu_quant(const void* x, int64_t ldx, int64_t M, int64_t F, int rotate,
+                                    int8_t* q, int64_t ldq, float* scales, void* stream);
+
+/* FC1 of the bridge: INT8 GEMM of a [M, K] with w [N2 = 2F, K] (rows [gate; up],
+ * the checkpoint's layout) and the channelwise two-rounding dequant (+ bf16 bias
+ * [2F]) of b200q_i8_matmul_nt_dequant, followed in the same epilogue by
+ * act = swiglu(gate, up) -> act_out [M, F] bf16.  The [M, 2F] output is never
+ * formed.  Needs the TMA path (K % 16 == 0, lda/ldw % 16 == 0, 16-byte aligned
+ * a and w; B200Q_ERR_INVALID otherwise).  Replaces i8_matmul2d_nt_fused_cs ->
+ * silu_mul_split (_patches/int8_linear_kernel_mps.py:643-654). */
+B200Q_API int b200q_i8_matmul_nt_dequant_swiglu(const int8_t* a, int64_t lda, const int8_t* w,
+                                                int64_t ldw, const float* row_scale,
+                                                const float* col_scale, int64_t col_scale_numel,
+                                                const void* bias, void* act_out, int64_t ldo,
+                                                int64_t M, int64_t N2, int64_t K, void* stream);
+
+/* The FC1 -> SwiGLU (-> convrot) -> FC2-quant bridge: per block of tile_rows
+ * rows (0 = all), b200q_i8_matmul_nt_dequant_swiglu into act_scratch
+ * ([tile_rows or M, F] bf16, caller-owned) then the per-token quant of act
+ * (rotate = 1: convrot, F % 256 == 0 and F <= B200Q_CONVROT_MAX_K) into
+ * q [M, F] (row stride ldq) and scales [M].  Replaces i8_mlp_bridge_prequant
+ * (_patches/int8_ext/int8_gemm.mm:2377-2537), which is rotate = 1. */
+B200Q_API int b200q_i8_mlp_bridge_prequant(const int8_t* a, int64_t lda, const int8_t* w1,
+                                           int64_t ldw, const float* row_scale,
+                                           const float* col_scale, int64_t col_scale_numel,
+                                           const void* bias, int64_t M, int64_t N2, int64_t K,
+                                           int rotate, int64_t tile_rows, void* act_scratch,
+                                           int8_t* q, int64_t ldq, float* scales, void* stream);
+
 /* Fused quant prologue: the activation quantization runs inside the GEMM launch
  * (idle warps quantize 128-row bands while the tensor cores work; the TMA
  * producer waits for a band's rows before loading them), so there is no separate

@@ -404,3 +404,63 @@ def rms_rope_partial(q, k, freqs, q_weight, k_weight, eps):
         return from_f32(out, torch.bfloat16)
 
     return one(q, q_weight), one(k, k_weight)
+
+
+# ------------------------------------------------------------------ SwiGLU bridge
+def silu_f32(a):
+    """silu(a) = a / (1 + exp(-a)) evaluated as the reference's kernels do, in
+    fp32 (silu_mul_split_bf16, _patches/dit_ext/dit_kernels.mm:724-737;
+    i8_swiglu_rot_bf16, _patches/int8_ext/int8_gemm.mm:1521-1540), with exp
+    correctly rounded to fp32 (float64 exp, then one rounding; overflow -> inf,
+    so a < -88.7 gives -0 as the fp32 formula does) and the add and divide
+    correctly rounded."""
+    a = np.asarray(a, dtype=np.float32)
+    with np.errstate(over="ignore", invalid="ignore"):
+        e = np.exp(-a.astype(np.float64)).astype(np.float32)
+        d = (np.float32(1.0) + e).astype(np.float32)
+        return (a / d).astype(np.float32)
+
+
+def swiglu(wide):
+    """wide [..., 2F] (bf16) -> act [..., F] = bf16(bf16(silu(gate)) * up), gate
+    = the first F columns, up = the last F (silu_mul_split_bf16; the same
+    operation sequence as i8_swiglu_rot_bf16's first step).  The product of two
+    bf16 values is exact in fp32, so it is rounded once."""
+    w = to_f32(wide)
+    F = w.shape[-1] // 2
+    s = round_bf16(silu_f32(w[..., :F]))
+    with np.errstate(over="ignore"):  # |product| > fp32 max -> inf, as on the device
+        return from_f32(round_bf16((s * w[..., F:]).astype(np.float32)), torch.bfloat16)
+
+
+def swiglu_rot(wide):
+    """i8_swiglu_rot (_patches/int8_ext/int8_gemm.mm:1521-1555): the 256-group
+    convrot rotation of swiglu(wide), bf16."""
+    return rotate_convrot(swiglu(wide))
+
+
+def swiglu_quant(wide, rotate=True):
+    """The FC2 pre-pass of _try_int8_swiglu_forward
+    (_patches/int8_linear_kernel_mps.py:757-773): per-token INT8 quant of the
+    (rotated) SwiGLU activation -> (q int8 [M, F], scale f32 [M, 1])."""
+    act = swiglu_rot(wide) if rotate else swiglu(wide)
+    return quantize_int8_rowwise(act.reshape(-1, act.shape[-1]))
+
+
+def fc1_swiglu(a, w, row_scale, col_scale, bias=None):
+    """FC1 of the bridge: int8 GEMM + the channelwise two-rounding bf16 dequant
+    (+ bias) of i8_matmul2d_nt_fused_cs (int8_gemm.mm:417-443), then swiglu.
+    w [2F, K] has rows [gate; up]."""
+    c = int_mm(a, w.t())
+    wide = int8_dequant_epilogue(c, row_scale.reshape(-1, 1), col_scale.reshape(-1), bias,
+                                 torch.bfloat16)
+    return swiglu(wide)
+
+
+def mlp_bridge_prequant(a, w, row_scale, col_scale, bias=None, rotate=True):
+    """i8_mlp_bridge_prequant (int8_gemm.mm:2377-2537; rotate=True there): the
+    FC2 input (q, scale) of FC1 -> SwiGLU -> convrot -> rowwise quant."""
+    act = fc1_swiglu(a, w, row_scale, col_scale, bias)
+    if rotate:
+        act = rotate_convrot(act)
+    return quantize_int8_rowwise(act)

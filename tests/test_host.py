@@ -51,12 +51,19 @@ def test_abi_rejects_bad_arguments_without_a_gpu():
     assert L.b200q_fp8_scaled_mm(None, 16, None, 16, None, 0, None, 0, None, None, 0, 0, None, 0,
                                  16, 4, 4, 16, None) == 1
     assert L.b200q_fp8_decode(None, 4, 0, None, 0, None) == 1
+    assert L.b200q_silu_mul_split(None, 32, 4, 16, None, 16, None) == 1
+    assert L.b200q_i8_swiglu_quant(None, 32, 4, 16, 1, None, 16, None, None) == 1
+    assert L.b200q_i8_matmul_nt_dequant_swiglu(None, 16, None, 16, None, None, 1, None, None, 8,
+                                               4, 15, 16, None) == 1
+    assert L.b200q_i8_mlp_bridge_prequant(None, 16, None, 16, None, None, 1, None, 4, 512, 16, 1,
+                                          0, None, None, 256, None, None) == 1
 
 
 def test_torch_ops_registered_with_fake_kernels():
     for name in ("quant_rowwise_i8", "int_mm", "i8_matmul_nt", "i8_matmul_nt_fused",
                  "i8_matmul_nt_fused_cs", "i8_linear", "fp8_quant_tensorwise", "fp8_scaled_mm",
-                 "w8a16_linear", "fp8_decode"):
+                 "w8a16_linear", "fp8_decode", "silu_mul_split", "i8_swiglu_rot",
+                 "i8_swiglu_quant", "i8_matmul_nt_fused_cs_swiglu", "i8_mlp_bridge_prequant"):
         assert hasattr(torch.ops.b200q, name)
     from torch._subclasses.fake_tensor import FakeTensorMode
     with FakeTensorMode():
@@ -65,6 +72,14 @@ def test_torch_ops_registered_with_fake_kernels():
         assert torch.ops.b200q.w8a16_linear(x, w).shape == (5, 32)
         q, s = torch.ops.b200q.quant_rowwise_i8(x)
         assert q.dtype == torch.int8 and s.shape == (5, 1)
+        q, s = torch.ops.b200q.i8_swiglu_quant(x)
+        assert q.shape == (5, 32) and s.shape == (5, 1)
+        a8 = torch.empty(5, 64, dtype=torch.int8, device="cuda")
+        w1 = torch.empty(512, 64, dtype=torch.int8, device="cuda")
+        rs, cs = torch.empty(5, device="cuda"), torch.empty(512, device="cuda")
+        assert torch.ops.b200q.i8_matmul_nt_fused_cs_swiglu(a8, w1, rs, cs).shape == (5, 256)
+        q, s = torch.ops.b200q.i8_mlp_bridge_prequant(a8, w1, rs, cs)
+        assert q.shape == (5, 256) and q.dtype == torch.int8 and s.shape == (5, 1)
 
 
 def test_ops_fail_loudly_off_gpu():
@@ -205,12 +220,95 @@ def test_factory_keeps_defaults_and_forward_falls_through(fake_comfy):
     assert res.Linear().forward("x") == ("orig", "x")
 
 
-def test_linear_input_act_preserves_extended_contract(fake_comfy):
+def test_linear_input_act_preserves_extended_contract(fake_comfy, monkeypatch):
     ops, calls, _ = fake_comfy
+    native_calls = []
+    monkeypatch.setattr(int8_linear_kernel, "_try_int8_swiglu_forward",
+                        lambda *a: native_calls.append(a))
     lin, x = object(), object()
     assert ops.linear_input_act(lin, x, "rms_norm", "w", 1e-5) == "lia"
-    assert calls == [((lin, x, "rms_norm", "w", 1e-5), {})]
+    assert ops.linear_input_act(lin, x, "swiglu", "w", 1e-5, "r", 0.5) == "lia"
+    assert ops.linear_input_act(lin, x, "swiglu", residual="r") == "lia"
+    assert len(calls) == 3 and native_calls == []
+    # three-argument SwiGLU: the native route is tried, comfy's helper answers on None
     assert ops.linear_input_act(lin, x, "swiglu") == "lia"
+    assert native_calls == [(lin, x)]
+
+
+def test_linear_input_act_routes_three_argument_swiglu(fake_comfy, monkeypatch):
+    ops, calls, _ = fake_comfy
+    result = object()
+    monkeypatch.setattr(int8_linear_kernel, "_try_int8_swiglu_forward", lambda *a: result)
+    assert ops.linear_input_act(object(), object(), "swiglu") is result
+    monkeypatch.setenv("ASFP8_INT8_SWIGLU", "0")
+    assert ops.linear_input_act(object(), object(), "swiglu") == "lia"
+    assert len(calls) == 1
+
+
+class _FakeQT:
+    def __init__(self, qdata, scale, convrot=True, layout="TensorWiseINT8Layout"):
+        self._qdata, self._layout_cls = qdata, layout
+        self._params = SimpleNamespace(scale=scale, convrot=convrot, convrot_groupsize=256,
+                                       transposed=False)
+
+
+def _fake_layer(w, s, convrot=True, **kw):
+    d = dict(weight=_FakeQT(w, s, convrot), bias=None, weight_function=[], bias_function=[],
+             _full_precision_mm=False, comfy_force_cast_weights=False)
+    d.update(kw)
+    return SimpleNamespace(**d)
+
+
+def test_mlp_bridge_eligibility_and_call_sequence(monkeypatch):
+    """int8_mlp_bridge's eligibility (int8_linear_kernel_mps.py:541-583) and its
+    route: cached quant of x -> i8_mlp_bridge_prequant -> FC2 epilogue selection."""
+    ck = ModuleType("comfy_kitchen")
+    ck_t = ModuleType("comfy_kitchen.tensor")
+    ck_t.QuantizedTensor = _FakeQT
+    monkeypatch.setitem(sys.modules, "comfy_kitchen", ck)
+    monkeypatch.setitem(sys.modules, "comfy_kitchen.tensor", ck_t)
+    seen = []
+
+    class K:
+        def i8_quant_rowwise(self, x):
+            seen.append("quant")
+            return torch.zeros(x.shape, dtype=torch.int8), torch.ones(x.shape[0], 1)
+
+        def i8_mlp_bridge_prequant(self, a, w1, rs, cs, bias=None):
+            seen.append(("bridge", tuple(a.shape), tuple(w1.shape)))
+            return torch.zeros(a.shape[0], w1.shape[0] // 2, dtype=torch.int8), torch.ones(
+                a.shape[0], 1)
+
+        def i8_matmul2d_nt_fused_cs(self, a, b, rs, cs, bias=None, *x, out_dtype=None):
+            seen.append("fc2")
+            return torch.zeros(a.shape[0], b.shape[0], dtype=out_dtype)
+
+    monkeypatch.setattr(int8_linear_kernel, "_kernel", K())
+    monkeypatch.setattr(int8_linear_kernel, "_act_cache", None)
+    x = SimpleNamespace()  # replaced per case below
+    w1, w2 = torch.zeros(1024, 64, dtype=torch.int8), torch.zeros(96, 512, dtype=torch.int8)
+    fc1 = _fake_layer(w1, torch.ones(1024), convrot=False)
+    fc2 = _fake_layer(w2, torch.ones(96))
+
+    class CudaLike(torch.Tensor):
+        """A CPU tensor that reports device cuda (the seam's eligibility only)."""
+        @property
+        def device(self):
+            return torch.device("cuda")
+
+    x = torch.zeros(10, 64, dtype=torch.bfloat16).as_subclass(CudaLike)
+    out = int8_linear_kernel.int8_mlp_bridge(fc1, fc2, x)
+    assert out is not None and tuple(out.shape) == (10, 96)
+    assert seen == ["quant", ("bridge", (10, 64), (1024, 64)), "fc2"]
+    # ineligible: FC2 without convrot, FC1 rows not a multiple of 512, env switch, CPU x
+    assert int8_linear_kernel.int8_mlp_bridge(fc1, _fake_layer(w2, torch.ones(96), False), x) is None
+    bad_w1 = torch.zeros(768, 64, dtype=torch.int8)
+    assert int8_linear_kernel.int8_mlp_bridge(
+        _fake_layer(bad_w1, torch.ones(768), False), _fake_layer(
+            torch.zeros(96, 384, dtype=torch.int8), torch.ones(96)), x) is None
+    assert int8_linear_kernel.int8_mlp_bridge(fc1, fc2, torch.zeros(10, 64, dtype=torch.bfloat16)) is None
+    monkeypatch.setenv("ASFP8_INT8_MLP_BRIDGE", "0")
+    assert int8_linear_kernel.int8_mlp_bridge(fc1, fc2, x) is None
 
 
 def test_int8_epilogue_selection(monkeypatch):
