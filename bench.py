@@ -398,8 +398,8 @@ def run_b200q(args):
     eight_bit = spec["route"] in ("fp8", "int8")
     peak = (2.0 if eight_bit else 1.0) * peaks["bf16_sustained"]
     achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None
-    # W8A16 with <= 256 tokens is bound by the FP8 weight stream (the
-    # HBM roofline), so its roofline is bytes moved per launch / launch time.
+    # W8A16 with <= 256 tokens is bound by the FP8 weight stream (an HBM
+    # roofline), so its roofline is bytes moved per launch / launch time.
     hbm_bound = spec["route"] == "w8a16" and M <= 256
     achieved_gbs, bytes_per_launch = None, 0
     if hbm_bound and n_gemm:

@@ -175,7 +175,7 @@ def quant_rowwise_i8(x):
     return q, s
 
 
-CONVROT_MAX_K = 28672  # B200Q_CONVROT_MAX_K
+CONVROT_MAX_K = 65536  # B200Q_CONVROT_MAX_K
 
 
 def quant_rowwise_i8_convrot(x, groupsize=256):
@@ -294,7 +294,7 @@ def rms_rope_partial_(q, k, freqs, q_weight, k_weight, eps=1e-6):
                                         float(eps), _stream(q)))
 
 
-SWIGLU_MAX_F = 28672  # B200Q_SWIGLU_MAX_F
+SWIGLU_MAX_F = 65536  # B200Q_SWIGLU_MAX_F
 
 
 def _wide_2d(x, name):

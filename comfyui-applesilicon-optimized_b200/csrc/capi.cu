@@ -232,19 +232,31 @@ int gemm8_swiglu(const void* a, int64_t lda, const void* w, int64_t ldw, int64_t
   return launch_gemm8_tc<MmaKind::I8, 256, 4, kEpiI8SwiGLU, kProNone>(d, a, lda, w, ldw, int(M), int(N2), int(K), ep, Prologue{}, st);
 }
 
+// Grouped row kernel: one resident wave of CTAs (occupancy-sized), each looping
+// over rows.
+template <typename T, bool SWIGLU, bool ROT, bool QUANT>
+int launch_rows(const DeviceInfo* d, const void* x, int64_t ldx, int64_t M, int64_t K, void* out,
+                int64_t ldo, int8_t* q, int64_t ldq, float* scales, cudaStream_t st) {
+  auto kern = rows_kernel<T, SWIGLU, ROT, QUANT>;
+  const int smem = rows_smem_bytes(static_cast<int>(K), ROT, QUANT);
+  if (!set_smem(kern, smem)) return B200Q_ERR_CUDA;
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kRowThreads, smem) !=
+          cudaSuccess ||
+      per_sm < 1)
+    return B200Q_ERR_CUDA;
+  const int64_t wave = int64_t(d->num_sms) * per_sm;
+  const int grid = static_cast<int>(M < wave ? M : wave);
+  kern<<<grid, kRowThreads, smem, st>>>(static_cast<const T*>(x), ldx, int(K), static_cast<T*>(out),
+                                         ldo, q, ldq, scales, int(M));
+  return finish_launch();
+}
+
 template <bool ROT, bool QUANT>
 int launch_swiglu_rows(const DeviceInfo* d, const void* x, int64_t ldx, int64_t M, int64_t F,
                        void* out, int64_t ldo, int8_t* q, int64_t ldq, float* scales,
                        cudaStream_t st) {
-  auto kern = swiglu_rows_kernel<ROT, QUANT>;
-  const int smem = ROT ? static_cast<int>(2 * F * sizeof(float))
-                       : (QUANT ? static_cast<int>(F * sizeof(float)) : 0);
-  if (smem > 0 && !set_smem(kern, smem)) return B200Q_ERR_CUDA;
-  const int grid = static_cast<int>(M < int64_t(d->num_sms) * 8 ? M : int64_t(d->num_sms) * 8);
-  kern<<<grid, kQuantThreads, smem, st>>>(static_cast<const __nv_bfloat16*>(x), ldx, int(F),
-                                          static_cast<__nv_bfloat16*>(out), ldo, q, ldq, scales,
-                                          int(M));
-  return finish_launch();
+  return launch_rows<__nv_bfloat16, true, ROT, QUANT>(d, x, ldx, M, F, out, ldo, q, ldq, scales, st);
 }
 
 EpiArgs make_epi(void* out, int64_t ldo, int out_dtype, int64_t M, int64_t N) {
@@ -477,18 +489,9 @@ int b200q_quant_rowwise_i8_convrot(const void* x, int x_dtype, int64_t M, int64_
   if (!d) return B200Q_ERR_UNSUPPORTED;
   if (M == 0) return B200Q_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int smem = static_cast<int>(2 * K * sizeof(float));
-  const int grid = static_cast<int>(M < int64_t(d->num_sms) * 8 ? M : int64_t(d->num_sms) * 8);
-  if (x_dtype == B200Q_BF16) {
-    auto kern = quant_rowwise_i8_rot_kernel<__nv_bfloat16>;
-    if (!set_smem(kern, smem)) return B200Q_ERR_CUDA;
-    kern<<<grid, kQuantThreads, smem, st>>>(static_cast<const __nv_bfloat16*>(x), ldx, q, ldq, scales, int(M), int(K));
-  } else {
-    auto kern = quant_rowwise_i8_rot_kernel<__half>;
-    if (!set_smem(kern, smem)) return B200Q_ERR_CUDA;
-    kern<<<grid, kQuantThreads, smem, st>>>(static_cast<const __half*>(x), ldx, q, ldq, scales, int(M), int(K));
-  }
-  return finish_launch();
+  if (x_dtype == B200Q_BF16)
+    return launch_rows<__nv_bfloat16, false, true, true>(d, x, ldx, M, K, nullptr, 0, q, ldq, scales, st);
+  return launch_rows<__half, false, true, true>(d, x, ldx, M, K, nullptr, 0, q, ldq, scales, st);
 }
 
 int b200q_i8_matmul_nt(const int8_t* a, int64_t lda, const int8_t* w, int64_t ldw, int32_t* c,

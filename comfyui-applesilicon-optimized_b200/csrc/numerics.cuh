@@ -75,24 +75,50 @@ __device__ __forceinline__ float gelu_erf(float x) {
 // dit_kernels.mm:724-737; i8_swiglu_rot_bf16, int8_gemm.mm:1521-1540):
 //   s = a / (1 + exp(-a)) in fp32, then rounded to bf16.
 // Defined here with exp correctly rounded to fp32 and the add and divide
-// correctly rounded, so the result is one well-defined number.  expf is within
-// 2 ulp, which moves s by at most ~10 fp32 ulp; that can change the bf16
-// rounding only when s lies within that distance of a bf16 tie (low 16 bits
-// near 0x8000), so those inputs, and the overflow edge a < -80, take the exact
-// route through a double-precision exp.
+// correctly rounded (silu_f32_exact), so the result is one well-defined number.
+//
+// Fast path: exp(-a) = 2^t, t = -a log2(e) carried as t_hi + t_lo (t_hi the
+// rounded product, t_lo its exact residual plus the low part of log2(e)), so
+// 2^t = ex2.approx(t_hi) * (1 + t_lo ln 2) to within ex2.approx's ~2^-22;
+// then s = a * rcp.approx(1 + e).  Its relative distance from the exact
+// definition is below 2^-21, i.e. at most 8 fp32 ulps of s.  Rounding to bf16
+// can only tell the two apart when s lies that close to a bf16 tie (low 16 bits
+// near 0x8000), so those inputs -- and a < -80, where exp(-a) nears fp32
+// overflow -- take the exact route through a double-precision exp.  The input
+// of every SwiGLU here is a bf16 value, so the whole input domain (65,280 finite
+// values) is checked against the exact definition by the tests.
 __device__ __forceinline__ float silu_f32_exact_inl(float a) {
   const float e = __double2float_rn(exp(-static_cast<double>(a)));
   return __fdiv_rn(a, __fadd_rn(1.0f, e));
 }
 __device__ __noinline__ float silu_f32_exact(float a) { return silu_f32_exact_inl(a); }
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ float silu_f32_fast(float a) {
-  return __fdiv_rn(a, __fadd_rn(1.0f, expf(-a)));
+  const float kL2eHi = 1.44269502162933349609375f;  // log2(e) rounded to fp32
+  const float kL2eLo = 1.925963033500011e-08f;      // log2(e) - kL2eHi
+  const float kLn2 = 0.6931471805599453f;
+  // a > 100: exp(-a) < 2^-144 and 1 + exp(-a) == 1, as with the clamped argument
+  const float na = fmaxf(-a, -100.0f);
+  const float th = __fmul_rn(na, kL2eHi);
+  const float tl = __fmaf_rn(na, kL2eLo, __fmaf_rn(na, kL2eHi, -th));
+  const float p = ex2_approx(th);
+  const float e = __fmaf_rn(p, __fmul_rn(tl, kLn2), p);
+  return __fmul_rn(a, rcp_approx(__fadd_rn(1.0f, e)));
 }
 // True when the fast s = silu_f32_fast(a) may round to a different bf16 than
 // the exact definition.
 __device__ __forceinline__ bool silu_needs_exact(float s, float a) {
   const int lo = static_cast<int>(__float_as_uint(s) & 0xFFFFu);
-  return abs(lo - 0x8000) <= 32 || !(a > -80.0f);
+  return abs(lo - 0x8000) <= 24 || !(a > -80.0f);
 }
 __device__ __forceinline__ float silu_bf16(float a) {
   float s = silu_f32_fast(a);

@@ -20,6 +20,8 @@
 //    pattern, valid because the values are non-negative) and the quantize pass.
 #pragma once
 
+#include <type_traits>
+
 #include "numerics.cuh"
 #include "ptx.cuh"
 
@@ -135,17 +137,49 @@ __device__ __forceinline__ void quotients8(const uint4& v, float s, float r, flo
   }
 }
 
+// INT8 code of a quotient already rounded to T: rint (half-even), clamped to
+// [-128, 127], as the low byte of the returned word.  Adding 1.5 * 2^23 rounds y
+// to an integer held in the low mantissa bits (exact for |y| < 2^22, and a
+// quantizer's quotients stay below 2^9); the clamp acts on that bit pattern.
+__device__ __forceinline__ int code_bits(float y) {
+  const int b = __float_as_int(__fadd_rn(y, 12582912.0f));
+  return min(max(b, 0x4B400000 - 128), 0x4B400000 + 127);
+}
+// Low bytes of four words, first in the lowest byte.
+__device__ __forceinline__ uint32_t pack_low_bytes(int c0, int c1, int c2, int c3) {
+  const uint32_t lo = __byte_perm(static_cast<uint32_t>(c0), static_cast<uint32_t>(c1), 0x0040);
+  const uint32_t hi = __byte_perm(static_cast<uint32_t>(c2), static_cast<uint32_t>(c3), 0x0040);
+  return __byte_perm(lo, hi, 0x5410);
+}
+
 template <typename T>
 __device__ __forceinline__ uint2 quant8_fast(const uint4& v, float s, float r) {
   float y[8];
   quotients8<T, false>(v, s, r, y);
-  uint32_t w[2] = {0u, 0u};
+  int c[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float d = fminf(fmaxf(rintf(round_to<T>(y[i])), -128.0f), 127.0f);
-    w[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(d)) & 0xFFu) << (8 * (i & 3));
+  for (int i = 0; i < 8; ++i) c[i] = code_bits(round_to<T>(y[i]));
+  return make_uint2(pack_low_bytes(c[0], c[1], c[2], c[3]), pack_low_bytes(c[4], c[5], c[6], c[7]));
+}
+
+// Four codes of T-valued inputs x[i] (rint(T(x/s)) clamped), packed; the same
+// divide-free quotient with the exact fallback near T's ties as quotients8.
+template <typename T>
+__device__ __forceinline__ uint32_t quant4_fast(const float (&x)[4], float s, float r) {
+  float y[4];
+  uint32_t slow = 0u;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    y[i] = __fmul_rn(x[i], r);
+    slow |= near_tie<T>(y[i]) ? (1u << i) : 0u;
   }
-  return make_uint2(w[0], w[1]);
+  if (slow) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if ((slow >> i) & 1u) y[i] = __fdiv_rn(x[i], s);
+  }
+  return pack_low_bytes(code_bits(round_to<T>(y[0])), code_bits(round_to<T>(y[1])),
+                        code_bits(round_to<T>(y[2])), code_bits(round_to<T>(y[3])));
 }
 
 template <typename T>
@@ -236,190 +270,322 @@ __global__ void __launch_bounds__(kQuantThreads)
   }
 }
 
-// ------------------------------------------------------------ convrot + INT8
-// Convrot rotation fused into the per-token quant (the _quant_cached path with
-// convrot, _patches/int8_linear_kernel_mps.py:97-140; the reference's fused
-// form is i8_merge_rot_quant, _patches/int8_ext/int8_gemm.mm:1409-1505).
-// Each 256-wide group of a row is multiplied by the regular Hadamard
-// H = H4 (x) H4 (x) H4 (x) H4 / 16, H4 = [[1,1,1,-1],[1,1,-1,1],[1,-1,1,1],
-// [-1,1,1,1]], as four radix-4 butterfly stages in fp32 (strides 1, 4, 16, 64,
-// each output the row of H4 selected by its base-4 digit, evaluated in the
-// reference's term order), then * 2^-4 (exact) and one rounding to the input
-// dtype.  The rotated row stays in shared memory for the absmax and the
-// quantize pass, which follow quant_rowwise_i8 exactly.  All groups of a row
-// advance through a stage together (ping-pong buffers of K floats), so a row
-// costs four block barriers whatever its width.
+// ------------------------------------------------------------ grouped row kernels
+// Per-token row work on 256-element groups, used by three reference operations:
+//   * convrot rotation fused into the per-token INT8 quant (the _quant_cached
+//     path with convrot, _patches/int8_linear_kernel_mps.py:97-140; fused form
+//     i8_merge_rot_quant, _patches/int8_ext/int8_gemm.mm:1409-1505);
+//   * SwiGLU of a split-half [M, 2F] bf16 row (silu_mul_split_bf16,
+//     dit_kernels.mm:724-737), optionally rotated (i8_swiglu_rot_bf16,
+//     int8_gemm.mm:1521-1555), optionally quantized (-> i8_quant_rowwise).
+// The rotation multiplies each group by H = H4 (x) H4 (x) H4 (x) H4 / 16,
+// H4 = [[1,1,1,-1],[1,1,-1,1],[1,-1,1,1],[-1,1,1,1]], as four radix-4 stages in
+// fp32 (strides 1, 4, 16, 64; the element with base-4 digit d at the stage's
+// stride becomes row d of H4 applied to its four butterfly inputs, summed in
+// the reference kernels' association), then * 2^-4 (exact) and one rounding.
+//
+// Work split: half a warp owns two groups (A, B) at a time; lane l holds
+// elements 16l..16l+15 of both as packed fp32 pairs (A_j, B_j), so every
+// butterfly is a packed f32x2 add/sub (two IEEE round-to-nearest operations per
+// instruction).  Strides 1 and 4 act on the lane's own 16 elements; one
+// shared-memory transpose of the pairs then gives lane l the elements 16t + l
+// (t = 0..15), on which strides 16 and 64 are again lane-local.  The rounded
+// 16-bit values of a quantized row stay in shared memory until the row's
+// absmax (a block reduction) is known; the codes are then produced from there
+// with 16-byte reads exactly as quant_rowwise_i8 does.
 constexpr int kRotGroup = 256;
+constexpr int kRowThreads = kQuantThreads;  // 8 warps
+constexpr int kTrPitch = 18;                // 8-byte pairs per transposed row (bank skew)
+constexpr int kTrPairsPerHalf = 16 * kTrPitch;
+constexpr int kTrBytes = (kRowThreads / 16) * kTrPairsPerHalf * 8;
+constexpr int kPairPitch = 2 * kRotGroup / 2 + 16;  // 32-bit words per group pair (256 + skew)
 
-// Four radix-4 butterfly stages (strides 1, 4, 16, 64) of the unnormalised
-// 256-point Hadamard over every 256-wide group of src[0, K), ping-ponging with
-// dst; returns the buffer that holds the result.  Thread t owns position t of
-// every group (kQuantThreads == kRotGroup).  The caller synchronises after
-// filling src; the stages synchronise after each pass.
-__device__ __forceinline__ float* convrot_stages(float* src, float* dst, int K) {
-  const int t = threadIdx.x;
-#pragma unroll
-  for (int stride = 1; stride <= 64; stride *= 4) {
-    const int digit = (t / stride) & 3;
-    const int base = t - digit * stride;
-    for (int g0 = 0; g0 < K; g0 += kRotGroup) {
-      const float a0 = src[g0 + base];
-      const float a1 = src[g0 + base + stride];
-      const float a2 = src[g0 + base + 2 * stride];
-      const float a3 = src[g0 + base + 3 * stride];
-      float y;
-      if (digit == 0) y = __fsub_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3);
-      else if (digit == 1) y = __fadd_rn(__fsub_rn(__fadd_rn(a0, a1), a2), a3);
-      else if (digit == 2) y = __fadd_rn(__fadd_rn(__fsub_rn(a0, a1), a2), a3);
-      else y = __fadd_rn(__fadd_rn(__fsub_rn(a1, a0), a2), a3);
-      dst[g0 + t] = y;
-    }
-    __syncthreads();
-    float* tmp = src;
-    src = dst;
-    dst = tmp;
-  }
-  return src;
+// Dynamic shared memory of rows_kernel for a row of K elements: the transpose
+// tiles (ROT) and the row held for the quantize pass (QUANT): rotated rows as
+// 16-bit pairs (A, B) per position of a group pair, unrotated rows as plain
+// 16-bit values.
+__host__ __device__ constexpr int rows_smem_bytes(int K, bool rot, bool quant) {
+  return (rot ? kTrBytes : 0) +
+         (quant ? (rot ? ((K + 2 * kRotGroup - 1) / (2 * kRotGroup)) * kPairPitch * 4
+                       : ((K + 2 * kRotGroup - 1) / (2 * kRotGroup)) * 2 * kRotGroup * 2)
+                : 0);
 }
 
-// Codes of one row whose values (already T-representable) sit in shared memory:
-// the divide-free quotient with the exact fallback near T's rounding ties.
+__device__ __forceinline__ uint64_t pack_f2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void unpack_f2(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t add_f2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t sub_f2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t mul_f2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+// Two floats rounded (nearest-even) to T and packed: a in the low half.
 template <typename T>
-__device__ __forceinline__ void quant_row_smem(const float* src, int K, float s_math, int8_t* qr,
-                                               bool vec) {
-  const int t = threadIdx.x;
-  const float r_math = __frcp_rn(s_math);
-  if (vec && (reinterpret_cast<uintptr_t>(qr) % 8 == 0)) {
-    for (int i = t; i < (K >> 3); i += kQuantThreads) {
-      float y[8];
-      uint32_t w[2] = {0u, 0u};
+__device__ __forceinline__ uint32_t cvt_pair16(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t cvt_pair16<__nv_bfloat16>(float a, float b) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+  return r;
+}
+template <>
+__device__ __forceinline__ uint32_t cvt_pair16<__half>(float a, float b) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+  return r;
+}
+// Both 16-bit halves of a packed pair widened to float (exact).
+template <typename T>
+__device__ __forceinline__ void widen_pair16(uint32_t w, float& lo, float& hi) {
+  if constexpr (std::is_same<T, __half>::value) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w));
+    lo = f.x;
+    hi = f.y;
+  } else {
+    lo = __uint_as_float(w << 16);
+    hi = __uint_as_float(w & 0xFFFF0000u);
+  }
+}
+__device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
+// The radix-4 butterfly on packed pairs.  Outputs by digit:
+//   0: ((a0 + a1) + a2) - a3      1: ((a0 + a1) - a2) + a3
+//   2: ((a0 - a1) + a2) + a3      3: ((a1 - a0) + a2) + a3 = (a2 - (a0 - a1)) + a3
+// (a1 - a0 is exactly -(a0 - a1), and x + (-y) is exactly x - y.)
+__device__ __forceinline__ void butterfly4_f2(uint64_t& a0, uint64_t& a1, uint64_t& a2,
+                                              uint64_t& a3) {
+  const uint64_t s = add_f2(a0, a1), d = sub_f2(a0, a1);
+  const uint64_t o0 = sub_f2(add_f2(s, a2), a3);
+  const uint64_t o1 = add_f2(sub_f2(s, a2), a3);
+  const uint64_t o2 = add_f2(add_f2(d, a2), a3);
+  const uint64_t o3 = add_f2(sub_f2(a2, d), a3);
+  a0 = o0;
+  a1 = o1;
+  a2 = o2;
+  a3 = o3;
+}
+
+// One stage over register stride S (1 or 4) of 16 packed pairs: the quadruples
+// {b, b+S, b+2S, b+3S} with b's digit at S equal to 0.
+template <int S>
+__device__ __forceinline__ void radix4_stage16(uint64_t (&p)[16]) {
+  constexpr int kStep = S == 1 ? 4 : 1;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) y[j] = src[8 * i + j];
+  for (int i = 0; i < 4; ++i) {
+    const int b = i * kStep;
+    butterfly4_f2(p[b], p[b + S], p[b + 2 * S], p[b + 3 * S]);
+  }
+}
+
+// Elements e0 .. e0+15 of a row (zeros past K): x itself, or for SWIGLU the
+// activation of gate x[e] and up x[K + e].
+template <typename T, bool SWIGLU>
+__device__ __forceinline__ void load16(const T* __restrict__ xr, int K, int e0, bool vec,
+                                       float (&v)[16]) {
+  if (vec && e0 + 16 <= K) {
+    const uint4 w0 = __ldcs(reinterpret_cast<const uint4*>(xr + e0));
+    const uint4 w1 = __ldcs(reinterpret_cast<const uint4*>(xr + e0 + 8));
+    const uint32_t g[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    if constexpr (SWIGLU) {
+      const uint4 u0 = __ldcs(reinterpret_cast<const uint4*>(xr + K + e0));
+      const uint4 u1 = __ldcs(reinterpret_cast<const uint4*>(xr + K + e0 + 8));
+      const uint32_t u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        float d = __fmul_rn(y[j], r_math);
-        if (near_tie<T>(d)) d = __fdiv_rn(y[j], s_math);
-        d = fminf(fmaxf(rintf(round_to<T>(d)), -128.0f), 127.0f);
-        w[j >> 2] |= (static_cast<uint32_t>(static_cast<int>(d)) & 0xFFu) << (8 * (j & 3));
+        float g0, g1, u0f, u1f;
+        widen_pair16<T>(g[j], g0, g1);
+        widen_pair16<T>(u[j], u0f, u1f);
+        v[2 * j] = swiglu_bf16(g0, u0f);
+        v[2 * j + 1] = swiglu_bf16(g1, u1f);
       }
-      reinterpret_cast<uint2*>(qr)[i] = make_uint2(w[0], w[1]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) widen_pair16<T>(g[j], v[2 * j], v[2 * j + 1]);
     }
   } else {
-    for (int i = t; i < K; i += kQuantThreads) qr[i] = static_cast<int8_t>(quant_code<T>(src[i], s_math));
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int e = e0 + j;
+      float a = 0.0f;
+      if (e < K) {
+        if constexpr (SWIGLU) a = swiglu_bf16(to_float<T>(xr[e]), to_float<T>(xr[K + e]));
+        else a = to_float<T>(xr[e]);
+      }
+      v[j] = a;
+    }
   }
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kQuantThreads)
-    quant_rowwise_i8_rot_kernel(const T* __restrict__ x, int64_t ldx, int8_t* __restrict__ q,
-                                int64_t ldq, float* __restrict__ scales, int M, int K) {
-  extern __shared__ float rot_smem[];
-  float* bufa = rot_smem;
-  float* bufb = rot_smem + K;
-  __shared__ float red[kQuantThreads / 32];
-  __shared__ float bcast;
-  const int t = threadIdx.x;  // position inside every 256-wide group
-  const bool vec = (K % 8 == 0) && (ldx % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
-  for (int row = blockIdx.x; row < M; row += gridDim.x) {
-    const T* xr = x + static_cast<int64_t>(row) * ldx;
-    if (vec) {
-      for (int i = t; i < (K >> 3); i += kQuantThreads) {
-        const uint4 v = __ldcs(reinterpret_cast<const uint4*>(xr) + i);
-        const T* e = reinterpret_cast<const T*>(&v);
+__device__ __forceinline__ uint16_t bits16(float v) {
+  if constexpr (std::is_same<T, __half>::value) return __half_as_ushort(__float2half_rn(v));
+  else return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
+
+// Stores 16 values (natural layout: elements e0 + j) to `dst` (16-bit
+// elements), vectorized when whole and aligned.
+template <typename T>
+__device__ __forceinline__ void store16_natural(uint16_t* dst, int e0, int K, bool vec,
+                                                const float (&v)[16]) {
+  if (vec && e0 + 16 <= K) {
+    uint4* o = reinterpret_cast<uint4*>(dst + e0);
+    o[0] = make_uint4(cvt_pair16<T>(v[0], v[1]), cvt_pair16<T>(v[2], v[3]),
+                      cvt_pair16<T>(v[4], v[5]), cvt_pair16<T>(v[6], v[7]));
+    o[1] = make_uint4(cvt_pair16<T>(v[8], v[9]), cvt_pair16<T>(v[10], v[11]),
+                      cvt_pair16<T>(v[12], v[13]), cvt_pair16<T>(v[14], v[15]));
+  } else {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) bufa[8 * i + j] = to_float<T>(e[j]);
-      }
-    } else {
-      for (int i = t; i < K; i += kQuantThreads) bufa[i] = to_float<T>(xr[i]);
-    }
-    __syncthreads();
-    float* src = convrot_stages(bufa, bufb, K);
-    // src holds the unscaled rotation; scale by 2^-4 (exact), round to T once.
-    float amax = 0.0f;
-    for (int i = t; i < K; i += kQuantThreads) {
-      const float r = round_to<T>(src[i] * 0.0625f);
-      src[i] = r;
-      amax = fmaxf(amax, fabsf(r));
-    }
-    const float s_math = row_scale_from_absmax<T>(amax, red, &bcast, scales, row);
-    quant_row_smem<T>(src, K, s_math, q + static_cast<int64_t>(row) * ldq, vec && (ldq % 8 == 0));
-    __syncthreads();  // buffers and red/bcast are reused by the next row
+    for (int j = 0; j < 16; ++j)
+      if (e0 + j < K) dst[e0 + j] = bits16<T>(v[j]);
   }
 }
 
-// ------------------------------------------------------------ SwiGLU rows
-// One CTA per row (grid-stride) of a split-half [M, 2F] bf16 tensor x (gate =
-// columns [0, F), up = [F, 2F)):
-//   act = bf16(bf16(silu(gate)) * up)                       (silu_mul_split_bf16,
-//                                                            dit_kernels.mm:724-737)
-//   ROT:   act <- bf16(H256(act) * 2^-4) per 256-group     (i8_swiglu_rot_bf16,
-//                                                            int8_gemm.mm:1521-1555)
-//   QUANT: per-token INT8 codes + scale of act              (i8_quant_rowwise,
-//                                                            int8_gemm.mm:1337-1381)
-//   else:  act written to out [M, F] (bf16).
-// Shared memory: ROT 2F floats, QUANT without ROT F floats, neither none.
-template <bool ROT, bool QUANT>
-__global__ void __launch_bounds__(kQuantThreads)
-    swiglu_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int F,
-                       __nv_bfloat16* __restrict__ out, int64_t ldo, int8_t* __restrict__ q,
-                       int64_t ldq, float* __restrict__ scales, int M) {
-  extern __shared__ float rot_smem[];
-  float* bufa = rot_smem;
-  float* bufb = rot_smem + F;
-  __shared__ float red[kQuantThreads / 32];
+// ROT requires K % 256 == 0.  QUANT: codes q [M, K] (row stride ldq) + scales [M];
+// otherwise the 16-bit results go to out [M, K] (row stride ldo).  For SWIGLU, K
+// is F and x rows hold [gate | up] (row stride ldx >= 2F).
+template <typename T, bool SWIGLU, bool ROT, bool QUANT>
+__global__ void __launch_bounds__(kRowThreads)
+    rows_kernel(const T* __restrict__ x, int64_t ldx, int K, T* __restrict__ out, int64_t ldo,
+                int8_t* __restrict__ q, int64_t ldq, float* __restrict__ scales, int M) {
+  extern __shared__ __align__(16) uint8_t rows_smem[];
+  uint64_t* tr = reinterpret_cast<uint64_t*>(rows_smem);
+  uint32_t* pairbuf = reinterpret_cast<uint32_t*>(rows_smem + (ROT ? kTrBytes : 0));
+  uint16_t* rowbuf = reinterpret_cast<uint16_t*>(rows_smem + (ROT ? kTrBytes : 0));
+  __shared__ float red[kRowThreads / 32];
   __shared__ float bcast;
-  constexpr bool kSmem = ROT || QUANT;
-  const int t = threadIdx.x;
-  const bool vec = (F % 8 == 0) && (ldx % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
-  const bool vec_out = !kSmem && vec && (ldo % 8 == 0) && (reinterpret_cast<uintptr_t>(out) % 16 == 0);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int half = lane >> 4, l = lane & 15;
+  uint64_t* mytr = tr + (warp * 2 + half) * kTrPairsPerHalf;
+  const int ngroups = (K + kRotGroup - 1) / kRotGroup;
+  const int npairs = (ngroups + 1) >> 1;
+  const bool vec = (K % 8 == 0) && (ldx % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
+  const bool vec_out = (K % 8 == 0) && (ldo % 8 == 0) && (reinterpret_cast<uintptr_t>(out) % 16 == 0);
+  const uint64_t k2m4 = pack_f2(0.0625f, 0.0625f);
   for (int row = blockIdx.x; row < M; row += gridDim.x) {
-    const __nv_bfloat16* xr = x + static_cast<int64_t>(row) * ldx;
-    __nv_bfloat16* orow = out + static_cast<int64_t>(row) * ldo;
-    if (vec) {
-      for (int i = t; i < (F >> 3); i += kQuantThreads) {
-        const uint4 gv = __ldcs(reinterpret_cast<const uint4*>(xr) + i);
-        const uint4 uv = __ldcs(reinterpret_cast<const uint4*>(xr + F) + i);
-        const __nv_bfloat16* ge = reinterpret_cast<const __nv_bfloat16*>(&gv);
-        const __nv_bfloat16* ue = reinterpret_cast<const __nv_bfloat16*>(&uv);
-        float a[8];
+    const T* xr = x + static_cast<int64_t>(row) * ldx;
+    uint16_t* orow = reinterpret_cast<uint16_t*>(out) + static_cast<int64_t>(row) * ldo;
+    float amax = 0.0f;
+    uint32_t amax2 = 0u;  // packed 16-bit magnitudes (ROT)
+    // warp iteration: group pairs gp0, gp0 + 1; half h takes pair gp = gp0 + h,
+    // i.e. groups A = 2gp and B = 2gp + 1
+    for (int gp0 = 2 * warp; gp0 < npairs; gp0 += 2 * (kRowThreads / 32)) {
+      const int gp = gp0 + half;
+      const int ga = 2 * gp, gb = ga + 1;
+      const bool act_a = ga < ngroups, act_b = gb < ngroups;
+      float va[16], vb[16];
+      if (act_a) load16<T, SWIGLU>(xr, K, ga * kRotGroup + 16 * l, vec, va);
+      else {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) a[j] = swiglu_bf16(__bfloat162float(ge[j]), __bfloat162float(ue[j]));
-        if constexpr (kSmem) {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) bufa[8 * i + j] = a[j];
-        } else if (vec_out) {
-          reinterpret_cast<uint4*>(orow)[i] =
-              make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]), pack_bf16x2(a[4], a[5]),
-                         pack_bf16x2(a[6], a[7]));
-        } else {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) orow[8 * i + j] = __float2bfloat16_rn(a[j]);
-        }
+        for (int j = 0; j < 16; ++j) va[j] = 0.0f;
       }
-    } else {
-      for (int i = t; i < F; i += kQuantThreads) {
-        const float a = swiglu_bf16(__bfloat162float(xr[i]), __bfloat162float(xr[F + i]));
-        if constexpr (kSmem) bufa[i] = a;
-        else orow[i] = __float2bfloat16_rn(a);
+      if (act_b) load16<T, SWIGLU>(xr, K, gb * kRotGroup + 16 * l, vec, vb);
+      else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) vb[j] = 0.0f;
+      }
+      if constexpr (ROT) {
+        uint64_t p[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) p[j] = pack_f2(va[j], vb[j]);
+        radix4_stage16<1>(p);  // stride 1: digit 0 = j & 3
+        radix4_stage16<4>(p);  // stride 4: digit 1 = j >> 2
+        __syncwarp();          // this half's previous reads of mytr are done
+#pragma unroll
+        for (int j = 0; j < 16; j += 2)
+          *reinterpret_cast<uint4*>(mytr + l * kTrPitch + j) =
+              make_uint4(static_cast<uint32_t>(p[j]), static_cast<uint32_t>(p[j] >> 32),
+                         static_cast<uint32_t>(p[j + 1]), static_cast<uint32_t>(p[j + 1] >> 32));
+        __syncwarp();
+#pragma unroll
+        for (int t = 0; t < 16; ++t) p[t] = mytr[t * kTrPitch + l];  // element 16t + l
+        radix4_stage16<1>(p);  // stride 16: digit 2 = t & 3
+        radix4_stage16<4>(p);  // stride 64: digit 3 = t >> 2
+#pragma unroll
+        for (int t = 0; t < 16; ++t) {
+          float a, b;
+          unpack_f2(mul_f2(p[t], k2m4), a, b);  // * 2^-4, exact
+          const uint32_t w = cvt_pair16<T>(a, b);
+          amax2 = max_u16x2(amax2, w & 0x7FFF7FFFu);
+          const int e = 16 * t + l;
+          if constexpr (QUANT) {
+            if (act_a) pairbuf[gp * kPairPitch + e] = w;  // gp < npairs
+          } else {
+            if (act_a) orow[ga * kRotGroup + e] = static_cast<uint16_t>(w & 0xFFFFu);
+            if (act_b) orow[gb * kRotGroup + e] = static_cast<uint16_t>(w >> 16);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fmaxf(fabsf(va[j]), fabsf(vb[j])));
+        uint16_t* dst = QUANT ? rowbuf : orow;
+        const bool v16 = QUANT ? true : vec_out;
+        if (act_a) store16_natural<T>(dst, ga * kRotGroup + 16 * l, K, v16, va);
+        if (act_b) store16_natural<T>(dst, gb * kRotGroup + 16 * l, K, v16, vb);
       }
     }
-    if constexpr (kSmem) {
-      __syncthreads();
-      float* src = bufa;
+    if constexpr (QUANT) {
       if constexpr (ROT) {
-        src = convrot_stages(bufa, bufb, F);
-        for (int i = t; i < F; i += kQuantThreads) src[i] = round_bf16(src[i] * 0.0625f);
+        float lo, hi;
+        widen_pair16<T>(amax2, lo, hi);
+        amax = fmaxf(lo, hi);
       }
-      if constexpr (QUANT) {
-        float amax = 0.0f;
-        for (int i = t; i < F; i += kQuantThreads) amax = fmaxf(amax, fabsf(src[i]));
-        const float s_math = row_scale_from_absmax<__nv_bfloat16>(amax, red, &bcast, scales, row);
-        quant_row_smem<__nv_bfloat16>(src, F, s_math, q + static_cast<int64_t>(row) * ldq,
-                                      (F % 8 == 0) && (ldq % 8 == 0));
+      // (the reduction's barrier also publishes the row buffer to the whole CTA)
+      const float s_math = row_scale_from_absmax<T>(amax, red, &bcast, scales, row);
+      const float r_math = __frcp_rn(s_math);
+      int8_t* qr = q + static_cast<int64_t>(row) * ldq;
+      if constexpr (ROT) {
+        // 4 positions of a group pair per step: codes of A and of B
+        const bool q4 = (ldq % 4 == 0) && (reinterpret_cast<uintptr_t>(q) % 4 == 0);
+        for (int c = threadIdx.x; c < npairs * (kRotGroup / 4); c += kRowThreads) {
+          const int gp = c / (kRotGroup / 4), e0 = (c % (kRotGroup / 4)) * 4;
+          const uint4 w = *reinterpret_cast<const uint4*>(pairbuf + gp * kPairPitch + e0);
+          float xa[4], xb[4];
+          widen_pair16<T>(w.x, xa[0], xb[0]);
+          widen_pair16<T>(w.y, xa[1], xb[1]);
+          widen_pair16<T>(w.z, xa[2], xb[2]);
+          widen_pair16<T>(w.w, xa[3], xb[3]);
+          const uint32_t ca = quant4_fast<T>(xa, s_math, r_math);
+          const int ea = 2 * gp * kRotGroup + e0;
+          if (q4) reinterpret_cast<uint32_t*>(qr + ea)[0] = ca;
+          else for (int i = 0; i < 4; ++i) qr[ea + i] = static_cast<int8_t>(ca >> (8 * i));
+          if (2 * gp + 1 < ngroups) {
+            const uint32_t cb = quant4_fast<T>(xb, s_math, r_math);
+            if (q4) reinterpret_cast<uint32_t*>(qr + ea + kRotGroup)[0] = cb;
+            else for (int i = 0; i < 4; ++i) qr[ea + kRotGroup + i] = static_cast<int8_t>(cb >> (8 * i));
+          }
+        }
+      } else if ((K % 8 == 0) && (ldq % 8 == 0) && (reinterpret_cast<uintptr_t>(q) % 8 == 0)) {
+        for (int i = threadIdx.x; i < (K >> 3); i += kRowThreads)
+          reinterpret_cast<uint2*>(qr)[i] =
+              quant8_fast<T>(reinterpret_cast<const uint4*>(rowbuf)[i], s_math, r_math);
       } else {
-        for (int i = t; i < F; i += kQuantThreads) orow[i] = __float2bfloat16_rn(src[i]);
+        for (int i = threadIdx.x; i < K; i += kRowThreads) {
+          const float v = std::is_same<T, __half>::value
+                              ? __half2float(__ushort_as_half(rowbuf[i]))
+                              : __uint_as_float(static_cast<uint32_t>(rowbuf[i]) << 16);
+          qr[i] = static_cast<int8_t>(quant_code<T>(v, s_math));
+        }
       }
-      __syncthreads();  // buffers and red/bcast are reused by the next row
+      __syncthreads();  // row buffers, red and bcast are reused by the next row
     }
   }
 }

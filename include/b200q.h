@@ -80,7 +80,7 @@ B200Q_API int b200q_quant_rowwise_i8(const void* x, int x_dtype, int64_t M, int6
  * the latter, so like it the result can differ from the eager bf16 Hadamard
  * matmul by a last-ulp rotation flip on rare ties.  groupsize must be 256 and
  * K a multiple of it, K <= B200Q_CONVROT_MAX_K (B200Q_ERR_UNSUPPORTED otherwise). */
-#define B200Q_CONVROT_MAX_K 28672
+#define B200Q_CONVROT_MAX_K 65536
 B200Q_API int b200q_quant_rowwise_i8_convrot(const void* x, int x_dtype, int64_t M, int64_t K,
                                              int64_t ldx, int groupsize, int8_t* q, int64_t ldq,
                                              float* scales, void* stream);
@@ -166,7 +166,7 @@ B200Q_API int b200q_rms_rope_partial(void* q, void* k, const void* freqs, const 
  * exp correctly rounded.  The convrot variants rotate every 256-wide group of
  * act (radix-4 Hadamard butterflies in fp32, then * 2^-4 and one bf16 rounding),
  * exactly as b200q_quant_rowwise_i8_convrot does for a plain activation. */
-#define B200Q_SWIGLU_MAX_F 28672
+#define B200Q_SWIGLU_MAX_F 65536
 
 /* act [M, F] of a wide tensor (row stride ldx >= 2F).  Replaces silu_mul_split
  * (_patches/dit_ext/dit_kernels.mm:724-737) behind _swiglu_activation

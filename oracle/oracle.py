@@ -120,6 +120,40 @@ def rotate_convrot(x, groupsize=256):
     return from_f32(rnd(y.astype(np.float32)), x.dtype).reshape(shp)
 
 
+def rotate_convrot_fwht(x, groupsize=256):
+    """The reference's own fp32 evaluation of the convrot rotation (the fast
+    Walsh-Hadamard butterflies of i8_swiglu_rot_bf16 and i8_merge_rot_quant,
+    _patches/int8_ext/int8_gemm.mm:1533-1553 and :1463-1479): per 256-group, four
+    radix-4 stages with strides 1, 4, 16, 64; at each stage the element with
+    base-4 digit d (of its index, at that stride) becomes, in fp32 with this
+    association,
+        d=0: ((a0 + a1) + a2) - a3      d=1: ((a0 + a1) - a2) + a3
+        d=2: ((a0 - a1) + a2) + a3      d=3: ((a1 - a0) + a2) + a3
+    where a0..a3 are the four elements of its butterfly; finally * 2^-4 (exact)
+    and one rounding to x.dtype.  Differs from rotate_convrot's single rounding
+    of the exact product only where fp32 sums round across a last-ulp tie."""
+    if groupsize != 256:
+        raise ValueError("convrot groupsize 256 only (the reference's fused kernels)")
+    rnd, _ = _rounder(x.dtype)
+    shp = x.shape
+    w = to_f32(x.reshape(-1, shp[-1]))
+    K = w.shape[1]
+    if K % groupsize:
+        raise ValueError("K must be a multiple of the convrot groupsize")
+    w = w.reshape(-1, K // groupsize, groupsize)
+    for stride in (1, 4, 16, 64):
+        v = w.reshape(w.shape[0], w.shape[1], groupsize // (4 * stride), 4, stride)
+        a0, a1, a2, a3 = v[..., 0, :], v[..., 1, :], v[..., 2, :], v[..., 3, :]
+        out = np.empty_like(v)
+        out[..., 0, :] = ((a0 + a1) + a2) - a3
+        out[..., 1, :] = ((a0 + a1) - a2) + a3
+        out[..., 2, :] = ((a0 - a1) + a2) + a3
+        out[..., 3, :] = ((a1 - a0) + a2) + a3
+        w = out.reshape(w.shape)
+    y = (w.reshape(-1, K) * np.float32(0.0625)).astype(np.float32)
+    return from_f32(rnd(y), x.dtype).reshape(shp)
+
+
 def quantize_int8_rowwise_convrot(x, groupsize=256):
     """Convrot rotation then per-token INT8 quant (_quant_cached,
     _patches/int8_linear_kernel_mps.py:97-140)."""
@@ -435,8 +469,9 @@ def swiglu(wide):
 
 def swiglu_rot(wide):
     """i8_swiglu_rot (_patches/int8_ext/int8_gemm.mm:1521-1555): the 256-group
-    convrot rotation of swiglu(wide), bf16."""
-    return rotate_convrot(swiglu(wide))
+    convrot rotation of swiglu(wide) with the reference kernel's fp32
+    butterflies, bf16."""
+    return rotate_convrot_fwht(swiglu(wide))
 
 
 def swiglu_quant(wide, rotate=True):
@@ -462,5 +497,5 @@ def mlp_bridge_prequant(a, w, row_scale, col_scale, bias=None, rotate=True):
     FC2 input (q, scale) of FC1 -> SwiGLU -> convrot -> rowwise quant."""
     act = fc1_swiglu(a, w, row_scale, col_scale, bias)
     if rotate:
-        act = rotate_convrot(act)
+        act = rotate_convrot_fwht(act)
     return quantize_int8_rowwise(act)

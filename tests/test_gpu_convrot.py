@@ -1,16 +1,15 @@
 """GPU parity of the convrot rotation fused into the per-token INT8 quant
-(b200q_quant_rowwise_i8_convrot; SURVEY 8f rank 1).
+(b200q_quant_rowwise_i8_convrot).
 
-The oracle rotates exactly (float64, one rounding to the input dtype) with the
-Hadamard restated from the reference's fused kernel (int8_gemm.mm:1417-1480)
-and then applies the bit-exact rowwise quant.  The kernel sums in fp32 in the
-reference kernel's butterfly order, so -- exactly as the reference's own test of
-its fused rotate+quant kernel states (tests/test_int8_linear_kernel.py:932-975)
--- a rotated value can flip its last bf16 ulp on a rare tie, moving one code by
-1 or, via a flipped row absmax, a row's scale by ~2^-8.  The bounds below are
-that test's: scale rel diff < 6e-3, |code diff| <= 1, code mismatch fraction
-< 5e-3.  In practice the codes agree almost everywhere, which is also asserted
-(fraction of rows with identical scales >= 99%).
+Two oracles.  (1) The reference kernel's own fp32 butterflies, restated
+(oracle.rotate_convrot_fwht, int8_gemm.mm:1463-1479): codes and scales must be
+bit-identical.  (2) comfy's semantics, the exact rotation rounded once
+(oracle.rotate_convrot): the fp32 sums can flip a rotated value's last bf16
+ulp on a rare tie, moving one code by 1 or, via a flipped row absmax, a row's
+scale by ~2^-8; the bounds are those of the reference's own test of its fused
+rotate+quant kernel (tests/test_int8_linear_kernel.py:932-975): scale rel diff
+< 6e-3, |code diff| <= 1, code mismatch fraction < 5e-3 (and >= 99% of rows
+with identical scales).
 """
 import pytest
 import torch
@@ -24,6 +23,12 @@ DEV = "cuda"
 
 def _gen(seed):
     return torch.Generator().manual_seed(seed)
+
+
+def _check_fwht_exact(q, s, x):
+    q_ref, s_ref = oracle.quantize_int8_rowwise(oracle.rotate_convrot_fwht(x))
+    assert torch.equal(s.cpu(), s_ref)
+    assert torch.equal(q.cpu(), q_ref)
 
 
 def _check_codes(q, s, q_ref, s_ref):
@@ -45,6 +50,7 @@ def test_convrot_quant_matches_oracle(native, M, K):
     q, s = native.quant_rowwise_i8_convrot(x.to(DEV))
     torch.cuda.synchronize()
     _check_codes(q, s, q_ref, s_ref)
+    _check_fwht_exact(q, s, x)
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
@@ -58,6 +64,7 @@ def test_convrot_quant_outliers_fp16_strided(native, dtype):
     q_ref, s_ref = oracle.quantize_int8_rowwise_convrot(xs.contiguous())
     q, s = native.quant_rowwise_i8_convrot(x.to(DEV)[:, 128:128 + K])
     _check_codes(q, s, q_ref, s_ref)
+    _check_fwht_exact(q, s, xs.contiguous())
 
 
 def test_convrot_rejects_unsupported_groups(native):
@@ -91,3 +98,6 @@ def test_convrot_linear_through_the_seam(native):
     assert torch.equal(out[same_rows], ref[same_rows])
     rel = ((out.float() - ref.float()).abs().max() / ref.float().abs().max()).item()
     assert rel < 0.02
+    # against the reference kernel's own fp32 butterflies: identical everywhere
+    ref_fwht = oracle.int8_linear(oracle.rotate_convrot_fwht(x), w, ws, b)
+    assert torch.equal(out, ref_fwht)

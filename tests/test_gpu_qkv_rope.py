@@ -1,5 +1,5 @@
 """GPU parity of the QKV attention-layout epilogue and the in-place Q/K
-RMSNorm + split-half RoPE (SURVEY 8f rank 2).
+RMSNorm + split-half RoPE.
 
 * The QKV epilogue only changes storage: its q, k, v must equal the dense
   [M, 3HD] fused_cs output split and permuted to [B, H, S, D], byte for byte

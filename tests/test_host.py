@@ -389,3 +389,9 @@ def test_int8_fast_hook_patches_module(monkeypatch):
     x, w, ws = torch.zeros(2, 4), torch.zeros(3, 4, dtype=torch.int8), torch.ones(1)
     assert mod.int8_forward_dynamic(x, w, ws, None, torch.bfloat16) == "dyn"
     assert mod.int8_forward_dynamic_per_row(x, w, ws, None, torch.bfloat16) == "dyn_pr"
+
+
+def test_abi_limits_match_the_bindings():
+    hdr = open(os.path.join(ROOT, "include", "b200q.h")).read()
+    assert f"#define B200Q_CONVROT_MAX_K {_native.CONVROT_MAX_K}" in hdr
+    assert f"#define B200Q_SWIGLU_MAX_F {_native.SWIGLU_MAX_F}" in hdr
