@@ -113,7 +113,16 @@ def _base_spec(name):
         return dict(route="w8a16", M=4096, seed=1, hidden=3072,
                     layers=[Layer("up", 3072, 12288, "gelu_tanh")], inputs=["x"],
                     desc="FP8 W8A16 linear (BASELINE config 2)")
+    if name == "h3mlp":
+        return dict(route="mlp", M=5378, seed=5, hidden=5376, layers=[
+            Layer("fc1", 5376, 28672, "swiglu"), Layer("fc2", 14336, 5376)], inputs=["x"],
+            desc="MiniMax H3 MLP, INT8: FC1 with SwiGLU in the epilogue -> convrot quant -> FC2 "
+                 "(the reference's fc2 SwiGLU fast-path shape [5378,28672]->[5378,5376])")
     raise SystemExit(f"unknown workload {name}")
+
+
+def _unit(spec):
+    return "TOP/s" if spec["route"] in ("int8", "mlp") else "TFLOP/s"
 
 
 def _flops(spec, M):
@@ -133,7 +142,7 @@ class B200Block:
         for l in spec["layers"]:
             w = torch.randn((l.N, l.K), generator=g, device=dev, dtype=torch.float32) * 0.02
             b = (torch.randn((l.N,), generator=g, device=dev) * 0.01).to(torch.bfloat16)
-            if spec["route"] == "int8":
+            if spec["route"] in ("int8", "mlp"):
                 s = (w.abs().amax(dim=1) / 127.0).clamp_min(1e-30)
                 q = torch.clamp(torch.round(w / s[:, None]), -128, 127).to(torch.int8)
                 self.weights.append((q, s.float().contiguous(), b))
@@ -148,7 +157,7 @@ class B200Block:
         for key in sorted(set(spec["inputs"])):
             K0 = spec["layers"][0].K
             x = torch.randn((M, K0), generator=gx, device=dev, dtype=torch.bfloat16)
-            if spec["route"] == "int8":
+            if spec["route"] in ("int8", "mlp"):
                 n_out = spec.get("outliers", max(1, round(K0 / 100)))
                 idx = torch.randperm(K0, generator=gx, device=dev)[:n_out]
                 x[:, idx] *= 20
@@ -162,6 +171,8 @@ class B200Block:
         spec = self.spec
         outs = []
         h = None
+        if spec["route"] == "mlp":
+            return self._mlp_step(inputs, record)
         for i, (l, (w, s, b)) in enumerate(zip(spec["layers"], self.weights)):
             x = inputs[spec["inputs"][i]] if i < len(spec["inputs"]) else h
             if spec["route"] == "fp8" and self.fused:
@@ -191,6 +202,22 @@ class B200Block:
             h = y
         return outs
 
+    def _mlp_step(self, inputs, record):
+        """FC1 -> SwiGLU -> convrot -> FC2 (the i8_mlp_bridge_prequant route: its two
+        launches, FC1 with the SwiGLU epilogue and the convrot quant of act, are
+        issued as their ops here so that each GEMM is timed on its own)."""
+        ops = torch.ops.b200q
+        (l1, l2), ((w1, s1, b1), (w2, s2, b2)) = self.spec["layers"], self.weights
+        xq, xs = ops.quant_rowwise_i8(inputs["x"])
+        ev = self._ev(record)
+        act = ops.i8_matmul_nt_fused_cs_swiglu(xq, w1, xs, s1, b1)
+        self._ev_end(ev, record, l1)
+        q2, s2a = ops.quant_rowwise_i8_convrot(act, 256)
+        ev = self._ev(record)
+        y = ops.i8_matmul_nt_fused_cs(q2, w2, s2a, s2, b2, torch.bfloat16)
+        self._ev_end(ev, record, l2)
+        return [y]
+
     def build_graphs(self, inputs):
         """Captures every op of one step as its own CUDA graph over static buffers.
         Returns [(graph, gemm_flops)] in execution order (flops 0 for quant ops) and
@@ -208,6 +235,19 @@ class B200Block:
                 out = fn()
             return g, out
 
+        if spec["route"] == "mlp":
+            (l1, l2), ((w1, s1, b1), (w2, s2, b2)) = spec["layers"], self.weights
+            x = inputs["x"]
+            g, (xq, xs) = capture(lambda: ops.quant_rowwise_i8(x))
+            seq.append((g, 0.0))
+            g, act = capture(lambda: ops.i8_matmul_nt_fused_cs_swiglu(xq, w1, xs, s1, b1))
+            seq.append((g, 2.0 * self.M * l1.K * l1.N))
+            g, (q2, s2a) = capture(lambda: ops.quant_rowwise_i8_convrot(act, 256))
+            seq.append((g, 0.0))
+            g, y = capture(lambda: ops.i8_matmul_nt_fused_cs(q2, w2, s2a, s2, b2, torch.bfloat16))
+            seq.append((g, 2.0 * self.M * l2.K * l2.N))
+            self.graph_outs.append(y)
+            return seq, _native.launch_count() - n0
         for i, (l, (w, s, b)) in enumerate(zip(spec["layers"], self.weights)):
             x = inputs[spec["inputs"][i]] if i < len(spec["inputs"]) else h
             flops = 2.0 * self.M * l.K * l.N
@@ -395,7 +435,7 @@ def run_b200q(args):
     value = total_flops * args.steps / (t_dev / 1e3) / 1e12
     e2e = total_flops * e2e_steps / (t_e2e / 1e3) / 1e12
     peaks = _peaks()
-    eight_bit = spec["route"] in ("fp8", "int8")
+    eight_bit = spec["route"] in ("fp8", "int8", "mlp")
     peak = (2.0 if eight_bit else 1.0) * peaks["bf16_sustained"]
     achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None
     # W8A16 with <= 256 tokens is bound by the FP8 weight stream (an HBM
@@ -413,20 +453,23 @@ def run_b200q(args):
         clocks = clk.summary()
         line = {
             "metric": "INT8/FP8 linear TOPS and % of tensor-core peak at 1/2/4/8 B200",
-            "value": round(value, 2), "unit": "TFLOP/s" if spec["route"] != "int8" else "TOP/s",
+            "value": round(value, 2), "unit": _unit(spec),
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(t_dev / args.steps, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None,
-            "dtype": {"fp8": "e4m3", "int8": "int8", "w8a16": "e4m3xbf16"}[spec["route"]],
+            "dtype": {"fp8": "e4m3", "int8": "int8", "mlp": "int8", "w8a16": "e4m3xbf16"}[spec["route"]],
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights; BASELINE shapes)",
             "config": {"workload": f"{args.workload}: {spec['desc']}", "M_total": spec["M"],
                        "M_per_rank": M, "layers": [(l.name, l.K, l.N, l.act) for l in spec["layers"]],
                        "parallelism": f"token-rows split over {world} rank(s), weights replicated, no collective",
                        "l2": "flushed (256 MB write) between timed steps, outside the events",
-                       "activation_quant": ({"fused": "inside each GEMM launch (quant prologue; fp8: "
-                                                      "+1 amax-reduction launch per linear)",
-                                             "separate": "own launch(es) before each GEMM"}[args.prologue]
-                                            if spec["route"] != "w8a16" else "none (weight-only)"),
+                       "activation_quant": (
+                           "FC1 input: own launch; FC2 input: SwiGLU in FC1's epilogue, then one "
+                           "convrot + per-token quant launch" if spec["route"] == "mlp" else
+                           {"fused": "inside each GEMM launch (quant prologue; fp8: "
+                                     "+1 amax-reduction launch per linear)",
+                            "separate": "own launch(es) before each GEMM"}[args.prologue]
+                           if spec["route"] != "w8a16" else "none (weight-only)"),
                        "launch": ("each op of the step captured once as a CUDA graph, replayed per step"
                                   if args.launch == "graph" else "eager torch.ops calls")},
             "roofline": ({"bound": "hbm", "achieved": round(achieved_gbs, 1) if achieved_gbs else None,
@@ -445,12 +488,14 @@ def run_b200q(args):
                          "frac": round(achieved / peak, 4) if achieved else None,
                          "traffic": traffic, "traffic_source": traffic_src,
                          "algorithmic_flops_per_launch": (round(gemm_flops / n_gemm) if n_gemm else None),
-                         "kernel": "gemm8_tc_kernel" if eight_bit else "w8a16_tc_kernel",
+                         "kernel": ("gemm8_tc2_kernel (FC1: SwiGLU epilogue; FC2: channelwise dequant)"
+                                    if spec["route"] == "mlp" else
+                                    "gemm8_tc_kernel" if eight_bit else "w8a16_tc_kernel"),
                          "peak_source": (f"{'2 x ' if eight_bit else ''}bf16_tflops_sustained of "
                                          f"{peaks['source']} MEASURED_PEAKS.json"
                                          + (" (dense FP8/INT8 rate = 2 x BF16 on B200)" if eight_bit else "")),
                          "gemm_launches_timed": n_gemm}),
-            "e2e": {"value": round(e2e, 3), "unit": "TFLOP/s" if spec["route"] != "int8" else "TOP/s",
+            "e2e": {"value": round(e2e, 3), "unit": _unit(spec),
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                     "steps": e2e_steps},
             "gpu_launches": int(launches_max),
@@ -486,6 +531,8 @@ def cpu_baseline(spec, args, rows=None):
     ops_total = 0.0
     elapsed = 0.0
     h = None
+    if spec["route"] == "mlp":
+        return _cpu_mlp(spec, args, rows, threads, g)
     for i, l in enumerate(spec["layers"]):
         if h is not None and i >= len(spec["inputs"]):
             x = h
@@ -510,10 +557,33 @@ def cpu_baseline(spec, args, rows=None):
         ops_total += 2.0 * rows * l.K * l.N
         h = y
     return {"value": round(ops_total / elapsed / 1e12, 5),
-            "unit": "TFLOP/s" if spec["route"] != "int8" else "TOP/s",
+            "unit": _unit(spec),
             "cores": threads, "kind": "port",
             "sample": f"{rows} token rows through every layer of {args.workload} (oracle port of the "
                       f"reference fallback: numpy/torch CPU), weight prep untimed"}
+
+
+def _cpu_mlp(spec, args, rows, threads, g):
+    """The oracle port of the reference's materialised MLP route on a row sample:
+    eager INT8 FC1 -> SwiGLU -> fp32 convrot butterflies -> rowwise quant -> INT8
+    GEMM -> dequant."""
+    from oracle import oracle
+    (l1, l2) = spec["layers"]
+    x = torch.randn(rows, l1.K, generator=g).to(torch.bfloat16)
+    w1q, s1 = oracle.quantize_weight_int8_per_channel(torch.randn(l1.N, l1.K, generator=g) * 0.02)
+    w2q, s2 = oracle.quantize_weight_int8_per_channel(torch.randn(l2.N, l2.K, generator=g) * 0.02)
+    b1 = (torch.randn(l1.N, generator=g) * 0.01).to(torch.bfloat16)
+    b2 = (torch.randn(l2.N, generator=g) * 0.01).to(torch.bfloat16)
+    t = time.perf_counter()
+    wide = oracle.int8_linear(x, w1q, s1, b1)
+    q, xs = oracle.quantize_int8_rowwise(oracle.rotate_convrot_fwht(oracle.swiglu(wide)))
+    oracle.int8_dequant_epilogue(oracle.int_mm(q, w2q.t()), xs, s2, b2)
+    elapsed = time.perf_counter() - t
+    ops_total = 2.0 * rows * (l1.K * l1.N + l2.K * l2.N)
+    return {"value": round(ops_total / elapsed / 1e12, 5), "unit": _unit(spec),
+            "cores": threads, "kind": "port",
+            "sample": f"{rows} token rows through FC1 -> SwiGLU -> convrot -> FC2 of {args.workload} "
+                      f"(oracle port of the reference's materialised route), weight prep untimed"}
 
 
 def run_reference(args):
@@ -532,21 +602,21 @@ def run_reference(args):
     value = statistics.mean(vals)
     line = {
         "metric": "INT8/FP8 linear TOPS and % of tensor-core peak at 1/2/4/8 B200",
-        "value": round(value, 5), "unit": "TFLOP/s" if spec["route"] != "int8" else "TOP/s",
+        "value": round(value, 5), "unit": _unit(spec),
         "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(wall / max(1, args.steps) * 1e3, 2), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None,
-        "dtype": {"fp8": "e4m3", "int8": "int8", "w8a16": "e4m3xbf16"}[spec["route"]],
+        "dtype": {"fp8": "e4m3", "int8": "int8", "mlp": "int8", "w8a16": "e4m3xbf16"}[spec["route"]],
         "data": "synthetic (seeded; BASELINE shapes, bounded row sample per step)",
         "config": {"workload": f"{args.workload}: {spec['desc']}", "M_total": spec["M"],
                    "sample_rows": args.cpu_rows},
         "cpu_baseline": {"value": round(value, 5),
-                         "unit": "TFLOP/s" if spec["route"] != "int8" else "TOP/s",
+                         "unit": _unit(spec),
                          "cores": os.cpu_count(), "kind": "port",
                          "sample": f"{args.cpu_rows} token rows per step through every layer; the "
                                    f"reference's kernels are Metal (Apple GPU) and do not build here, so "
                                    f"its CPU path is the oracle port of its fallback semantics"},
-        "e2e": {"value": round(value, 5), "unit": "TFLOP/s" if spec["route"] != "int8" else "TOP/s",
+        "e2e": {"value": round(value, 5), "unit": _unit(spec),
                 "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -557,7 +627,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--workload", default="c5", choices=["c1", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--workload", default="c5", choices=["c1", "c2", "c3", "c4", "c5", "h3mlp"])
     ap.add_argument("--m", type=int, default=None, help="override the workload's total token count M")
     ap.add_argument("--launch", default="graph", choices=["graph", "eager"],
                     help="replay per-op CUDA graphs (default) or call the torch ops eagerly")

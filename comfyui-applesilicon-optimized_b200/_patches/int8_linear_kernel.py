@@ -62,6 +62,32 @@ class _NativeInt8Kernel:
         return torch.ops.b200q.i8_matmul_nt_fused_cs(a, b, row_scale, col_scale, bias, out_dtype)
 
     @staticmethod
+    def i8_matmul2d_nt_fused_cs_half(a, b, row_scale, col_scale, bias=None):
+        """FP16 two-rounding epilogue (int8_gemm.mm:1965-2024), with the reference
+        host's argument checks (contiguous 2-D int8 operands, float32 scales of M
+        and N elements on the device, M, N, K > 0)."""
+        for t in (a, b, row_scale, col_scale):
+            if not isinstance(t, torch.Tensor) or t.device.type != "cuda":
+                raise RuntimeError("inputs must be on cuda")
+        if a.dtype != torch.int8 or b.dtype != torch.int8 or a.dim() != 2 or b.dim() != 2:
+            raise RuntimeError("a/b must be 2D int8")
+        if a.shape[1] != b.shape[1]:
+            raise RuntimeError("K mismatch: A[M,K], B[N,K]")
+        if not (a.is_contiguous() and b.is_contiguous()):
+            raise RuntimeError("a/b must be contiguous")
+        if (row_scale.dtype != torch.float32 or col_scale.dtype != torch.float32
+                or not row_scale.is_contiguous() or not col_scale.is_contiguous()):
+            raise RuntimeError("row_scale / col_scale must be contiguous float32")
+        if row_scale.numel() != a.shape[0] or col_scale.numel() != b.shape[0]:
+            raise RuntimeError("row_scale must have M and col_scale N elements")
+        if a.shape[0] <= 0 or b.shape[0] <= 0 or a.shape[1] <= 0:
+            raise RuntimeError("matrix dimensions must be positive")
+        if bias is not None and (bias.device.type != "cuda" or bias.numel() != b.shape[0]):
+            raise RuntimeError("bias must be N cuda elements")
+        return torch.ops.b200q.i8_matmul_nt_fused_cs(a, b, row_scale, col_scale, bias,
+                                                      torch.float16)
+
+    @staticmethod
     def i8_swiglu_rot(x):
         return torch.ops.b200q.i8_swiglu_rot(x)
 
@@ -128,9 +154,16 @@ def _quant_cached(x, convrot, convrot_groupsize):
 
 
 def _int8_linear_prequant(x_8, x_scale, weight, weight_scale, bias, out_dtype, input_shape):
-    """Epilogue selection of int8_linear_kernel_mps.py:152-215."""
+    """Epilogue selection of int8_linear_kernel_mps.py:152-215 (fp16 outputs first
+    offered to the Wan fp16 hook, :157-162)."""
     weight_scale = weight_scale.reshape(-1)
     N = weight.shape[0]
+    if out_dtype == torch.float16:
+        from . import wan_fp16
+        result = wan_fp16.maybe_prequant(_kernel, x_8, x_scale, weight, weight_scale, bias,
+                                         input_shape)
+        if result is not None:
+            return result
     if out_dtype in (torch.bfloat16, torch.float16) and weight_scale.numel() in (1, N):
         if out_dtype == torch.bfloat16 and weight_scale.numel() == 1:
             row_scale = (weight_scale.float() * x_scale.reshape(-1).float()).contiguous()

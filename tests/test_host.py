@@ -395,3 +395,24 @@ def test_abi_limits_match_the_bindings():
     hdr = open(os.path.join(ROOT, "include", "b200q.h")).read()
     assert f"#define B200Q_CONVROT_MAX_K {_native.CONVROT_MAX_K}" in hdr
     assert f"#define B200Q_SWIGLU_MAX_F {_native.SWIGLU_MAX_F}" in hdr
+
+
+def test_wan_fp16_hook_eligibility(monkeypatch):
+    """maybe_prequant declines without the opt-in, for CPU tensors, other shapes
+    and a missing kernel method (reference tests/test_wan_fp16.py:95-99)."""
+    from b200q._patches import wan_fp16
+    x = torch.zeros(1, 5120, dtype=torch.int8)
+    w = torch.zeros(5120, 5120, dtype=torch.int8)
+    k = SimpleNamespace(i8_matmul2d_nt_fused_cs_half=lambda *a: pytest.fail("must not run"))
+    with torch.inference_mode():
+        monkeypatch.delenv("ASFP8_DIT_EXT", raising=False)
+        assert wan_fp16.maybe_prequant(k, x, torch.ones(1), w, torch.ones(5120), None,
+                                       (1, 1, 5120)) is None
+        monkeypatch.setenv("ASFP8_DIT_EXT", "1")
+        assert wan_fp16.maybe_prequant(None, x, torch.ones(1), w, torch.ones(5120), None,
+                                       (1, 1, 5120)) is None
+        assert wan_fp16.maybe_prequant(k, x, torch.ones(1), w, torch.ones(5120), None,
+                                       (1, 1, 5120)) is None  # CPU tensors
+        w2 = torch.zeros(4096, 5120, dtype=torch.int8)
+        assert wan_fp16.maybe_prequant(k, x, torch.ones(1), w2, torch.ones(4096), None,
+                                       (1, 1, 5120)) is None  # not a Wan shape
