@@ -259,6 +259,20 @@ int launch_swiglu_rows(const DeviceInfo* d, const void* x, int64_t ldx, int64_t 
   return launch_rows<__nv_bfloat16, true, ROT, QUANT>(d, x, ldx, M, F, out, ldo, q, ldq, scales, st);
 }
 
+// GEMM on 16-bit operands (kind::f16) through the 8-bit tile kernels: the tiles
+// are byte-described, so K, the row strides and the tensor-map extents are passed
+// in bytes.  Needs 16-byte aligned operands and K % 8 == 0.
+template <MmaKind KIND, int EPI>
+int gemm16(const DeviceInfo* d, const void* a, int64_t lda, const void* w, int64_t ldw, int64_t M,
+           int64_t N, int64_t K, const EpiArgs& ep, cudaStream_t st) {
+  const int64_t kb = 2 * K, la = 2 * lda, lw = 2 * ldw;
+  if (N <= 128)
+    return launch_gemm8_tc<KIND, 128, 6, EPI, kProNone>(d, a, la, w, lw, int(M), int(N), int(kb), ep, Prologue{}, st);
+  if (M >= 256 && pair_kernels_enabled())
+    return launch_gemm8_tc2<KIND, 6, EPI, kProNone>(d, a, la, w, lw, int(M), int(N), int(kb), ep, Prologue{}, st);
+  return launch_gemm8_tc<KIND, 256, 4, EPI, kProNone>(d, a, la, w, lw, int(M), int(N), int(kb), ep, Prologue{}, st);
+}
+
 EpiArgs make_epi(void* out, int64_t ldo, int out_dtype, int64_t M, int64_t N) {
   EpiArgs e{};
   e.out = out;
@@ -278,6 +292,27 @@ struct W16Plan {
   size_t partial_bytes;
   size_t counter_bytes;
 };
+
+// W8A16 at M >= 128: the weight is decoded to the activation's 16-bit type once
+// per call (exact) into the caller's workspace and the product runs on the 8-bit
+// tile kernels as kind::f16.  The in-kernel conversion of the weight-stationary
+// kernels repeats per token tile (M / 256 times); the decode costs one pass of
+// 3 bytes per weight element.  Measured crossover on B200 (K x N = 3072 x 12288,
+// 5120 x 5120, 5120 x 13824): the decoded route is ahead from M = 65..192 and
+// 1.6-2.6x ahead at M >= 512; B200Q_W8A16_DECODE_MIN_M overrides the threshold.
+int64_t w8a16_decode_min_m() {
+  static const int64_t v = [] {
+    const char* e = getenv("B200Q_W8A16_DECODE_MIN_M");
+    return e ? static_cast<int64_t>(atoll(e)) : static_cast<int64_t>(128);
+  }();
+  return v;
+}
+bool w8a16_decode_selected(int64_t M, int64_t N, int64_t K) {
+  return M >= w8a16_decode_min_m() && K % 16 == 0 && N > 0 && N <= 65535;
+}
+size_t w8a16_decode_bytes(int64_t N, int64_t K) {
+  return (static_cast<size_t>(N) * static_cast<size_t>(K) * 2 + 255) & ~size_t(255);
+}
 
 W16Plan w8a16_plan(int num_sms, int64_t M, int64_t N, int64_t K) {
   W16Plan p{};
@@ -825,7 +860,10 @@ int b200q_fp8_quant_tensorwise(const void* x, int x_dtype, int64_t M, int64_t K,
   return finish_launch();
 }
 
-size_t b200q_w8a16_workspace_size(int64_t M, int64_t N, int64_t K) {
+}  // extern "C"
+namespace {
+// Workspace of the weight-stationary kernels alone (split-K partials + counters).
+size_t w8a16_kernel_workspace(int64_t M, int64_t N, int64_t K) {
   const DeviceInfo* d = current_device();
   const int sms = d ? d->num_sms : 148;
   if (M <= 0 || N <= 0 || K <= 0) return 0;
@@ -834,11 +872,22 @@ size_t b200q_w8a16_workspace_size(int64_t M, int64_t N, int64_t K) {
   if (p.splits <= 1) return 0;
   return ((p.partial_bytes + 255) & ~size_t(255)) + p.counter_bytes;
 }
+}  // namespace
+extern "C" {
 
-int b200q_w8a16_linear(const void* x, int x_dtype, int64_t ldx, const uint8_t* w, int64_t ldw,
-                       const float* w_scale, const void* bias, int bias_dtype, int act, void* out,
-                       int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K,
-                       void* workspace, size_t workspace_bytes, void* stream) {
+size_t b200q_w8a16_workspace_size(int64_t M, int64_t N, int64_t K) {
+  const size_t kernel_ws = w8a16_kernel_workspace(M, N, K);
+  if (M <= 0 || N <= 0 || K <= 0 || !w8a16_decode_selected(M, N, K)) return kernel_ws;
+  const size_t dec = w8a16_decode_bytes(N, K);
+  return dec > kernel_ws ? dec : kernel_ws;
+}
+
+}  // extern "C"
+namespace {
+int w8a16_linear_impl(const void* x, int x_dtype, int64_t ldx, const uint8_t* w, int64_t ldw,
+                      const float* w_scale, const void* bias, int bias_dtype, int act, void* out,
+                      int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K, void* workspace,
+                      size_t workspace_bytes, bool allow_decode, void* stream) {
   if (!x || !w || !out || !valid_dims(M, N, K) || K == 0 || ldx < K || ldw < K || ldo < N ||
       (x_dtype != B200Q_BF16 && x_dtype != B200Q_F16) ||
       (out_dtype != B200Q_BF16 && out_dtype != B200Q_F16 && out_dtype != B200Q_F32) ||
@@ -871,6 +920,22 @@ int b200q_w8a16_linear(const void* x, int x_dtype, int64_t ldx, const uint8_t* w
     return x_dtype == B200Q_F16 ? launch_w8a16_gemv<2, true>(x, ldx, w, ldw, M, N, K, ep, st)
                                 : launch_w8a16_gemv<2, false>(x, ldx, w, ldw, M, N, K, ep, st);
   }
+  if (allow_decode && w8a16_decode_selected(M, N, K) && workspace &&
+      workspace_bytes >= w8a16_decode_bytes(N, K) && aligned16(workspace)) {
+    const dim3 dgrid(static_cast<unsigned>((K / 16 + 127) / 128), static_cast<unsigned>(N));
+    if (x_dtype == B200Q_F16) {
+      auto* wd = static_cast<__half*>(workspace);
+      e4m3_rows_to16_kernel<__half><<<dgrid, 128, 0, st>>>(w, ldw, int(N), int(K), wd);
+      int s = finish_launch();
+      if (s != B200Q_OK) return s;
+      return gemm16<MmaKind::F16, kEpiScaled>(d, x, ldx, wd, K, M, N, K, ep, st);
+    }
+    auto* wd = static_cast<__nv_bfloat16*>(workspace);
+    e4m3_rows_to16_kernel<__nv_bfloat16><<<dgrid, 128, 0, st>>>(w, ldw, int(N), int(K), wd);
+    int s = finish_launch();
+    if (s != B200Q_OK) return s;
+    return gemm16<MmaKind::BF16, kEpiScaled>(d, x, ldx, wd, K, M, N, K, ep, st);
+  }
   const W16Plan p = w8a16_plan(d->num_sms, M, N, K);
   W8A16Args args{};
   args.M = int(M);
@@ -887,6 +952,16 @@ int b200q_w8a16_linear(const void* x, int x_dtype, int64_t ldx, const uint8_t* w
   }
   if (x_dtype == B200Q_F16) return dispatch_w8a16_tc<true>(d, p.bt, x, ldx, w, ldw, args, ep, st);
   return dispatch_w8a16_tc<false>(d, p.bt, x, ldx, w, ldw, args, ep, st);
+}
+}  // namespace
+extern "C" {
+
+int b200q_w8a16_linear(const void* x, int x_dtype, int64_t ldx, const uint8_t* w, int64_t ldw,
+                       const float* w_scale, const void* bias, int bias_dtype, int act, void* out,
+                       int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+  return w8a16_linear_impl(x, x_dtype, ldx, w, ldw, w_scale, bias, bias_dtype, act, out,
+                           out_dtype, ldo, M, N, K, workspace, workspace_bytes, true, stream);
 }
 
 // ---------------------------------------------------------------------------
@@ -929,7 +1004,7 @@ int b200q_w8a16_linear_noalloc(const void* x, int x_dtype, int64_t ldx, const ui
                                int act, void* out, int out_dtype, int64_t ldo, int64_t M, int64_t N,
                                int64_t K, void* stream) {
   if (!x || !w || !out || !valid_dims(M, N, K) || K == 0) return B200Q_ERR_INVALID;
-  const size_t need = b200q_w8a16_workspace_size(M, N, K);
+  const size_t need = w8a16_kernel_workspace(M, N, K);
   if (need > B200Q_NOALLOC_SCRATCH_BYTES) return B200Q_ERR_TOO_LARGE;
   void* scratch = nullptr;
   if (need) {
@@ -938,9 +1013,9 @@ int b200q_w8a16_linear_noalloc(const void* x, int x_dtype, int64_t ldx, const ui
   }
   // The shared path clears the tile counters on `stream` before the kernel
   // (the partials need no clearing: every split writes its slice first).
-  return b200q_w8a16_linear(x, x_dtype, ldx, w, ldw, w_scale, bias, bias_dtype, act, out,
-                            out_dtype, ldo, M, N, K, scratch,
-                            need ? size_t(B200Q_NOALLOC_SCRATCH_BYTES) : 0, stream);
+  return w8a16_linear_impl(x, x_dtype, ldx, w, ldw, w_scale, bias, bias_dtype, act, out,
+                           out_dtype, ldo, M, N, K, scratch,
+                           need ? size_t(B200Q_NOALLOC_SCRATCH_BYTES) : 0, false, stream);
 }
 
 int b200q_fp8_decode(const uint8_t* src, int64_t n, int fp8_kind, void* dst, int out_dtype,

@@ -3,6 +3,9 @@
 //
 //  kind::i8      int8 x int8 -> int32 in TMEM   (INT8 W8A8 route, torch._int_mm)
 //  kind::f8f6f4  e4m3 x e4m3 -> fp32 in TMEM    (FP8 W8A8 route, torch._scaled_mm)
+//  kind::f16     bf16/f16 x bf16/f16 -> fp32     (W8A16 at large M on the decoded weight)
+// The tiles are described in bytes (128-byte rows, 32 bytes of K per MMA), so a
+// 16-bit operand is passed with K, row strides and extents in bytes.
 //
 // Structure (one CTA per SM, persistent over output tiles):
 //   warp 0      TMA producer: 128x128-byte A tile + BNx128-byte W tile per stage,
@@ -437,9 +440,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t kIdesc =
-          KIND == MmaKind::I8 ? make_idesc(2, 1, 1, kGemmBM, BN)   // s32 <- s8 x s8
-                              : make_idesc(1, 0, 0, kGemmBM, BN);  // f32 <- e4m3 x e4m3
+      constexpr uint32_t kIdesc = kind_idesc<KIND>(kGemmBM, BN);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -672,8 +673,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (even CTA)
     if (lane == 0 && rank == 0) {
-      constexpr uint32_t kIdesc =
-          KIND == MmaKind::I8 ? make_idesc(2, 1, 1, BM, BN) : make_idesc(1, 0, 0, BM, BN);
+      constexpr uint32_t kIdesc = kind_idesc<KIND>(BM, BN);
       const uint32_t empty_self = smem_u32(&empty[0]);
       const uint32_t empty_peer = mapa_shared(empty_self, peer);
       const uint32_t accf_self = smem_u32(&acc_full[0]);

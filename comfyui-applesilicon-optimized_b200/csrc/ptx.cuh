@@ -172,8 +172,9 @@ __device__ __forceinline__ void tc_fence_after() {
 }
 
 // One MMA D(tmem) (+)= A(smem desc) x B(smem desc)^T, issued by a single thread.
-// KIND selects the PTX .kind qualifier.
-enum class MmaKind { I8, F8F6F4, F16 };
+// KIND selects the PTX .kind qualifier (F16 and BF16 are both kind::f16; they
+// differ in the instruction descriptor's operand formats).
+enum class MmaKind { I8, F8F6F4, F16, BF16 };
 
 template <MmaKind KIND>
 __device__ __forceinline__ void umma_ss(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
@@ -288,10 +289,16 @@ __device__ __forceinline__ void umma_ss_pair(uint32_t tmem_d, uint64_t adesc, ui
         "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
-  } else {
+  } else if constexpr (KIND == MmaKind::F8F6F4) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
   }
@@ -324,6 +331,14 @@ __device__ __forceinline__ uint64_t make_sw128_desc(uint32_t smem_addr) {
 __host__ __device__ constexpr uint32_t make_idesc(uint32_t c_fmt, uint32_t a_fmt, uint32_t b_fmt,
                                                   uint32_t M, uint32_t N) {
   return (c_fmt << 4) | (a_fmt << 7) | (b_fmt << 10) | ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+// Descriptor of an MMA kind with both operands of one type: s32 <- s8 x s8;
+// f32 <- e4m3 x e4m3; f32 <- f16 x f16; f32 <- bf16 x bf16.
+template <MmaKind KIND>
+__host__ __device__ constexpr uint32_t kind_idesc(uint32_t M, uint32_t N) {
+  return KIND == MmaKind::I8 ? make_idesc(2, 1, 1, M, N)
+         : KIND == MmaKind::BF16 ? make_idesc(1, 1, 1, M, N)
+                                 : make_idesc(1, 0, 0, M, N);
 }
 
 }  // namespace b200q

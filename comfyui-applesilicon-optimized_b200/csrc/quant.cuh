@@ -702,4 +702,36 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// FP8 e4m3 weight rows [N, K] (row stride ldw bytes, K % 16 == 0, 16-byte
+// aligned rows) -> 16-bit rows [N, K] (contiguous): 16 codes per thread, one
+// 16-byte load and two 16-byte stores.  Exact: every e4m3 value is a bf16 and an
+// fp16 value.  Grid: x over 16-code columns, y over rows.
+template <typename T>
+__global__ void __launch_bounds__(128)
+    e4m3_rows_to16_kernel(const uint8_t* __restrict__ w, int64_t ldw, int N, int K,
+                          T* __restrict__ out) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int row = blockIdx.y;
+  if (c >= (K >> 4) || row >= N) return;
+  const uint4 v = __ldcs(reinterpret_cast<const uint4*>(w + static_cast<int64_t>(row) * ldw) + c);
+  const uint32_t in[4] = {v.x, v.y, v.z, v.w};
+  uint32_t o[8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint16_t lo = static_cast<uint16_t>(in[j] & 0xFFFFu), hi = static_cast<uint16_t>(in[j] >> 16);
+    if constexpr (std::is_same<T, __half>::value) {
+      __half2_raw a = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(lo), __NV_E4M3);
+      __half2_raw b = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(hi), __NV_E4M3);
+      o[2 * j] = static_cast<uint32_t>(a.x) | (static_cast<uint32_t>(a.y) << 16);
+      o[2 * j + 1] = static_cast<uint32_t>(b.x) | (static_cast<uint32_t>(b.y) << 16);
+    } else {
+      o[2 * j] = e4m3x2_to_bf16x2(lo);
+      o[2 * j + 1] = e4m3x2_to_bf16x2(hi);
+    }
+  }
+  uint4* dst = reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * K) + 2 * c;
+  dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+  dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+}
+
 }  // namespace b200q

@@ -270,14 +270,30 @@ def test_w8a16_fp16_activations_and_ragged(native):
 
 
 def test_w8a16_split_k_is_deterministic(native):
+    """The weight-stationary kernel's split-K (fixed-order fix-up) is deterministic.
+    It runs when the workspace is below the decoded-weight route's requirement."""
     g = _gen(12)
     M, K, N = 300, 12288, 3072  # 24 weight tiles x 2 token tiles x 2 splits
     x = torch.randn(M, K, generator=g).to(torch.bfloat16).to(DEV)
     w = (torch.randn(N, K, generator=g) * 50).clamp(-448, 448).to(torch.float8_e4m3fn).to(DEV)
-    assert native.lib().b200q_w8a16_workspace_size(M, N, K) > 0, "expected the split-K plan"
-    o1 = native.w8a16_linear(x, w)
-    o2 = native.w8a16_linear(x, w)
+    L = native.lib()
+    nbytes = (N * K * 2 + 255) // 256 * 256 - 256   # just below the decode route's need
+    work = torch.empty(nbytes, dtype=torch.uint8, device=DEV)
+
+    def run(ws_bytes):
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+        native._check(L.b200q_w8a16_linear(native._p(x), 0, K, native._p(w.view(torch.uint8)), K,
+                                           None, None, 0, 0, native._p(out), 0, N, M, N, K,
+                                           native._p(work), ws_bytes, native._stream(x)))
+        return out
+    assert L.b200q_w8a16_linear(native._p(x), 0, K, native._p(w.view(torch.uint8)), K, None, None,
+                                0, 0, native._p(torch.empty(M, N, dtype=torch.bfloat16, device=DEV)),
+                                0, N, M, N, K, None, 0, native._stream(x)) == 4, \
+        "expected the split-K plan (no workspace -> B200Q_ERR_WORKSPACE)"
+    o1, o2 = run(nbytes), run(nbytes)
     assert torch.equal(o1, o2)
+    ref = oracle.w8a16_linear(x.cpu(), w.cpu(), None, None, None, out_dtype="fp32")
+    assert oracle.elementwise_ulp_ratio(o1, ref) <= 1.0
 
 
 def test_device_status_clean(native):
