@@ -272,6 +272,13 @@ class B200Block:
             h = y
         return seq, _native.launch_count() - n0
 
+    def build_step_graph(self, inputs):
+        """The whole step (every op, in order) captured as one CUDA graph."""
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.step_graph_outs = self.step(inputs)
+        return g
+
     def _ev(self, record):
         if not record:
             return None
@@ -363,14 +370,19 @@ def run_b200q(args):
     for _ in range(args.warmup):
         blk.step(blk.inputs)
     barrier()
-    graphs = None
+    graphs = step_graph = None
     if args.launch == "graph":
         graphs, launches_per_step = blk.build_graphs(blk.inputs)
         for g, _ in graphs:  # one untimed replay after capture
             g.replay()
+        step_graph = blk.build_step_graph(blk.inputs)
+        step_graph.replay()
         barrier()
 
-    # ---- device-resident timing: per-step events, L2 flushed between steps (untimed)
+    # ---- device-resident timing, L2 flushed between steps (outside the events).
+    # value: one event pair per step around the whole step (with graphs: the step
+    # replayed as one CUDA graph).  roofline: event pairs around each GEMM launch
+    # (with graphs: each op replayed as its own graph), in a second timed loop.
     launches0 = _native.launch_count()
     step_ms = []
     blk.gemm_events = []
@@ -381,9 +393,16 @@ def run_b200q(args):
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record()
-            if graphs is None:
+            if step_graph is None:
                 blk.step(blk.inputs, record=True)
             else:
+                step_graph.replay()
+            e1.record()
+            step_ms.append((e0, e1))
+        barrier()
+        if graphs is not None:
+            for _ in range(args.steps):
+                flush.zero_()
                 for g, fl in graphs:
                     if fl:
                         ea = torch.cuda.Event(enable_timing=True)
@@ -394,9 +413,7 @@ def run_b200q(args):
                         blk.gemm_events.append((ea, eb, fl))
                     else:
                         g.replay()
-            e1.record()
-            step_ms.append((e0, e1))
-        barrier()
+            barrier()
     launches = (_native.launch_count() - launches0 if graphs is None
                 else launches_per_step * args.steps)
     t_dev = sum(a.elapsed_time(b) for a, b in step_ms)
@@ -470,7 +487,9 @@ def run_b200q(args):
                                      "+1 amax-reduction launch per linear)",
                             "separate": "own launch(es) before each GEMM"}[args.prologue]
                            if spec["route"] != "w8a16" else "none (weight-only)"),
-                       "launch": ("each op of the step captured once as a CUDA graph, replayed per step"
+                       "launch": ("the step captured once as one CUDA graph, replayed per step (value); "
+                                  "each op also captured as its own graph for the per-GEMM events "
+                                  "(roofline), timed in a second loop"
                                   if args.launch == "graph" else "eager torch.ops calls")},
             "roofline": ({"bound": "hbm", "achieved": round(achieved_gbs, 1) if achieved_gbs else None,
                           "peak": peaks["hbm_gbs"], "unit": "GB/s",
