@@ -19,6 +19,8 @@ _patches/fp8_ext/fp8_matmul2d.mm:355-360, _patches/fp8s_ext/w8a16_gemm.mm:316-32
   i8_matmul_nt_fused_cs_qkv(a, w, rs, cs, bias, heads, head_dim, batch)
                                             -> q, k, v in [B, H, S, D] (i8_matmul2d_nt_fused_cs_qkv)
   rms_rope_partial_(q, k, freqs, qw, kw, eps) -> in-place RMSNorm + split-half RoPE
+  i8_matmul_nt_fused_cs_qkv_rms_rope(a, w, rs, cs, bias, freqs, qw, kw, heads, head_dim, eps, batch)
+                                            -> q, k, v with Q/K normalized + rotated in the epilogue
   silu_mul_split(x [M,2F] bf16)             -> act [M,F] = bf16(bf16(silu(gate)) * up)
   i8_swiglu_rot(x [M,2F] bf16)              -> convrot(act) [M,F] bf16   (i8_swiglu_rot)
   i8_swiglu_quant(x [M,2F], rotate)         -> (q int8 [M,F], scale [M,1]) of (rotated) act
@@ -69,6 +71,9 @@ _SIGNATURES = {
                                        _int, _i64, _i64, _i64, _i64, _i64, _i64, _vp], _int),
     "b200q_rms_rope_partial": ([_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
                                ctypes.c_float, _vp], _int),
+    "b200q_i8_matmul_nt_dequant_qkv_rms_rope": ([_vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _vp,
+                                                 _vp, _vp, _i64, _i64, _vp, _i64, _vp, _vp,
+                                                 ctypes.c_float, _i64, _i64, _i64, _vp], _int),
     "b200q_i8_matmul_nt_dequant": ([_vp, _i64, _vp, _i64, _vp, _vp, _i64, _vp, _int, _vp, _int,
                                     _i64, _i64, _i64, _i64, _vp], _int),
     "b200q_i8_linear": ([_vp, _int, _i64, _vp, _i64, _vp, _i64, _vp, _int, _vp, _int, _i64, _i64,
@@ -271,6 +276,38 @@ def i8_matmul_nt_fused_cs_qkv(a, w, row_scale, col_scale, bias=None, heads=1, he
         _p(a), a.stride(0), _p(w), w.stride(0), _p(row_scale), _p(col_scale), col_scale.numel(),
         _p(bias), _p(outs[0]), _p(outs[1]), _p(outs[2]), code, heads, head_dim, batch, M, N, K,
         _stream(a)))
+    return tuple(outs)
+
+
+def i8_matmul_nt_fused_cs_qkv_rms_rope(a, w, row_scale, col_scale, bias, freqs, q_weight,
+                                       k_weight, heads, head_dim=128, eps=1e-6, batch=1):
+    """INT8 QKV projection into attention layout with Q/K RMSNorm + split-half
+    RoPE applied in the GEMM epilogue (i8_matmul2d_nt_fused_cs_qkv_rms_rope):
+    q, k, v [batch, heads, M // batch, 128] bf16; freqs [M, R, 2, 2] bf16 with
+    R % 8 == 0 (use rms_rope_partial_ after the plain scatter otherwise)."""
+    _require_cuda(a, w, row_scale, col_scale, bias, freqs, q_weight, k_weight)
+    a, w = _rows_2d(a, "a"), _rows_2d(w, "w")
+    M, K = a.shape
+    N = w.shape[0]
+    if head_dim != 128 or w.shape[1] != K or N != 3 * heads * head_dim or M % batch:
+        raise RuntimeError(f"{TAG} qkv rms/rope shapes: M={M} K={K} N={N} heads={heads} "
+                           f"head_dim={head_dim} batch={batch}")
+    row_scale = row_scale.reshape(-1).float().contiguous()
+    col_scale = col_scale.reshape(-1).float().contiguous()
+    if bias is not None:
+        bias = bias.to(torch.bfloat16).contiguous()
+    fr = freqs.to(torch.bfloat16).contiguous()
+    R = fr.shape[-3] if fr.dim() >= 3 else 0
+    if fr.numel() != M * R * 4:
+        raise RuntimeError(f"{TAG} freqs must hold [M, R, 2, 2] = {M} x R x 4 values")
+    qw, kw = q_weight.float().contiguous(), k_weight.float().contiguous()
+    S = M // batch
+    outs = [torch.empty((batch, heads, S, head_dim), dtype=torch.bfloat16, device=a.device)
+            for _ in range(3)]
+    _check(lib().b200q_i8_matmul_nt_dequant_qkv_rms_rope(
+        _p(a), a.stride(0), _p(w), w.stride(0), _p(row_scale), _p(col_scale), col_scale.numel(),
+        _p(bias), _p(outs[0]), _p(outs[1]), _p(outs[2]), heads, batch, _p(fr), R, _p(qw), _p(kw),
+        float(eps), M, N, K, _stream(a)))
     return tuple(outs)
 
 
@@ -615,6 +652,9 @@ def _register_ops():
              "-> (Tensor, Tensor, Tensor)")
     L.define("rms_rope_partial_(Tensor(a!) q, Tensor(b!) k, Tensor freqs, Tensor q_weight, "
              "Tensor k_weight, float eps=1e-06) -> ()")
+    L.define("i8_matmul_nt_fused_cs_qkv_rms_rope(Tensor a, Tensor w, Tensor row_scale, "
+             "Tensor col_scale, Tensor? bias, Tensor freqs, Tensor q_weight, Tensor k_weight, "
+             "int heads, int head_dim=128, float eps=1e-06, int batch=1) -> (Tensor, Tensor, Tensor)")
     L.define("i8_linear(Tensor x, Tensor w, Tensor w_scale, Tensor? bias=None, "
              "ScalarType out_dtype=15, str act='none') -> Tensor")
     L.define("fp8_quant_tensorwise(Tensor x) -> (Tensor, Tensor)")
@@ -644,6 +684,7 @@ def _register_ops():
         "i8_linear": i8_linear,
         "i8_matmul_nt_fused_cs_qkv": i8_matmul_nt_fused_cs_qkv,
         "rms_rope_partial_": rms_rope_partial_,
+        "i8_matmul_nt_fused_cs_qkv_rms_rope": i8_matmul_nt_fused_cs_qkv_rms_rope,
         "fp8_quant_tensorwise": fp8_quant_tensorwise,
         "fp8_linear": fp8_linear,
         "fp8_scaled_mm": lambda a, w, sa=None, sb=None, sr=None, b=None, od=torch.bfloat16,
@@ -677,6 +718,10 @@ def _register_ops():
         od=torch.bfloat16: tuple(a.new_empty((batch, heads, a.shape[0] // batch, head_dim), dtype=od)
                                  for _ in range(3)),
         "rms_rope_partial_": lambda q, k, fr, qw, kw, eps=1e-6: None,
+        "i8_matmul_nt_fused_cs_qkv_rms_rope": lambda a, w, rs, cs, bias, fr, qw, kw, heads,
+        head_dim=128, eps=1e-6, batch=1: tuple(
+            a.new_empty((batch, heads, a.shape[0] // batch, head_dim), dtype=torch.bfloat16)
+            for _ in range(3)),
         "i8_linear": lambda x, w, ws, bias=None, od=torch.bfloat16, act="none": x.new_empty(
             (*x.shape[:-1], w.shape[0]), dtype=od),
         "fp8_quant_tensorwise": lambda x: (x.new_empty((x.numel() // x.shape[-1], x.shape[-1]),

@@ -88,6 +88,29 @@ class _NativeInt8Kernel:
                                                       torch.float16)
 
     @staticmethod
+    def i8_matmul2d_nt_fused_cs_qkv(a, b, row_scale, col_scale, bias, H, D, long_schedule=True):
+        """[1, H, M, D] Q/K/V straight from the epilogue (int8_gemm.mm:2028)."""
+        return torch.ops.b200q.i8_matmul_nt_fused_cs_qkv(a, b, row_scale, col_scale, bias, H, D, 1)
+
+    @staticmethod
+    def i8_matmul2d_nt_fused_cs_qkv_rms_rope(a, b, row_scale, col_scale, bias, fr, qw, kw, H, D,
+                                             eps, long_schedule=True):
+        """Q/K/V with Q and K RMS-normalized and rotated (int8_gemm.mm:2111).  Default:
+        the scatter epilogue, then the in-place norm + RoPE kernel (two launches).
+        B200Q_QKV_FUSED_NORM_ROPE=1 runs the norm and RoPE inside the GEMM epilogue
+        (rotary widths that are multiples of 8); both give the same bytes, and the
+        two-launch route measured faster on B200."""
+        R = fr.shape[-3] if fr.dim() >= 3 else 0
+        if (os.environ.get("B200Q_QKV_FUSED_NORM_ROPE", "0") == "1" and D == 128
+                and R % 8 == 0):
+            return torch.ops.b200q.i8_matmul_nt_fused_cs_qkv_rms_rope(
+                a, b, row_scale, col_scale, bias, fr, qw, kw, H, D, float(eps), 1)
+        q, k, v = torch.ops.b200q.i8_matmul_nt_fused_cs_qkv(a, b, row_scale, col_scale, bias, H, D,
+                                                            1)
+        torch.ops.b200q.rms_rope_partial_(q, k, fr, qw, kw, float(eps))
+        return q, k, v
+
+    @staticmethod
     def i8_swiglu_rot(x):
         return torch.ops.b200q.i8_swiglu_rot(x)
 
@@ -335,6 +358,66 @@ def int8_mlp_bridge(fc1, fc2, x):
     except Exception as e:
         print(f"{TAG} MLP bridge fell back ({e!r})")
         return None
+
+
+def _int8_qkv_prequant(layer, x, heads, head_dim, norm_rope):
+    """QKV projection straight to attention layout [1, H, S, D] (int8_linear_kernel_mps.py
+    :266-412): ``norm_rope`` is None for the layout-only epilogue or (freqs, q_weight_fp32,
+    k_weight_fp32, eps) for the D = 128 epilogue that also normalizes and rotates Q and K.
+    Returns (q, k, v) or None (the caller keeps its own path)."""
+    fused = norm_rope is not None
+    name = "i8_matmul2d_nt_fused_cs_qkv_rms_rope" if fused else "i8_matmul2d_nt_fused_cs_qkv"
+    if (_kernel is None or not hasattr(_kernel, name)
+            or os.environ.get("ASFP8_INT8_QKV_SCATTER", "1") != "1"
+            or (fused and os.environ.get("ASFP8_INT8_QKV_NORM_ROPE", "1") != "1")):
+        return None
+    try:
+        if (not isinstance(x, torch.Tensor) or x.dim() != 2 or x.device.type != "cuda"
+                or x.dtype != torch.bfloat16 or not x.is_contiguous()):
+            return None
+        if not _int8_layer_ok(layer):
+            return None
+        w = layer.weight
+        params = w._params
+        qdata = w._qdata
+        if tuple(qdata.shape) != (3 * heads * head_dim, x.shape[1]):
+            return None
+        weight_scale = params.scale.view(-1)
+        if weight_scale.numel() != qdata.shape[0]:
+            return None
+        x_8, x_scale = _quant_cached(x, getattr(params, "convrot", False),
+                                     getattr(params, "convrot_groupsize", 256))
+        bias_arg = layer.bias.to(torch.bfloat16) if layer.bias is not None else None
+        common = (x_8, qdata.contiguous(), x_scale.reshape(-1).float().contiguous(),
+                  weight_scale.float().contiguous(), bias_arg)
+        if fused:
+            freqs, q_weight, k_weight, eps = norm_rope
+            if (head_dim != 128 or not isinstance(freqs, torch.Tensor)
+                    or freqs.device.type != "cuda" or freqs.dtype != torch.bfloat16
+                    or not freqs.is_contiguous() or freqs.dim() < 3
+                    or freqs.numel() != x.shape[0] * freqs.shape[-3] * 4
+                    or 2 * freqs.shape[-3] > head_dim
+                    or any(not isinstance(t, torch.Tensor) or t.device.type != "cuda"
+                           or t.dtype != torch.float32 or not t.is_contiguous()
+                           or t.numel() != head_dim for t in (q_weight, k_weight))):
+                return None
+            return getattr(_kernel, name)(*common, freqs, q_weight, k_weight, heads, head_dim,
+                                          float(eps))
+        return getattr(_kernel, name)(*common, heads, head_dim)
+    except Exception as e:
+        route = "qkv norm/RoPE epilogue" if fused else "qkv scatter"
+        print(f"{TAG} {route} fell back ({e!r})")
+        return None
+
+
+def int8_qkv_prequant(layer, x, heads, head_dim):
+    """QKV projection directly to contiguous [1, H, S, D] Q/K/V (:409-414)."""
+    return _int8_qkv_prequant(layer, x, heads, head_dim, None)
+
+
+def int8_qkv_rms_rope_prequant(layer, x, freqs, q_weight, k_weight, heads, head_dim, eps):
+    """INT8 QKV projection + Q/K RMSNorm / partial RoPE epilogue (:417-427)."""
+    return _int8_qkv_prequant(layer, x, heads, head_dim, (freqs, q_weight, k_weight, eps))
 
 
 def _load_kernel():

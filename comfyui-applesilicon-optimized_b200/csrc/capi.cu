@@ -684,26 +684,72 @@ int b200q_i8_mlp_bridge_prequant(const int8_t* a, int64_t lda, const int8_t* w1,
   return B200Q_OK;
 }
 
+int b200q_i8_matmul_nt_dequant_qkv_rms_rope(
+    const int8_t* a, int64_t lda, const int8_t* w, int64_t ldw, const float* row_scale,
+    const float* col_scale, int64_t col_scale_numel, const void* bias, void* q_out, void* k_out,
+    void* v_out, int64_t heads, int64_t batch, const void* freqs, int64_t rot_half,
+    const float* q_weight, const float* k_weight, float eps, int64_t M, int64_t N, int64_t K,
+    void* stream) {
+  constexpr int64_t D = 128;
+  if (!a || !w || !row_scale || !col_scale || !q_out || !k_out || !v_out || !q_weight ||
+      !k_weight || !valid_dims(M, N, K) || K == 0 || lda < K || ldw < K || heads <= 0 ||
+      batch <= 0 || M % batch != 0 || N != 3 * heads * D ||
+      (col_scale_numel != 1 && col_scale_numel != N) || rot_half < 0 || rot_half % 8 != 0 ||
+      2 * rot_half > D || (rot_half > 0 && (!freqs || !aligned16(freqs))) ||
+      !aligned16(q_out) || !aligned16(k_out) || !aligned16(v_out) || !aligned16(q_weight) ||
+      !aligned16(k_weight) || !gemm8_tc_eligible(a, lda, w, ldw, K))
+    return B200Q_ERR_INVALID;
+  const DeviceInfo* d = current_device();
+  if (!d) return B200Q_ERR_UNSUPPORTED;
+  if (M == 0) return B200Q_OK;
+  EpiArgs ep = make_epi(q_out, N, B200Q_BF16, M, N);
+  ep.row_scale = row_scale;
+  ep.row_scale_vec = 1;
+  ep.col_scale = col_scale;
+  ep.col_scale_vec = col_scale_numel == N ? 1 : 0;
+  ep.bias = bias;
+  ep.bias_dtype = bias ? kBiasBF16 : kBiasNone;
+  ep.qkv[0] = q_out;
+  ep.qkv[1] = k_out;
+  ep.qkv[2] = v_out;
+  ep.qkv_heads = static_cast<int>(heads);
+  ep.qkv_dim = static_cast<int>(D);
+  ep.qkv_seq = static_cast<int>(M / batch);
+  ep.rope_freqs = static_cast<const __nv_bfloat16*>(freqs);
+  ep.q_norm_w = q_weight;
+  ep.k_norm_w = k_weight;
+  ep.rope_r = static_cast<int>(rot_half);
+  ep.norm_eps = eps;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (M >= 256 && pair_kernels_enabled())
+    return launch_gemm8_tc2<MmaKind::I8, 6, kEpiI8QkvNormRope, kProNone>(d, a, lda, w, ldw, int(M), int(N), int(K), ep, Prologue{}, st);
+  return launch_gemm8_tc<MmaKind::I8, 256, 4, kEpiI8QkvNormRope, kProNone>(d, a, lda, w, ldw, int(M), int(N), int(K), ep, Prologue{}, st);
+}
+
 int b200q_rms_rope_partial(void* q, void* k, const void* freqs, const float* q_weight,
                            const float* k_weight, int64_t batch, int64_t heads, int64_t seq,
                            int64_t head_dim, int64_t rot_half, float eps, void* stream) {
   if (!q || !k || !q_weight || !k_weight || batch <= 0 || heads <= 0 || seq <= 0 ||
       head_dim <= 0 || head_dim % 32 != 0 || head_dim > 256 || rot_half < 0 ||
       2 * rot_half > head_dim || (rot_half > 0 && !freqs) ||
-      batch * heads * seq >= (int64_t(1) << 30))
+      batch * heads * seq >= (int64_t(1) << 30) ||
+      (reinterpret_cast<uintptr_t>(q) & 7) != 0 || (reinterpret_cast<uintptr_t>(k) & 7) != 0 ||
+      !aligned16(q_weight) || !aligned16(k_weight) ||
+      (rot_half > 0 && rot_half % 4 == 0 && !aligned16(freqs)))
     return B200Q_ERR_INVALID;
   const DeviceInfo* d = current_device();
   if (!d) return B200Q_ERR_UNSUPPORTED;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int64_t warps = 2 * batch * heads * seq;
-  const dim3 grid(static_cast<unsigned>((warps + kRrWarps - 1) / kRrWarps));
+  if (batch * heads > 65535) return B200Q_ERR_INVALID;
+  const dim3 grid(static_cast<unsigned>((seq + kRrWarps - 1) / kRrWarps),
+                  static_cast<unsigned>(batch * heads), 2);
   auto* qp = static_cast<__nv_bfloat16*>(q);
   auto* kp = static_cast<__nv_bfloat16*>(k);
   auto* fp = static_cast<const __nv_bfloat16*>(freqs);
   if (head_dim <= 128)
-    rms_rope_partial_kernel<1><<<grid, kRrWarps * 32, 0, st>>>(qp, kp, fp, q_weight, k_weight, int(batch), int(heads), int(seq), int(head_dim), int(rot_half), eps);
+    rms_rope_partial_kernel<1><<<grid, kRrWarps * 32, 0, st>>>(qp, kp, fp, q_weight, k_weight, int(heads), int(seq), int(head_dim), int(rot_half), eps);
   else
-    rms_rope_partial_kernel<2><<<grid, kRrWarps * 32, 0, st>>>(qp, kp, fp, q_weight, k_weight, int(batch), int(heads), int(seq), int(head_dim), int(rot_half), eps);
+    rms_rope_partial_kernel<2><<<grid, kRrWarps * 32, 0, st>>>(qp, kp, fp, q_weight, k_weight, int(heads), int(seq), int(head_dim), int(rot_half), eps);
   return finish_launch();
 }
 

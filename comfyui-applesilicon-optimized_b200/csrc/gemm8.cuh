@@ -42,7 +42,11 @@ constexpr int kGemmGroupM = 16;
 // [gate; up]; each tile holds matching gate and up columns (the producer loads
 // the two row ranges into the two halves of the B tile) and the epilogue writes
 // act = swiglu(gate, up) [M, F] instead of the [M, 2F] output.
-enum EpiMode : int { kEpiInt32 = 0, kEpiI8Dequant = 1, kEpiScaled = 2, kEpiI8SwiGLU = 3 };
+// kEpiI8QkvNormRope: the INT8 dequant epilogue storing Q/K/V in attention
+// layout (EpiArgs.qkv*, head_dim 128) with Q and K RMS-normalized and rotated
+// (split-half RoPE) before the store.
+enum EpiMode : int { kEpiInt32 = 0, kEpiI8Dequant = 1, kEpiScaled = 2, kEpiI8SwiGLU = 3,
+                     kEpiI8QkvNormRope = 4 };
 
 template <int BN, int STAGES>
 struct Gemm8Layout {
@@ -190,7 +194,7 @@ template <int EPI, bool ACC_INT>
 __device__ __forceinline__ void epilogue_math(const uint32_t (&r)[32], const float (&cs)[32],
                                               const float (&bi)[32], bool has_bias, float rs,
                                               float xs, const EpiArgs& e, float (&v)[32]) {
-  if constexpr (EPI == kEpiI8Dequant || EPI == kEpiI8SwiGLU) {
+  if constexpr (EPI == kEpiI8Dequant || EPI == kEpiI8SwiGLU || EPI == kEpiI8QkvNormRope) {
     // Reference order (int8_gemm.mm:417-443): s = cs*rs; T(C*s); T(r + bias).
     if (e.out_dtype == kOutF16) {
 #pragma unroll
@@ -338,6 +342,131 @@ __device__ __forceinline__ void swiglu_tile_epilogue(uint32_t taddr, int half, i
         for (int j = 0; j < 32; ++j)
           if (f0 + j < F) p[j] = static_cast<uint16_t>(packed[j >> 1] >> (16 * (j & 1)));
       }
+    }
+  }
+}
+
+// Eight columns of one row: tcgen05.ld of the accumulators at taddr, then the
+// reference's bf16 two-rounding dequant (+ bias) at global columns n0 .. n0+7.
+// Warp-collective (every lane of the warp calls it).
+__device__ __forceinline__ void dequant8_bf16(uint32_t taddr, int n0, float rs, const EpiArgs& ep,
+                                              float (&v)[8]) {
+  uint32_t r[8];
+  float cs[8], bi[8];
+  tmem_ld8(taddr, r);
+  const bool hb = load_col_params8(ep, n0, cs, bi);
+  tmem_ld_wait();
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    v[j] = round_bf16(__fmul_rn(__int2float_rn(static_cast<int32_t>(r[j])), __fmul_rn(cs[j], rs)));
+    if (hb) v[j] = round_bf16(__fadd_rn(v[j], bi[j]));
+  }
+}
+
+// One head (128 columns, TMEM columns taddr .. taddr+127, global columns
+// n0 .. n0+127) of one row per thread, for a warp that owns the head:
+// the reference's fused Q/K RMSNorm + partial split-half RoPE epilogue
+// (int8_gemm.mm:672-862; rms_rope_attention_partial semantics,
+// dit_kernels.mm:825-874).  V heads are stored as they are.
+//  pass 1: dequant, sum of squares in the reference order (element groups
+//          4vt..4vt+3 summed in order, then the 32 group sums combined by the
+//          xor-butterfly tree of a warp-wide reduction, here inside one thread);
+//  pass 2: TMEM read again (the same dequant values), y = bf16((x*inv)*w),
+//          RoPE on column pairs (i, i+R) read together, stores of 8 columns.
+__device__ __forceinline__ void qkv_norm_rope_head(uint32_t taddr, int n0, int64_t m, bool row_ok,
+                                                   float rs, const EpiArgs& ep) {
+  constexpr int D = 128;
+  // The last tile's second half lies past N when the head count is odd (N = 384 H);
+  // the whole warp skips it together, so no tcgen05.ld is left half-issued.
+  if (n0 >= ep.N) return;
+  const int kind = n0 / (ep.qkv_heads * D);
+  if (kind == 2) {
+#pragma unroll 1
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t r[32];
+      float cs[32], bi[32], v[32];
+      const bool hb = load_col_params(ep, n0 + 32 * c, cs, bi);
+      tmem_ld32(taddr + 32 * c, r);
+      tmem_ld_wait();
+      if (row_ok) {
+        epilogue_math<kEpiI8Dequant, true>(r, cs, bi, hb, rs, 1.0f, ep, v);
+        store_chunk(ep, m, n0 + 32 * c, v, ep.N);
+      }
+    }
+    return;
+  }
+  float p[32];
+#pragma unroll
+  for (int s = 0; s < D / 8; ++s) {
+    float x[8];
+    dequant8_bf16(taddr + 8 * s, n0 + 8 * s, rs, ep, x);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float acc = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc = __fadd_rn(acc, __fmul_rn(x[4 * h + j], x[4 * h + j]));
+      p[2 * s + h] = acc;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int i = 0; i < o; ++i) p[i] = __fadd_rn(p[i], p[i + o]);
+  const float inv = __frsqrt_rn(__fadd_rn(__fdiv_rn(p[0], static_cast<float>(D)), ep.norm_eps));
+  const float* w = kind == 0 ? ep.q_norm_w : ep.k_norm_w;
+  const int R = ep.rope_r;
+#pragma unroll 1
+  for (int d0 = 0; d0 < D; d0 += 8) {
+    if (d0 >= R && d0 < 2 * R) continue;  // stored with its partner d0 - R
+    float ya[8];
+    dequant8_bf16(taddr + d0, n0 + d0, rs, ep, ya);
+    {
+      const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + d0));
+      const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + d0) + 1);
+      const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ya[j] = round_bf16(__fmul_rn(__fmul_rn(ya[j], inv), wv[j]));
+    }
+    if (d0 < R) {
+      float yb[8];
+      dequant8_bf16(taddr + d0 + R, n0 + d0 + R, rs, ep, yb);
+      {
+        const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + d0 + R));
+        const float4 w1 = __ldg(reinterpret_cast<const float4*>(w + d0 + R) + 1);
+        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) yb[j] = round_bf16(__fmul_rn(__fmul_rn(yb[j], inv), wv[j]));
+      }
+      if (row_ok) {
+        // freqs[m][i][r][c] for i = d0 .. d0+7: 32 consecutive bf16
+        const uint4* fp = reinterpret_cast<const uint4*>(ep.rope_freqs + (m * R + d0) * 4);
+        float oa[8], ob[8];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 f = __ldg(fp + q);  // i = d0 + 2q, d0 + 2q + 1
+          const uint32_t fw[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const int j = 2 * q + t;
+            const float m00 = __uint_as_float(fw[2 * t] << 16);
+            const float m01 = __uint_as_float(fw[2 * t] & 0xFFFF0000u);
+            const float m10 = __uint_as_float(fw[2 * t + 1] << 16);
+            const float m11 = __uint_as_float(fw[2 * t + 1] & 0xFFFF0000u);
+            oa[j] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(m00, ya[j])), __fmul_rn(m01, yb[j])));
+            ob[j] = round_bf16(__fadd_rn(round_bf16(__fmul_rn(m11, yb[j])), __fmul_rn(m10, ya[j])));
+          }
+        }
+        uint4* pa = reinterpret_cast<uint4*>(out_ptr16(ep, m, n0 + d0));
+        uint4* pb = reinterpret_cast<uint4*>(out_ptr16(ep, m, n0 + d0 + R));
+        pa[0] = make_uint4(pack_bf16x2(oa[0], oa[1]), pack_bf16x2(oa[2], oa[3]),
+                           pack_bf16x2(oa[4], oa[5]), pack_bf16x2(oa[6], oa[7]));
+        pb[0] = make_uint4(pack_bf16x2(ob[0], ob[1]), pack_bf16x2(ob[2], ob[3]),
+                           pack_bf16x2(ob[4], ob[5]), pack_bf16x2(ob[6], ob[7]));
+      }
+    } else if (row_ok) {
+      uint4* pa = reinterpret_cast<uint4*>(out_ptr16(ep, m, n0 + d0));
+      pa[0] = make_uint4(pack_bf16x2(ya[0], ya[1]), pack_bf16x2(ya[2], ya[3]),
+                         pack_bf16x2(ya[4], ya[5]), pack_bf16x2(ya[6], ya[7]));
     }
   }
 }
@@ -513,6 +642,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
       if constexpr (kSwiGLU) {
         swiglu_tile_epilogue<BN>(taddr, half, nb * kTileN, F, m, row_ok, rs, ep);
+      } else if constexpr (EPI == kEpiI8QkvNormRope) {
+        // BN = 256: each warp half owns one 128-column head
+        qkv_norm_rope_head(taddr + half * 128, nb * BN + half * 128, m, row_ok, rs, ep);
       } else {
 #pragma unroll 1
         for (int c = half * kChunks; c < (half + 1) * kChunks; ++c) {
@@ -752,6 +884,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
       if constexpr (kSwiGLU) {
         swiglu_tile_epilogue<BN>(taddr, half, nb * kTileN, F, m, row_ok, rs, ep);
+      } else if constexpr (EPI == kEpiI8QkvNormRope) {
+        // BN = 256: each warp half owns one 128-column head
+        qkv_norm_rope_head(taddr + half * 128, nb * BN + half * 128, m, row_ok, rs, ep);
       } else {
 #pragma unroll 1
         for (int c = half * kChunks; c < (half + 1) * kChunks; ++c) {

@@ -163,6 +163,13 @@ struct EpiArgs {
   // instead of out[m*ldo + n].  Requires N == 3*H*D and D % 32 == 0.
   void* qkv[3];
   int qkv_heads, qkv_dim, qkv_seq;
+  // Q/K RMSNorm + split-half RoPE in the QKV epilogue (kEpiI8QkvNormRope):
+  // freqs [B*S, R, 2, 2] bf16, norm weights [D] fp32 for Q and K.
+  const __nv_bfloat16* rope_freqs;
+  const float* q_norm_w;
+  const float* k_norm_w;
+  int rope_r;
+  float norm_eps;
 };
 
 // Element pointer of output (m, n) for 16-bit outputs, in either layout.

@@ -148,12 +148,29 @@ B200Q_API int b200q_i8_matmul_nt_dequant_qkv(const int8_t* a, int64_t lda, const
                                              int64_t head_dim, int64_t batch, int64_t M,
                                              int64_t N, int64_t K, void* stream);
 
+/* b200q_i8_matmul_nt_dequant_qkv (bf16 out, head_dim 128) with Q and K
+ * RMS-normalized and rotated in the epilogue before the store, as
+ * b200q_rms_rope_partial would do afterwards: y = bf16((x * rsqrt(sum(x^2)/128 +
+ * eps)) * w) with q_weight / k_weight [128] fp32, then split-half RoPE on the
+ * first 2*rot_half dims with freqs [batch*seq, rot_half, 2, 2] bf16.  rot_half % 8
+ * == 0, 2*rot_half <= 128 (0: norm only); V is stored unnormalized.  Needs the
+ * TMA path (K % 16 == 0, lda/ldw % 16 == 0, 16-byte aligned a, w, outputs,
+ * freqs and weights).  Replaces i8_matmul2d_nt_fused_cs_qkv_rms_rope
+ * (_patches/int8_ext/int8_gemm.mm:2111, epilogue :672-862), batch 1 there. */
+B200Q_API int b200q_i8_matmul_nt_dequant_qkv_rms_rope(
+    const int8_t* a, int64_t lda, const int8_t* w, int64_t ldw, const float* row_scale,
+    const float* col_scale, int64_t col_scale_numel, const void* bias, void* q_out, void* k_out,
+    void* v_out, int64_t heads, int64_t batch, const void* freqs, int64_t rot_half,
+    const float* q_weight, const float* k_weight, float eps, int64_t M, int64_t N, int64_t K,
+    void* stream);
+
 /* In place on bf16 q, k [batch, heads, seq, head_dim] (contiguous): per row
  * RMSNorm y = bf16((x * rsqrt(sum(x^2)/D + eps)) * w) with fp32 weights
  * q_weight/k_weight [D], then split-half RoPE on the first 2*rot_half dims with
  * the bf16 rotation-matrix table freqs [batch*seq, rot_half, 2, 2] (diagonal
  * product rounded, then the off-diagonal product added with one rounding).
- * head_dim % 32 == 0, <= 256; rot_half = 0 skips RoPE.  Replaces
+ * head_dim % 32 == 0, <= 256; rot_half = 0 skips RoPE.  q, k 8-byte aligned,
+ * weights 16-byte aligned, freqs 16-byte aligned when rot_half % 4 == 0.  Replaces
  * rms_rope_attention_partial (_patches/dit_ext/dit_kernels.mm:825-874, 1677). */
 B200Q_API int b200q_rms_rope_partial(void* q, void* k, const void* freqs, const float* q_weight,
                                      const float* k_weight, int64_t batch, int64_t heads,

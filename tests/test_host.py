@@ -57,13 +57,17 @@ def test_abi_rejects_bad_arguments_without_a_gpu():
                                                4, 15, 16, None) == 1
     assert L.b200q_i8_mlp_bridge_prequant(None, 16, None, 16, None, None, 1, None, 4, 512, 16, 1,
                                           0, None, None, 256, None, None) == 1
+    assert L.b200q_i8_matmul_nt_dequant_qkv_rms_rope(None, 16, None, 16, None, None, 1, None, None,
+                                                     None, None, 1, 1, None, 8, None, None, 1e-6,
+                                                     4, 384, 16, None) == 1
 
 
 def test_torch_ops_registered_with_fake_kernels():
     for name in ("quant_rowwise_i8", "int_mm", "i8_matmul_nt", "i8_matmul_nt_fused",
                  "i8_matmul_nt_fused_cs", "i8_linear", "fp8_quant_tensorwise", "fp8_scaled_mm",
                  "w8a16_linear", "fp8_decode", "silu_mul_split", "i8_swiglu_rot",
-                 "i8_swiglu_quant", "i8_matmul_nt_fused_cs_swiglu", "i8_mlp_bridge_prequant"):
+                 "i8_swiglu_quant", "i8_matmul_nt_fused_cs_swiglu", "i8_mlp_bridge_prequant",
+                 "i8_matmul_nt_fused_cs_qkv_rms_rope"):
         assert hasattr(torch.ops.b200q, name)
     from torch._subclasses.fake_tensor import FakeTensorMode
     with FakeTensorMode():
