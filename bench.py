@@ -349,7 +349,9 @@ def run_b200q(args):
     world, rank, local = _dist_env()
     if world > 1:
         import datetime
-        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     _load_pack()
