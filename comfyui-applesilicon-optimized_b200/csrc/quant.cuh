@@ -82,59 +82,30 @@ __device__ __forceinline__ float warp_max(float v) {
 //
 // The reference computes q = round(x / s) with a correctly rounded fp32 divide
 // and then rounds that quotient to a coarser format F (bf16/fp16 before rint
-// for int8, e4m3 for fp8).  Here y = RN(x * r) with r = RN(1/s):
-//   y = (x/s)(1+d1)(1+d2), |d1|,|d2| <= 2^-24   =>   |y - RN(x/s)| <= 3 ulp.
-// Rounding to F drops the low bits of the fp32 pattern and only changes
-// outcome where those bits cross the tie pattern 100..0.  So when the dropped
-// bits of y are more than 4 ulps away from the tie, y and RN(x/s) round to the
-// same F value and y is used; otherwise (about 9 in 2^16 values for bf16) the
-// exact __fdiv_rn quotient is taken.  The result is therefore identical to
-// round_F(__fdiv_rn(x, s)) for every input.
-//
-// Range notes: for fp16 the 13-bit rule is only the tie rule in fp16's normal
-// range; below it (|y| < 2^-14) rint gives 0 whichever way the quotient
-// rounds, so the code is unaffected.  For e4m3 the 20-bit rule holds in the
-// normal range (|y| >= 2^-6); nonzero quotients below it take the exact path.
-template <typename T>
-struct TieBits;
-template <>
-struct TieBits<__nv_bfloat16> {
-  static constexpr uint32_t kMask = 0xFFFFu, kTie = 0x8000u;
-};
-template <>
-struct TieBits<__half> {
-  static constexpr uint32_t kMask = 0x1FFFu, kTie = 0x1000u;
-};
-
-template <typename T>
-__device__ __forceinline__ bool near_tie(float y) {
-  return (__float_as_uint(y) & TieBits<T>::kMask) - (TieBits<T>::kTie - 4u) <= 8u;
+// for int8, e4m3 for fp8).  Here, from r = RN(1/s):
+//   q0 = RN(x r)                      within 1.5 ulp of x/s;
+//   q1 = RN(q0 + RN(x - q0 s) r)      within half an ulp plus ~2^-47 relative,
+//                                     i.e. a faithful quotient;
+//   q2 = RN(q1 + (x - q1 s) r)        = RN(x / s) by Markstein's theorem (r the
+//                                     correctly rounded reciprocal, q1 faithful,
+//                                     x - q1 s exact as an fma).
+// Four fmas per element, no branch, and the result equals __fdiv_rn(x, s) for
+// every quotient in fp32's normal range; quotients below it (|x/s| < 2^-126)
+// round to code 0 / e4m3 zero whichever way they round.  The corrections turn
+// x = -0 into +0 (+0 + -0 = +0), so the sign is restored from x: with s > 0 (every
+// quantizer scale is) the quotient always has x's sign, and e4m3 keeps -0 apart.
+__device__ __forceinline__ float exact_quotient(float x, float s, float r) {
+  const float q0 = __fmul_rn(x, r);
+  const float q1 = __fmaf_rn(__fmaf_rn(-q0, s, x), r, q0);
+  return copysignf(__fmaf_rn(__fmaf_rn(-q1, s, x), r, q1), x);
 }
 
-__device__ __forceinline__ bool near_tie_e4m3(float y) {
-  const uint32_t b = __float_as_uint(y);
-  const uint32_t mag = b & 0x7FFFFFFFu;
-  return (mag < 0x3C800000u && mag != 0u) || (b & 0xFFFFFu) - (0x80000u - 4u) <= 8u;
-}
-
-// Eight quotients x[i] / s, each equal to __fdiv_rn(x[i], s) wherever the
-// rounding to F could tell them apart (F = T, or e4m3 when E4M3 is true).  The
-// exact divides sit in one rarely taken branch after the straight-line path.
+// Eight quotients x[i] / s, each equal to __fdiv_rn(x[i], s).
 template <typename T, bool E4M3>
 __device__ __forceinline__ void quotients8(const uint4& v, float s, float r, float (&y)[8]) {
   const T* e = reinterpret_cast<const T*>(&v);
-  uint32_t slow = 0u;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    y[i] = __fmul_rn(to_float<T>(e[i]), r);
-    const bool t = E4M3 ? near_tie_e4m3(y[i]) : near_tie<T>(y[i]);
-    slow |= t ? (1u << i) : 0u;
-  }
-  if (slow) {  // fully unrolled: a runtime index would move y[] to local memory
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      if ((slow >> i) & 1u) y[i] = __fdiv_rn(to_float<T>(e[i]), s);
-  }
+  for (int i = 0; i < 8; ++i) y[i] = exact_quotient(to_float<T>(e[i]), s, r);
 }
 
 // INT8 code of a quotient already rounded to T: rint (half-even), clamped to
@@ -162,24 +133,13 @@ __device__ __forceinline__ uint2 quant8_fast(const uint4& v, float s, float r) {
   return make_uint2(pack_low_bytes(c[0], c[1], c[2], c[3]), pack_low_bytes(c[4], c[5], c[6], c[7]));
 }
 
-// Four codes of T-valued inputs x[i] (rint(T(x/s)) clamped), packed; the same
-// divide-free quotient with the exact fallback near T's ties as quotients8.
+// Four codes of T-valued inputs x[i] (rint(T(x/s)) clamped), packed.
 template <typename T>
 __device__ __forceinline__ uint32_t quant4_fast(const float (&x)[4], float s, float r) {
-  float y[4];
-  uint32_t slow = 0u;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    y[i] = __fmul_rn(x[i], r);
-    slow |= near_tie<T>(y[i]) ? (1u << i) : 0u;
-  }
-  if (slow) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      if ((slow >> i) & 1u) y[i] = __fdiv_rn(x[i], s);
-  }
-  return pack_low_bytes(code_bits(round_to<T>(y[0])), code_bits(round_to<T>(y[1])),
-                        code_bits(round_to<T>(y[2])), code_bits(round_to<T>(y[3])));
+  return pack_low_bytes(code_bits(round_to<T>(exact_quotient(x[0], s, r))),
+                        code_bits(round_to<T>(exact_quotient(x[1], s, r))),
+                        code_bits(round_to<T>(exact_quotient(x[2], s, r))),
+                        code_bits(round_to<T>(exact_quotient(x[3], s, r))));
 }
 
 template <typename T>
