@@ -294,6 +294,43 @@ class B200Block:
         self.gemm_events.append((ev, e, 2.0 * self.M * layer.K * layer.N))
 
 
+def w8a16_back_to_back_ms(blk, reps=16, copies=4, iters=10):
+    """Average launch time of the small-M W8A16 linear (the HBM-bound case):
+    `reps` launches captured back to back in one CUDA graph, cycling through
+    `copies` copies of the layer-0 weight (together larger than L2, so every
+    launch streams its weight from HBM), one event pair per replay.  A single
+    launch between two events would also time the ~6 us event/launch overhead of
+    a graph replay, which is larger than the kernel itself at M <= 32."""
+    ops = torch.ops.b200q
+    l = blk.spec["layers"][0]
+    w, s, b = blk.weights[0]
+    x = blk.inputs[blk.spec["inputs"][0]]
+    act = l.act or "none"
+    ws = [w] + [w.clone() for _ in range(copies - 1)]
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        ops.w8a16_linear(x, w, s, b, act)
+    torch.cuda.current_stream().wait_stream(side)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(reps):
+            ops.w8a16_linear(x, ws[i % copies], s, b, act)
+    g.replay()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) / reps)
+    del g, ws
+    return statistics.median(ts)
+
+
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -416,8 +453,10 @@ def run_b200q(args):
                     else:
                         g.replay()
             barrier()
-    launches = (_native.launch_count() - launches0 if graphs is None
-                else launches_per_step * args.steps)
+        launches = (_native.launch_count() - launches0 if graphs is None
+                    else launches_per_step * args.steps)
+        b2b_ms = (w8a16_back_to_back_ms(blk) if spec["route"] == "w8a16" and M <= 256
+                  and graphs is not None else None)
     t_dev = sum(a.elapsed_time(b) for a, b in step_ms)
     gemm_ms = sum(a.elapsed_time(b) for a, b, _ in blk.gemm_events)
     gemm_flops = sum(f for _, _, f in blk.gemm_events)
@@ -461,11 +500,14 @@ def run_b200q(args):
     # roofline), so its roofline is bytes moved per launch / launch time.
     hbm_bound = spec["route"] == "w8a16" and M <= 256
     achieved_gbs, bytes_per_launch = None, 0
+    per_launch_event_gbs = None
     if hbm_bound and n_gemm:
         l0 = spec["layers"][0]
         bytes_per_launch = (l0.N * l0.K + M * l0.K * 2 + M * l0.N * 2 + l0.N * 2) * len(spec["layers"])
-        achieved_gbs = bytes_per_launch * n_gemm / (gemm_ms / 1e3) / 1e9 / len(spec["layers"]) \
+        per_launch_event_gbs = bytes_per_launch * n_gemm / (gemm_ms / 1e3) / 1e9 / len(spec["layers"]) \
             if gemm_ms > 0 else None
+        achieved_gbs = (bytes_per_launch / len(spec["layers"]) / (b2b_ms / 1e3) / 1e9
+                        if b2b_ms else per_launch_event_gbs)
     traffic, traffic_src = _committed_traffic(args.workload) if args.m is None else (None, None)
 
     if rank == 0:
@@ -498,11 +540,16 @@ def run_b200q(args):
                           "frac": round(achieved_gbs / peaks["hbm_gbs"], 4) if achieved_gbs else None,
                           "traffic": None, "traffic_source": None,
                           "algorithmic_bytes_per_launch": bytes_per_launch // len(spec["layers"]),
-                          "kernel": "w8a16_gemv_kernel" if M <= 32 else (
-                              "w8a16_stream_kernel" if M <= 64 else "w8a16_tc_kernel"),
+                          "kernel": "x_planes_kernel + w8a16_planes_kernel (activation planes on "
+                                    "kind::f8f6f4, one call = both launches)" if M <= 128 else
+                                    "e4m3_rows_to16_kernel + gemm8 kind::f16",
                           "peak_source": f"hbm_gbs of {peaks['source']} MEASURED_PEAKS.json",
-                          "timing": "CUDA events around each launch (includes ~6 us launch latency "
-                                    "measured for an empty kernel on this path)",
+                          "timing": ("16 calls back to back in one CUDA graph over 4 weight copies "
+                                     "(151 MB > L2), events around the replay, median of 10; per call"
+                                     if b2b_ms else "CUDA events around each launch"),
+                          "us_per_call": round(b2b_ms * 1e3, 2) if b2b_ms else None,
+                          "per_launch_event_gbs": (round(per_launch_event_gbs, 1)
+                                                   if per_launch_event_gbs else None),
                           "gemm_launches_timed": n_gemm} if hbm_bound else
                          {"bound": "tensor", "achieved": round(achieved, 1) if achieved else None,
                          "peak": round(peak, 1), "unit": "TFLOP/s",

@@ -13,7 +13,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 PACK = os.path.dirname(HERE)
 ROOT = os.path.dirname(PACK)
 OUT = os.path.join(PACK, "_lib", "libb200q.so")
-SOURCES = ["capi.cu", "gemm8.cuh", "prologue.cuh", "qkv_rope.cuh", "quant.cuh", "w8a16.cuh", "numerics.cuh", "ptx.cuh"]
+SOURCES = ["capi.cu", "gemm8.cuh", "prologue.cuh", "qkv_rope.cuh", "quant.cuh", "w8a16.cuh", "w8a16_planes.cuh", "numerics.cuh", "ptx.cuh"]
 HEADER = os.path.join(ROOT, "include", "b200q.h")
 
 

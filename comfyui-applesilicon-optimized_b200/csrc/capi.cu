@@ -16,6 +16,7 @@
 #include "qkv_rope.cuh"
 #include "quant.cuh"
 #include "w8a16.cuh"
+#include "w8a16_planes.cuh"
 
 using namespace b200q;
 
@@ -443,6 +444,239 @@ bool w8a16_gemv_selected(int64_t M) {
 bool sync_ok(const unsigned int* sync, size_t sync_bytes, int64_t M) {
   return sync && (reinterpret_cast<uintptr_t>(sync) & 15) == 0 &&
          sync_bytes >= b200q_prologue_sync_bytes(M);
+}
+
+// ---------------------------------------------------------------------------
+// W8A16 planes route (w8a16_planes.cuh): M <= 128 bf16 / M <= 64 fp16 tokens,
+// raw e4m3 weight tiles x exact e4m3 activation planes on kind::f8f6f4.
+// B200Q_W8A16_PLANES=0 turns it off (A/B runs); B200Q_W8A16_PLANES_SPLITS=n
+// forces the cluster size; B200Q_PDL=0 launches the GEMM without the
+// programmatic dependency on the planes pass.
+struct WpPlan {
+  bool ok = false;
+  int bt = 0, P = 0, nt = 0, S = 1, stages = 0, smem = 0;
+};
+
+bool env_flag(const char* name, bool dflt) {
+  const char* e = getenv(name);
+  return e ? e[0] != '0' : dflt;
+}
+// Read per call (a getenv), so tests can switch routes inside one process.
+// B200Q_W8A16_PLANES: unset = the token counts where the planes route measured
+// ahead of the decode-in-kernel kernels on B200 (33..64), "1" = every eligible
+// call, "0" = never.
+bool w8a16_planes_for(int64_t M) {
+  const char* e = getenv("B200Q_W8A16_PLANES");
+  if (e) return e[0] != '0';
+  return M > 32 && M <= 64;
+}
+bool pdl_on() { return env_flag("B200Q_PDL", true); }
+int wp_bt(int64_t M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128; }
+size_t wp_plane_bytes(int P, int bt, int64_t K) {
+  return (size_t(P) * size_t(bt) * size_t(K) + 255) & ~size_t(255);
+}
+size_t wp_workspace_bytes(int P, int bt, int64_t K) {
+  return wp_plane_bytes(P, bt, K) + size_t(P) * size_t(bt) * sizeof(float);
+}
+// Workspace of the planes route for either activation type (the size query
+// does not know the type): 0 when M is out of its range.
+size_t wp_workspace_any(int64_t M, int64_t K) {
+  if (!w8a16_planes_for(M) || M < 1 || M > 128 || K % 16 != 0 || K > kWpMaxK) return 0;
+  const int bt = wp_bt(M);
+  return wp_workspace_bytes(M <= 64 ? 3 : 2, bt, K);
+}
+
+template <int NT>
+int wp_max_clusters_for(int S, int smem) {
+  auto kern = w8a16_planes_kernel<NT>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return 0;
+  if (env_flag("B200Q_DEBUG_PLAN", false)) {
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kWpThreads, smem);
+    fprintf(stderr, "[b200q] planes GEMM NT %d smem %d: %d CTAs per SM\n", NT, smem, per_sm);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(S) * 16u);
+  cfg.blockDim = dim3(kWpThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = static_cast<unsigned>(S);
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  int n = 0;
+  const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    if (env_flag("B200Q_DEBUG_PLAN", false))
+      fprintf(stderr, "[b200q] cluster occupancy query (NT %d, S %d, smem %d): %s\n", NT, S, smem,
+              cudaGetErrorString(e));
+    return 0;
+  }
+  return n;
+}
+
+// Clusters of S CTAs that can be resident at once (cached per device and shape).
+int wp_max_clusters(int nt, int S, int smem) {
+  struct Entry { int dev, nt, S, smem, n; };
+  static Entry cache[64];
+  static int used = 0;
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    for (int i = 0; i < used; ++i)
+      if (cache[i].dev == dev && cache[i].nt == nt && cache[i].S == S && cache[i].smem == smem)
+        return cache[i].n;
+  }
+  int n = 0;
+  switch (nt) {
+    case 32: n = wp_max_clusters_for<32>(S, smem); break;
+    case 48: n = wp_max_clusters_for<48>(S, smem); break;
+    case 64: n = wp_max_clusters_for<64>(S, smem); break;
+    case 96: n = wp_max_clusters_for<96>(S, smem); break;
+    case 128: n = wp_max_clusters_for<128>(S, smem); break;
+    case 192: n = wp_max_clusters_for<192>(S, smem); break;
+    case 256: n = wp_max_clusters_for<256>(S, smem); break;
+    default: break;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  if (used < 64) cache[used++] = Entry{dev, nt, S, smem, n};
+  return n;
+}
+
+// Plan: the weight's 128-row tiles times S K-splits run as ONE wave of clusters
+// with 1 or 2 CTAs per SM; among those, the plan minimising the K extent each SM
+// streams (ceil(CTAs / SMs) / S of a tile row) wins, then the smaller S.
+WpPlan w8a16_planes_plan(const DeviceInfo* d, int64_t M, int64_t N, int64_t K, bool f16) {
+  WpPlan best;
+  if (!w8a16_planes_for(M) || M < 1 || M > (f16 ? 64 : 128) || K % 16 != 0 || K > kWpMaxK ||
+      N < 1 || N > (int64_t(1) << 24))
+    return best;
+  const int P = f16 ? 3 : 2;
+  const int bt = wp_bt(M);
+  const int nt = P * bt;
+  const int stage = 128 * kWpBK + nt * kWpBK;
+  const int dump = nt * 128 * 4;
+  const int tmem = nt <= 32 ? 32 : nt <= 64 ? 64 : nt <= 128 ? 128 : 256;
+  const int bar = (2 * kWpMaxStages + 1) * 8 + 16 + 1024;
+  const int64_t tiles = (N + 127) / 128;
+  const int nkb = static_cast<int>((K + kWpBK - 1) / kWpBK);
+  const char* fs = getenv("B200Q_W8A16_PLANES_SPLITS");
+  const int forced_s = fs ? atoi(fs) : 0;
+  double best_cost = 1e30;
+  for (int c = 1; c <= 2; ++c) {
+    if (c * tmem > 512) continue;
+    const int budget = (c == 1 ? 232448 : 233472 / c - 1024);  // per-CTA dynamic smem
+    int stages = (budget - bar) / stage;
+    if (stages > kWpMaxStages) stages = kWpMaxStages;
+    if (stages < 2 || dump + bar > budget) continue;
+    const int ring = stages * stage > dump ? stages * stage : dump;
+    const int smem = ring + bar;
+    for (int S = 1; S <= 8 && S <= nkb; ++S) {
+      if (forced_s > 0 && S != forced_s) continue;
+      const int64_t ctas = tiles * S;
+      if (ctas > int64_t(c) * d->num_sms && forced_s == 0) continue;
+      const int64_t per_sm = (ctas + d->num_sms - 1) / d->num_sms;
+      const double cost = double(per_sm) / S;
+      if (env_flag("B200Q_DEBUG_PLAN", false))
+        fprintf(stderr, "[b200q] planes plan M %lld N %lld K %lld: c %d S %d stages %d smem %d "
+                "clusters %d (need %lld) cost %.3f\n", (long long)M, (long long)N, (long long)K, c,
+                S, stages, smem, S > 1 ? wp_max_clusters(nt, S, smem) : -1, (long long)tiles, cost);
+      // A forced cluster size (measurements) skips the single-wave check.
+      if (S > 1 && forced_s == 0 && wp_max_clusters(nt, S, smem) < tiles) continue;
+      if (cost < best_cost - 1e-9) {
+        best_cost = cost;
+        best.ok = true;
+        best.bt = bt;
+        best.P = P;
+        best.nt = nt;
+        best.S = S;
+        best.stages = stages;
+        best.smem = smem;
+      }
+    }
+  }
+  return best;
+}
+
+template <int NT>
+int launch_planes_gemm(const WpPlan& p, const CUtensorMap& tw, const CUtensorMap& tx,
+                       const WpArgs& args, const EpiArgs& ep, cudaStream_t st) {
+  auto kern = w8a16_planes_kernel<NT>;
+  if (!set_smem(kern, p.smem)) return B200Q_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>((args.N + 127) / 128 * p.S));
+  cfg.blockDim = dim3(kWpThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(p.smem);
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  int na = 0;
+  if (pdl_on()) {
+    at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (p.S > 1) {
+    at[na].id = cudaLaunchAttributeClusterDimension;
+    at[na].val.clusterDim.x = static_cast<unsigned>(p.S);
+    at[na].val.clusterDim.y = 1;
+    at[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = at;
+  cfg.numAttrs = na;
+  cudaLaunchKernelEx(&cfg, kern, tw, tx, args, ep);  // errors surface in finish_launch
+  return finish_launch();
+}
+
+int launch_w8a16_planes(const WpPlan& p, const void* x, int x_dtype, int64_t ldx, const uint8_t* w,
+                        int64_t ldw, int64_t M, int64_t N, int64_t K, const EpiArgs& ep,
+                        void* workspace, cudaStream_t st) {
+  uint8_t* planes = static_cast<uint8_t*>(workspace);
+  float* pscale = reinterpret_cast<float*>(planes + wp_plane_bytes(p.P, p.bt, K));
+  const dim3 pgrid(static_cast<unsigned>(M));
+  const int row_smem = static_cast<int>(K) * 2;
+  if (x_dtype == B200Q_F16) {
+    if (!set_smem(x_planes_kernel<__half, 3>, row_smem)) return B200Q_ERR_CUDA;
+    x_planes_kernel<__half, 3><<<pgrid, kWpPlaneThreads, row_smem, st>>>(
+        static_cast<const __half*>(x), ldx, int(K), p.bt, planes, pscale);
+  } else {
+    if (!set_smem(x_planes_kernel<__nv_bfloat16, 2>, row_smem)) return B200Q_ERR_CUDA;
+    x_planes_kernel<__nv_bfloat16, 2><<<pgrid, kWpPlaneThreads, row_smem, st>>>(
+        static_cast<const __nv_bfloat16*>(x), ldx, int(K), p.bt, planes, pscale);
+  }
+  int s = finish_launch();
+  if (s != B200Q_OK) return s;
+  CUtensorMap tw, tx;
+  if (!make_tmap(&tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldw, kWpBK, 128,
+                 CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tmap(&tx, planes, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, uint64_t(p.P) * p.bt, K, kWpBK,
+                 p.nt, CU_TENSOR_MAP_SWIZZLE_128B))
+    return B200Q_ERR_CUDA;
+  WpArgs args{};
+  args.M = int(M);
+  args.N = int(N);
+  args.K = int(K);
+  args.bt = p.bt;
+  args.planes = p.P;
+  args.splits = p.S;
+  args.stages = p.stages;
+  args.pscale = pscale;
+  switch (p.nt) {
+    case 32: return launch_planes_gemm<32>(p, tw, tx, args, ep, st);
+    case 48: return launch_planes_gemm<48>(p, tw, tx, args, ep, st);
+    case 64: return launch_planes_gemm<64>(p, tw, tx, args, ep, st);
+    case 96: return launch_planes_gemm<96>(p, tw, tx, args, ep, st);
+    case 128: return launch_planes_gemm<128>(p, tw, tx, args, ep, st);
+    case 192: return launch_planes_gemm<192>(p, tw, tx, args, ep, st);
+    case 256: return launch_planes_gemm<256>(p, tw, tx, args, ep, st);
+    default: return B200Q_ERR_INVALID;
+  }
 }
 
 int grid_for(int64_t work, int per_block, const DeviceInfo* d) {
@@ -922,10 +1156,13 @@ size_t w8a16_kernel_workspace(int64_t M, int64_t N, int64_t K) {
 extern "C" {
 
 size_t b200q_w8a16_workspace_size(int64_t M, int64_t N, int64_t K) {
-  const size_t kernel_ws = w8a16_kernel_workspace(M, N, K);
-  if (M <= 0 || N <= 0 || K <= 0 || !w8a16_decode_selected(M, N, K)) return kernel_ws;
+  size_t ws = w8a16_kernel_workspace(M, N, K);
+  if (M <= 0 || N <= 0 || K <= 0) return ws;
+  const size_t planes = wp_workspace_any(M, K);
+  if (planes > ws) ws = planes;
+  if (!w8a16_decode_selected(M, N, K)) return ws;
   const size_t dec = w8a16_decode_bytes(N, K);
-  return dec > kernel_ws ? dec : kernel_ws;
+  return dec > ws ? dec : ws;
 }
 
 }  // extern "C"
@@ -958,6 +1195,11 @@ int w8a16_linear_impl(const void* x, int x_dtype, int64_t ldx, const uint8_t* w,
     else
       w8a16_simt_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(x), ldx, w, ldw, int(M), int(N), int(K), ep);
     return finish_launch();
+  }
+  if (workspace && aligned16(workspace)) {
+    const WpPlan wp = w8a16_planes_plan(d, M, N, K, x_dtype == B200Q_F16);
+    if (wp.ok && workspace_bytes >= wp_workspace_bytes(wp.P, wp.bt, K))
+      return launch_w8a16_planes(wp, x, x_dtype, ldx, w, ldw, M, N, K, ep, workspace, st);
   }
   if (w8a16_gemv_selected(M)) {
     if (M <= 16)
@@ -1050,8 +1292,10 @@ int b200q_w8a16_linear_noalloc(const void* x, int x_dtype, int64_t ldx, const ui
                                int act, void* out, int out_dtype, int64_t ldo, int64_t M, int64_t N,
                                int64_t K, void* stream) {
   if (!x || !w || !out || !valid_dims(M, N, K) || K == 0) return B200Q_ERR_INVALID;
-  const size_t need = w8a16_kernel_workspace(M, N, K);
+  size_t need = w8a16_kernel_workspace(M, N, K);
   if (need > B200Q_NOALLOC_SCRATCH_BYTES) return B200Q_ERR_TOO_LARGE;
+  const size_t planes = wp_workspace_any(M, K);  // optional: used when it fits
+  if (planes > need && planes <= B200Q_NOALLOC_SCRATCH_BYTES) need = planes;
   void* scratch = nullptr;
   if (need) {
     const int st = noalloc_scratch(&scratch);

@@ -1,0 +1,421 @@
+// FP8 weight-only W8A16 for small token counts without decoding the weight.
+//
+// At M <= 128 the W8A16 linear is bound by the e4m3 weight stream from HBM (one
+// byte per weight).  Decoding each weight to bf16 on the SMs costs ~4 ALU
+// instructions per pair of weights, which at HBM rate takes about half of every
+// SM's issue slots; instead, the activations (few rows) are split exactly into
+// e4m3 "planes" and the tensor cores multiply the raw weight tile with them
+// (tcgen05 kind::f8f6f4), so the weight goes TMA -> shared memory -> MMA with no
+// instruction touching it:
+//
+//   x[t,k]   = sum_p q_p[t,k] * 2^-e_p[t]          q_p e4m3, e_p a per-row exponent
+//   out[t,n] = act( (sum_p 2^-e_p[t] * sum_k W[n,k] q_p[t,k]) * w_scale + bias[n] )
+//
+// Plane 0 is x * 2^e_0 rounded to e4m3, with e_0 putting the row's |x| maximum in
+// [128, 256); plane p+1 is the remainder of plane p, rescaled the same way by its
+// own maximum.  A bf16 value has 8 significant bits and a rounded e4m3 plane
+// keeps 4 of them, so two planes hold a bf16 row exactly (fp16: 11 bits, three
+// planes) -- except for elements more than ~2^13 below the row maximum, whose
+// last bits fall under e4m3's subnormal spacing; the part lost there is below
+// 2^-21 of the row maximum, far under the fp32 rounding of the dot product.
+//
+// Kernels (one call = the planes pass, then the GEMM launched as its
+// programmatic dependent, so the GEMM's CTAs start streaming weights while the
+// planes are being written):
+//   x_planes_kernel   one CTA per token row: |x| max, planes, plane scales.
+//   w8a16_planes_kernel<NT>
+//     weight-stationary tile: MMA M = 128 weight rows, N = NT = P x BT plane rows
+//     (BT tokens padded to 16/32/64/128), D^T[n, p*BT + t] in TMEM (fp32).
+//     warp 0   TMA producer: 128 x 128 B weight tile + NT x 128 B plane tile per
+//              stage, 128-byte swizzle; the weight loads of the first stages are
+//              issued before griddepcontrol.wait, the plane loads after it.
+//     warp 1   MMA issuer: 4 x kind::f8f6f4 (K = 32) per stage.
+//     warp 2   TMEM allocator.
+//     warps 4..7  epilogue, one thread per weight row (TMEM lane).
+//   Split-K for occupancy: a cluster of S CTAs shares a weight tile, CTA rank s
+//   taking K blocks [s*nkb/S, (s+1)*nkb/S).  Ranks 1..S-1 dump their fp32
+//   accumulators into their own (drained) ring memory; rank 0 adds them in rank
+//   order through distributed shared memory (fixed order, so results are
+//   bit-reproducible), combines the planes and runs the epilogue.  No global
+//   workspace, counters or memset node is involved.
+#pragma once
+
+#include <type_traits>
+
+#include "w8a16.cuh"
+
+namespace b200q {
+
+constexpr int kWpBK = 128;          // K bytes per stage (one 128-byte swizzle atom)
+constexpr int kWpThreads = 256;
+constexpr int kWpMaxStages = 8;
+constexpr int kWpPlaneThreads = 256;
+
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t cluster_addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
+  return v;
+}
+
+template <int NT>
+struct WpLayout {
+  static constexpr int kWSlot = 128 * kWpBK;  // e4m3 weight tile
+  static constexpr int kXSlot = NT * kWpBK;   // e4m3 plane tile
+  static constexpr int kStage = kWSlot + kXSlot;
+  static constexpr int kDump = NT * 128 * 4;  // fp32 accumulators, [column][row]
+  static constexpr uint32_t kTmemCols = NT <= 32 ? 32 : NT <= 64 ? 64 : NT <= 128 ? 128 : 256;
+  // full[8], empty[8], acc_full, tmem slot, abort flag
+  static constexpr int kBarBytes = (2 * kWpMaxStages + 1) * 8 + 16;
+  __host__ __device__ static constexpr int ring_bytes(int stages) {
+    return stages * kStage > kDump ? stages * kStage : kDump;
+  }
+  __host__ __device__ static constexpr int smem_bytes(int stages) {
+    return ring_bytes(stages) + kBarBytes + 1024;
+  }
+};
+
+struct WpArgs {
+  int M, N, K;
+  int bt;                 // tokens per plane (16, 32, 64 or 128)
+  int planes;             // P = 2 (bf16 activations) or 3 (fp16)
+  int splits;             // cluster size S
+  int stages;             // ring depth (<= kWpMaxStages)
+  const float* pscale;    // [P][bt]: 2^-e_p[t]
+};
+
+// ---------------------------------------------------------------------------
+// Planes of one activation row.  The row is read once from global memory into
+// shared memory (16-byte vectors: K % 8 == 0 and 16-byte aligned rows, checked
+// by the host; K <= kWpMaxK) and every pass (max; plane 0 and its remainder's
+// max; plane 1 ...) reads it from there.  A row holding an infinity or NaN gets
+// NaN plane scales, so its whole output row is NaN.
+constexpr int kWpMaxK = 32768;  // 64 KB of bf16 / fp16 row in shared memory
+
+// Largest e with max * 2^e < 256 and max * 2^e >= 128 for a normal max, clamped
+// so that 2^(total) and 2^-(total) stay normal floats.
+__device__ __forceinline__ int plane_exponent(float amax, int used) {
+  if (!(amax > 0.0f)) return 0;
+  const int E = static_cast<int>((__float_as_uint(amax) >> 23) & 0xFFu);  // biased exponent
+  int e = 134 - E;                       // amax in [2^(E-127), 2^(E-126)) -> [128, 256)
+  if (e > 126 - used) e = 126 - used;    // keep 2^-(used + e) a normal float
+  if (e < -120) e = -120;
+  return e;
+}
+__device__ __forceinline__ float exp2i(int e) {  // 2^e for -126 <= e <= 127
+  return __uint_as_float(static_cast<uint32_t>(e + 127) << 23);
+}
+
+template <typename XT>
+__device__ __forceinline__ void unpack8f(const uint4 u, float (&v)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (std::is_same<XT, __half>::value) {
+      __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+      const float2 f = __half22float2(h);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    } else {
+      v[2 * i] = __uint_as_float(w[i] << 16);
+      v[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+  }
+}
+
+// e4m3 round-to-nearest-even of two floats (|v| <= 256 here, never saturates),
+// returned as the code pair and as the decoded values.
+__device__ __forceinline__ uint16_t e4m3x2_rn(float a, float b, float& da, float& db) {
+  const __nv_fp8x2_storage_t c = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(c, __NV_E4M3);
+  const float2 f = __half22float2(__half2(h));
+  da = f.x;
+  db = f.y;
+  return static_cast<uint16_t>(c);
+}
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int warp = threadIdx.x >> 5;
+  __syncthreads();  // red[] free from the previous use
+  if ((threadIdx.x & 31) == 0) red[warp] = v;
+  __syncthreads();
+  float m = red[0];
+#pragma unroll
+  for (int w = 1; w < kWpPlaneThreads / 32; ++w) m = fmaxf(m, red[w]);
+  return m;
+}
+
+// Grid: one CTA per token row t < M.  planes: [P][bt][K] bytes; pscale [P][bt].
+template <typename XT, int P>
+__global__ void __launch_bounds__(kWpPlaneThreads)
+    x_planes_kernel(const XT* __restrict__ x, int64_t ldx, int K, int bt,
+                    uint8_t* __restrict__ planes, float* __restrict__ pscale) {
+  griddep_launch_dependents();  // the GEMM may start streaming weights now
+  __shared__ float red[kWpPlaneThreads / 32];
+  extern __shared__ uint4 srow[];  // the row, K / 8 vectors
+  const int t = blockIdx.x;
+  const uint4* row = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t) * ldx);
+  const int64_t plane_stride = static_cast<int64_t>(bt) * K;
+  uint8_t* out0 = planes + static_cast<int64_t>(t) * K;
+  const int nv = K / 8;
+
+  // max |x|, and whether the row is finite; the row is kept in shared memory
+  float amax = 0.0f;
+  bool finite = true;
+  for (int i = threadIdx.x; i < nv; i += kWpPlaneThreads) {
+    const uint4 u = __ldg(row + i);
+    srow[i] = u;
+    float v[8];
+    unpack8f<XT>(u, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float a = fabsf(v[i]);
+      finite = finite && a <= 3.402823466e38f;
+      amax = fmaxf(amax, a);
+    }
+  }
+  const bool all_finite = __syncthreads_and(finite) != 0;
+  amax = block_max(amax, red);
+  int e_tot[P];  // plane p holds x's remainder scaled by 2^e_tot[p]
+  e_tot[0] = plane_exponent(amax, 0);
+  int used = e_tot[0];
+  const float mult0 = exp2i(e_tot[0]);
+
+  // Plane p pass: recompute planes 0..p-1 (their remainders), write plane p,
+  // and take the max of the remainder after it.
+#pragma unroll
+  for (int p = 0; p < P; ++p) {
+    float rmax = 0.0f;
+    for (int i = threadIdx.x; i < nv; i += kWpPlaneThreads) {
+      const int k = i * 8;
+      float v[8];
+      unpack8f<XT>(srow[i], v);
+      uint32_t codes[2] = {0u, 0u};
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        float r0 = v[i] * mult0, r1 = v[i + 1] * mult0;  // exact (power of two)
+        uint16_t c = 0;
+#pragma unroll
+        for (int j = 0; j <= p; ++j) {
+          if (j > 0) {  // rescale the remainder to plane j's range (exact)
+            const float s = exp2i(e_tot[j] - e_tot[j - 1]);
+            r0 *= s;
+            r1 *= s;
+          }
+          float d0, d1;
+          c = e4m3x2_rn(r0, r1, d0, d1);
+          r0 -= d0;  // exact: the remainder of a rounding to a coarser grid
+          r1 -= d1;
+        }
+        codes[i >> 2] |= static_cast<uint32_t>(c) << ((i & 2) * 8);
+        rmax = fmaxf(rmax, fmaxf(fabsf(r0), fabsf(r1)));
+      }
+      *reinterpret_cast<uint2*>(out0 + p * plane_stride + k) = make_uint2(codes[0], codes[1]);
+    }
+    if (p + 1 < P) {
+      rmax = block_max(rmax, red);
+      // The remainder is in plane p's units: its exponent adds to e_tot[p].
+      used += plane_exponent(rmax, used);
+      e_tot[p + 1] = used;
+    }
+  }
+  if (threadIdx.x == 0) {
+    const float nan = __uint_as_float(0x7FC00000u);
+#pragma unroll
+    for (int p = 0; p < P; ++p) pscale[p * bt + t] = all_finite ? exp2i(-e_tot[p]) : nan;
+  }
+}
+
+// ---------------------------------------------------------------------------
+template <int NT>
+__global__ void __launch_bounds__(kWpThreads, 2)
+    w8a16_planes_kernel(const __grid_constant__ CUtensorMap tmW,
+                        const __grid_constant__ CUtensorMap tmX, WpArgs a, EpiArgs ep) {
+  using L = WpLayout<NT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int stages = a.stages;
+  const int ring = L::ring_bytes(stages);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + ring);
+  uint64_t* empty = full + kWpMaxStages;
+  uint64_t* acc_full = empty + kWpMaxStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* dump = reinterpret_cast<float*>(smem);  // reuses the drained ring
+  __shared__ float s_pscale[3 * 128];            // [P][bt] plane scales
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int S = a.splits;
+  const int split = S > 1 ? static_cast<int>(cluster_ctarank()) : 0;
+  const int tile = blockIdx.x / S;
+  const int nkb = (a.K + kWpBK - 1) / kWpBK;
+  const int kb0 = split * nkb / S, kb1 = (split + 1) * nkb / S;
+  const int nst = kb1 - kb0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmX);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_d = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const int pre = nst < stages ? nst : stages;
+      // The weights were written before the planes pass started, so they may be
+      // read before this grid's dependency on that pass resolves.
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], L::kStage);
+        tma_load_2d(&tmW, &full[i], smem + i * L::kStage, (kb0 + i) * kWpBK, tile * 128);
+      }
+      griddep_wait();
+      for (int i = 0; i < pre; ++i)
+        tma_load_2d(&tmX, &full[i], smem + i * L::kStage + L::kWSlot, (kb0 + i) * kWpBK, 0);
+      int issued = pre;
+      bool ok = true;
+      for (int i = pre; i < nst; ++i) {
+        const int s = i % stages;
+        const uint32_t ph = static_cast<uint32_t>(i / stages) & 1u;
+        if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) { ok = false; break; }
+        mbar_arrive_expect_tx(&full[s], L::kStage);
+        uint8_t* dst = smem + s * L::kStage;
+        tma_load_2d(&tmW, &full[s], dst, (kb0 + i) * kWpBK, tile * 128);
+        tma_load_2d(&tmX, &full[s], dst + L::kWSlot, (kb0 + i) * kWpBK, 0);
+        issued = i + 1;
+      }
+      if (!ok) {
+        // Let the copies still in flight land before the ring is reused or freed.
+        for (int i = issued - stages < 0 ? 0 : issued - stages; i < issued; ++i)
+          mbar_wait_drain(&full[i % stages], static_cast<uint32_t>(i / stages) & 1u);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdesc = kind_idesc<MmaKind::F8F6F4>(128, NT);
+      bool ok = true;
+      for (int i = 0; i < nst; ++i) {
+        const int s = i % stages;
+        if (!mbar_wait(&full[s], static_cast<uint32_t>(i / stages) & 1u, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint64_t adesc = make_sw128_desc(smem_u32(smem + s * L::kStage));
+        const uint64_t bdesc = make_sw128_desc(smem_u32(smem + s * L::kStage + L::kWSlot));
+#pragma unroll
+        for (int k = 0; k < 4; ++k)  // K = 32 bytes per MMA = +2 in the >>4 address field
+          umma_ss<MmaKind::F8F6F4>(tmem_d, adesc + 2 * k, bdesc + 2 * k, kIdesc,
+                                   (i > 0 || k > 0) ? 1u : 0u);
+        umma_commit(&empty[s]);
+      }
+      if (ok) umma_commit(acc_full);
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int r = q * 32 + lane;  // weight row in the tile = TMEM lane
+    const uint32_t taddr = tmem_d + (static_cast<uint32_t>(q * 32) << 16);
+    const bool valid = mbar_wait_warp(acc_full, 0u, abort_flag);
+    tc_fence_after();
+    if (split > 0) {
+      // Ranks 1..S-1: accumulators -> own shared memory, [column][row].
+#pragma unroll 1
+      for (int c = 0; valid && c < NT; c += 16) {
+        uint32_t v[16];
+        tmem_ld_cols<16>(taddr + c, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) dump[(c + j) * 128 + r] = __uint_as_float(v[j]);
+      }
+    }
+  }
+
+  if (S > 1) cluster_sync();  // every rank's dump is written and visible
+
+  if (warp >= 4 && split == 0) {
+    griddep_wait();  // plane scales come from the planes pass
+    // Stage the P x bt plane scales in shared memory once: the per-token reads
+    // below are then broadcasts instead of a dependent global load per token.
+    for (int i = threadIdx.x - 128; i < a.planes * a.bt; i += 128) s_pscale[i] = a.pscale[i];
+    named_bar_sync(1, 128);
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const int n = tile * 128 + r;
+    const bool n_ok = n < a.N;
+    const uint32_t taddr = tmem_d + (static_cast<uint32_t>(q * 32) << 16);
+    const bool valid = *abort_flag == 0;
+    const float xs = ep.extra_scale ? __ldg(ep.extra_scale) : 1.0f;
+    const float bias_v = (n_ok && ep.bias_dtype != kBiasNone) ? load_bias(ep.bias, ep.bias_dtype, n) : 0.0f;
+    const int bt = a.bt;
+    const uint32_t dump_base = smem_u32(dump);
+#pragma unroll 1
+    for (int t0 = 0; valid && t0 < a.M; t0 += 16) {
+      float acc[3][16];
+#pragma unroll
+      for (int p = 0; p < 3; ++p) {
+        if (p >= a.planes) break;
+        uint32_t v[16];
+        tmem_ld_cols<16>(taddr + p * bt + t0, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[p][j] = __uint_as_float(v[j]);
+        for (int s2 = 1; s2 < S; ++s2) {  // rank order: ((D_0 + D_1) + D_2) + ...
+          const uint32_t peer = mapa_shared(dump_base, static_cast<uint32_t>(s2));
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            acc[p][j] = __fadd_rn(acc[p][j], ld_dsmem_f32(peer + ((p * bt + t0 + j) * 128 + r) * 4));
+        }
+      }
+      // Tokens t0 .. t0+15 < bt always index valid (if unused) plane columns and
+      // scales; only the stores are limited to tokens < M.
+      float out_v[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        float v = __fmul_rn(acc[0][j], s_pscale[t0 + j]);
+        v = __fadd_rn(v, __fmul_rn(acc[1][j], s_pscale[bt + t0 + j]));
+        if (a.planes > 2) v = __fadd_rn(v, __fmul_rn(acc[2][j], s_pscale[2 * bt + t0 + j]));
+        if (ep.extra_scale) v = __fmul_rn(v, xs);
+        if (ep.bias_dtype != kBiasNone) v = __fadd_rn(v, bias_v);
+        out_v[j] = apply_act(v, ep.act);
+      }
+      if (n_ok) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (t0 + j < a.M) store_out(ep, t0 + j, n, out_v[j]);
+      }
+    }
+  }
+
+  if (S > 1) cluster_sync();  // rank 0 has read every peer's dump
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 2) tmem_dealloc(tmem_d, L::kTmemCols);
+}
+
+}  // namespace b200q

@@ -307,6 +307,54 @@ def w8a16_linear(x, w, w_scale=None, bias=None, act=None, out_dtype=None):
     return res.reshape(*shp[:-1], w.shape[0])
 
 
+def _plane_exponent(amax, used):
+    """Per row: e with amax * 2^e in [128, 256) (amax normal), 0 for amax == 0 or
+    NaN, clamped to [-120, 126 - used] (the GEMM's planes pass, plane_exponent)."""
+    a = amax.astype(np.float32)
+    E = ((a.view(np.uint32) >> 23) & 0xFF).astype(np.int64)
+    e = 134 - E
+    e = np.minimum(e, 126 - used)
+    e = np.maximum(e, -120)
+    return np.where(a > 0, e, 0)
+
+
+def x_planes(x, planes):
+    """Exact e4m3 plane split of activation rows (the small-M W8A16 route's
+    planes pass, b200q's own design -- no reference counterpart; the reference
+    decodes the weight instead): returns (codes uint8 [P, M, K], exponents int
+    [P, M]) with x = sum_p decode(codes[p]) * 2^-exponents[p] (exact for bf16
+    with P = 2 and fp16 with P = 3, up to elements far below the row maximum).
+    Plane 0 is x * 2^e0 rounded (RNE) to e4m3; plane p+1 is the remainder of
+    plane p times 2^(e_{p+1} - e_p), both exponents chosen so the maximum lands
+    in [128, 256)."""
+    xf = to_f32(x).reshape(-1, x.shape[-1]).astype(np.float32)
+    with np.errstate(invalid="ignore"):
+        amax = np.nanmax(np.abs(xf), axis=1) if xf.shape[1] else np.zeros(xf.shape[0], np.float32)
+    amax = np.nan_to_num(amax, nan=0.0)
+    used = _plane_exponent(amax, np.zeros_like(amax, dtype=np.int64))
+    exps = [used.copy()]
+    r = xf * np.exp2(used.astype(np.float64)).astype(np.float32)[:, None]
+    codes = []
+    for p in range(planes):
+        q = torch.from_numpy(np.ascontiguousarray(r)).to(torch.float8_e4m3fn)
+        codes.append(q.view(torch.uint8).numpy().copy())
+        r = (r - q.float().numpy()).astype(np.float32)
+        if p + 1 < planes:
+            rmax = np.abs(r).max(axis=1) if r.shape[1] else np.zeros(r.shape[0], np.float32)
+            e = _plane_exponent(np.nan_to_num(rmax, nan=0.0), used)
+            used = used + e
+            exps.append(used.copy())
+            r = (r * np.exp2(e.astype(np.float64)).astype(np.float32)[:, None]).astype(np.float32)
+    return np.stack(codes), np.stack(exps)
+
+
+def x_planes_value(codes, exps):
+    """sum_p decode(codes[p]) * 2^-exps[p] in float64 ([M, K])."""
+    dec = decode_fp8(torch.from_numpy(codes).view(torch.float8_e4m3fn), torch.float32).numpy()
+    return sum(dec[p].astype(np.float64) * np.exp2(-exps[p].astype(np.float64))[:, None]
+               for p in range(codes.shape[0]))
+
+
 # ------------------------------------------------------------------ error metrics
 def fp8_errors(out, ref):
     """(max|d| / rms(ref), max|d| / max|ref|): the BASELINE bound and the
