@@ -462,13 +462,14 @@ bool env_flag(const char* name, bool dflt) {
   return e ? e[0] != '0' : dflt;
 }
 // Read per call (a getenv), so tests can switch routes inside one process.
-// B200Q_W8A16_PLANES: unset = the token counts where the planes route measured
-// ahead of the decode-in-kernel kernels on B200 (33..64), "1" = every eligible
-// call, "0" = never.
-bool w8a16_planes_for(int64_t M) {
+// B200Q_W8A16_PLANES: unset = where the planes route measured at least level
+// with the decode-in-kernel kernels on B200 (back-to-back calls, weights larger
+// than L2): every M > 16, and M <= 16 when K > 4096 (at K = 3072 the GEMV is
+// ~8% ahead for M <= 16); "1" = every eligible call, "0" = never.
+bool w8a16_planes_for(int64_t M, int64_t K) {
   const char* e = getenv("B200Q_W8A16_PLANES");
   if (e) return e[0] != '0';
-  return M > 32 && M <= 64;
+  return M > 16 || K > 4096;
 }
 bool pdl_on() { return env_flag("B200Q_PDL", true); }
 int wp_bt(int64_t M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128; }
@@ -481,80 +482,22 @@ size_t wp_workspace_bytes(int P, int bt, int64_t K) {
 // Workspace of the planes route for either activation type (the size query
 // does not know the type): 0 when M is out of its range.
 size_t wp_workspace_any(int64_t M, int64_t K) {
-  if (!w8a16_planes_for(M) || M < 1 || M > 128 || K % 16 != 0 || K > kWpMaxK) return 0;
+  if (!w8a16_planes_for(M, K) || M < 1 || M > 128 || K % 16 != 0 || K > kWpMaxK) return 0;
   const int bt = wp_bt(M);
   return wp_workspace_bytes(M <= 64 ? 3 : 2, bt, K);
 }
 
-template <int NT>
-int wp_max_clusters_for(int S, int smem) {
-  auto kern = w8a16_planes_kernel<NT>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-    return 0;
-  if (env_flag("B200Q_DEBUG_PLAN", false)) {
-    int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kWpThreads, smem);
-    fprintf(stderr, "[b200q] planes GEMM NT %d smem %d: %d CTAs per SM\n", NT, smem, per_sm);
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(S) * 16u);
-  cfg.blockDim = dim3(kWpThreads);
-  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeClusterDimension;
-  at[0].val.clusterDim.x = static_cast<unsigned>(S);
-  at[0].val.clusterDim.y = 1;
-  at[0].val.clusterDim.z = 1;
-  cfg.attrs = at;
-  cfg.numAttrs = 1;
-  int n = 0;
-  const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
-  if (e != cudaSuccess) {
-    cudaGetLastError();
-    if (env_flag("B200Q_DEBUG_PLAN", false))
-      fprintf(stderr, "[b200q] cluster occupancy query (NT %d, S %d, smem %d): %s\n", NT, S, smem,
-              cudaGetErrorString(e));
-    return 0;
-  }
-  return n;
-}
-
-// Clusters of S CTAs that can be resident at once (cached per device and shape).
-int wp_max_clusters(int nt, int S, int smem) {
-  struct Entry { int dev, nt, S, smem, n; };
-  static Entry cache[64];
-  static int used = 0;
-  static std::mutex mu;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    for (int i = 0; i < used; ++i)
-      if (cache[i].dev == dev && cache[i].nt == nt && cache[i].S == S && cache[i].smem == smem)
-        return cache[i].n;
-  }
-  int n = 0;
-  switch (nt) {
-    case 32: n = wp_max_clusters_for<32>(S, smem); break;
-    case 48: n = wp_max_clusters_for<48>(S, smem); break;
-    case 64: n = wp_max_clusters_for<64>(S, smem); break;
-    case 96: n = wp_max_clusters_for<96>(S, smem); break;
-    case 128: n = wp_max_clusters_for<128>(S, smem); break;
-    case 192: n = wp_max_clusters_for<192>(S, smem); break;
-    case 256: n = wp_max_clusters_for<256>(S, smem); break;
-    default: break;
-  }
-  std::lock_guard<std::mutex> lk(mu);
-  if (used < 64) cache[used++] = Entry{dev, nt, S, smem, n};
-  return n;
-}
-
-// Plan: the weight's 128-row tiles times S K-splits run as ONE wave of clusters
-// with 1 or 2 CTAs per SM; among those, the plan minimising the K extent each SM
-// streams (ceil(CTAs / SMs) / S of a tile row) wins, then the smaller S.
+// Plan: the weight's 128-row tiles times S K-splits (one cluster of S CTAs per
+// tile), with the ring sized for 1 or 2 CTAs per SM.  Cost model, from B200
+// measurements of this kernel: a CTA streams its weight at ~45 GB/s with its
+// ring full, the GPU at ~6 TB/s; every split adds a reduction step.  Only
+// plans that are resident in one wave are taken; two CTAs per SM were measured
+// to co-reside (the occupancy calculator reports one), and with clusters of
+// S > 1 about 10% of the slots are lost to cluster placement (S = 3 at 2 per SM
+// did not fit 288 CTAs on 148 SMs).
 WpPlan w8a16_planes_plan(const DeviceInfo* d, int64_t M, int64_t N, int64_t K, bool f16) {
   WpPlan best;
-  if (!w8a16_planes_for(M) || M < 1 || M > (f16 ? 64 : 128) || K % 16 != 0 || K > kWpMaxK ||
+  if (!w8a16_planes_for(M, K) || M < 1 || M > (f16 ? 64 : 128) || K % 16 != 0 || K > kWpMaxK ||
       N < 1 || N > (int64_t(1) << 24))
     return best;
   const int P = f16 ? 3 : 2;
@@ -568,9 +511,13 @@ WpPlan w8a16_planes_plan(const DeviceInfo* d, int64_t M, int64_t N, int64_t K, b
   const int nkb = static_cast<int>((K + kWpBK - 1) / kWpBK);
   const char* fs = getenv("B200Q_W8A16_PLANES_SPLITS");
   const int forced_s = fs ? atoi(fs) : 0;
+  const char* fc = getenv("B200Q_W8A16_PLANES_CTAS");  // CTAs per SM the ring is sized for
+  const int forced_c = fc ? atoi(fc) : 0;
+  const double kb_bytes = 128.0 * kWpBK;
+  const double t_hbm = double(tiles) * nkb * kb_bytes / 6.0e6;  // us
   double best_cost = 1e30;
   for (int c = 1; c <= 2; ++c) {
-    if (c * tmem > 512) continue;
+    if (c * tmem > 512 || (forced_c > 0 && c != forced_c)) continue;
     const int budget = (c == 1 ? 232448 : 233472 / c - 1024);  // per-CTA dynamic smem
     int stages = (budget - bar) / stage;
     if (stages > kWpMaxStages) stages = kWpMaxStages;
@@ -580,15 +527,13 @@ WpPlan w8a16_planes_plan(const DeviceInfo* d, int64_t M, int64_t N, int64_t K, b
     for (int S = 1; S <= 8 && S <= nkb; ++S) {
       if (forced_s > 0 && S != forced_s) continue;
       const int64_t ctas = tiles * S;
-      if (ctas > int64_t(c) * d->num_sms && forced_s == 0) continue;
-      const int64_t per_sm = (ctas + d->num_sms - 1) / d->num_sms;
-      const double cost = double(per_sm) / S;
+      const double slots = double(c) * d->num_sms * (S > 1 ? 0.9 : 1.0);
+      if (double(ctas) > slots && forced_s == 0) continue;
+      const double t_cta = double((nkb + S - 1) / S) * kb_bytes / 45.0e3;  // us
+      const double cost = (t_cta > t_hbm ? t_cta : t_hbm) + (S > 1 ? 0.3 : 0.0) + 0.1 * S;
       if (env_flag("B200Q_DEBUG_PLAN", false))
-        fprintf(stderr, "[b200q] planes plan M %lld N %lld K %lld: c %d S %d stages %d smem %d "
-                "clusters %d (need %lld) cost %.3f\n", (long long)M, (long long)N, (long long)K, c,
-                S, stages, smem, S > 1 ? wp_max_clusters(nt, S, smem) : -1, (long long)tiles, cost);
-      // A forced cluster size (measurements) skips the single-wave check.
-      if (S > 1 && forced_s == 0 && wp_max_clusters(nt, S, smem) < tiles) continue;
+        fprintf(stderr, "[b200q] planes plan M %lld N %lld K %lld: c %d S %d stages %d smem %d cost %.2f\n",
+                (long long)M, (long long)N, (long long)K, c, S, stages, smem, cost);
       if (cost < best_cost - 1e-9) {
         best_cost = cost;
         best.ok = true;

@@ -70,6 +70,8 @@ struct WpLayout {
   static constexpr int kStage = kWSlot + kXSlot;
   static constexpr int kDump = NT * 128 * 4;  // fp32 accumulators, [column][row]
   static constexpr uint32_t kTmemCols = NT <= 32 ? 32 : NT <= 64 ? 64 : NT <= 128 ? 128 : 256;
+  // bf16 tiles are 2 x {16,32,64,128} plane rows, fp16 tiles 3 x {16,32,64}.
+  static constexpr int kPlanes = NT % 3 == 0 ? 3 : 2;
   // full[8], empty[8], acc_full, tmem slot, abort flag
   static constexpr int kBarBytes = (2 * kWpMaxStages + 1) * 8 + 16;
   __host__ __device__ static constexpr int ring_bytes(int stages) {
@@ -157,6 +159,11 @@ template <typename XT, int P>
 __global__ void __launch_bounds__(kWpPlaneThreads)
     x_planes_kernel(const XT* __restrict__ x, int64_t ldx, int K, int bt,
                     uint8_t* __restrict__ planes, float* __restrict__ pscale) {
+  // Launched as a programmatic dependent of whatever ran before it: nothing of
+  // that work is touched before griddepcontrol.wait, and the GEMM is released
+  // only after it, so the GEMM's early weight loads never overtake a kernel
+  // that wrote the weight.
+  griddep_wait();
   griddep_launch_dependents();  // the GEMM may start streaming weights now
   __shared__ float red[kWpPlaneThreads / 32];
   extern __shared__ uint4 srow[];  // the row, K / 8 vectors
@@ -234,8 +241,82 @@ __global__ void __launch_bounds__(kWpPlaneThreads)
 }
 
 // ---------------------------------------------------------------------------
+// Rank 0's epilogue for one thread (weight row r of the tile): 16-token groups
+// t0 = 16 * (2i + half).  Each group loads its P accumulator column groups with
+// one TMEM wait, adds the peers' accumulators in rank order (distributed shared
+// memory), combines the planes with their scales, applies w_scale (xs), bias
+// and the activation (ACT fixed at compile time, so the 16 tokens are
+// independent straight-line code) and stores tokens < M.  An absent scale is
+// 1.0 and an absent bias -0.0: both exact, so no per-token branches remain.
+template <int NT, int ACT>
+__device__ __forceinline__ void wp_epilogue(const WpArgs& a, const EpiArgs& ep, int tile, int r,
+                                            uint32_t taddr, int half, const float* s_pscale,
+                                            uint32_t dump_base, float xs, float bias_v) {
+  constexpr int P = WpLayout<NT>::kPlanes;
+  constexpr int BT = NT / P;
+  const int n = tile * 128 + r;
+  const bool n_ok = n < a.N;
+  const int S = a.splits;
+#pragma unroll 1
+  for (int t0 = 16 * half; t0 < a.M; t0 += 32) {
+    float acc[P][16];
+    {
+      uint32_t v[P][16];
+#pragma unroll
+      for (int p = 0; p < P; ++p) tmem_ld_cols<16>(taddr + p * BT + t0, v[p]);
+      tmem_ld_wait();
+#pragma unroll
+      for (int p = 0; p < P; ++p)
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[p][j] = __uint_as_float(v[p][j]);
+    }
+    for (int s2 = 1; s2 < S; ++s2) {  // rank order: ((D_0 + D_1) + D_2) + ...
+      const uint32_t peer = mapa_shared(dump_base, static_cast<uint32_t>(s2));
+#pragma unroll
+      for (int p = 0; p < P; ++p)
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          acc[p][j] = __fadd_rn(acc[p][j], ld_dsmem_f32(peer + ((p * BT + t0 + j) * 128 + r) * 4));
+    }
+    // Tokens t0 .. t0+15 < bt always index valid (if unused) plane columns and
+    // scales; only the stores are limited to tokens < M.
+    float out_v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      float v = __fmul_rn(acc[0][j], s_pscale[t0 + j]);
+#pragma unroll
+      for (int p = 1; p < P; ++p) v = __fadd_rn(v, __fmul_rn(acc[p][j], s_pscale[p * BT + t0 + j]));
+      v = __fadd_rn(__fmul_rn(v, xs), bias_v);
+      out_v[j] = apply_act(v, ACT);
+    }
+    // Direct typed stores (32 lanes = 32 consecutive output features of one
+    // token row); measured 2x faster here than the generic per-element store.
+    if (n_ok) {
+      if (ep.out_dtype == kOutF32) {
+        float* o = static_cast<float*>(ep.out) + n;
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (t0 + j < a.M) o[static_cast<int64_t>(t0 + j) * ep.ldo] = out_v[j];
+      } else if (ep.out_dtype == kOutF16) {
+        __half* o = static_cast<__half*>(ep.out) + n;
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (t0 + j < a.M) o[static_cast<int64_t>(t0 + j) * ep.ldo] = __float2half_rn(out_v[j]);
+      } else {
+        __nv_bfloat16* o = static_cast<__nv_bfloat16*>(ep.out) + n;
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (t0 + j < a.M) o[static_cast<int64_t>(t0 + j) * ep.ldo] = __float2bfloat16_rn(out_v[j]);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 120 registers per thread: two 256-thread CTAs fit an SM's register file
+// (at 128 the occupancy calculator allowed only one).
 template <int NT>
-__global__ void __launch_bounds__(kWpThreads, 2)
+__global__ void __maxnreg__(120)
     w8a16_planes_kernel(const __grid_constant__ CUtensorMap tmW,
                         const __grid_constant__ CUtensorMap tmX, WpArgs a, EpiArgs ep) {
   using L = WpLayout<NT>;
@@ -282,6 +363,13 @@ __global__ void __launch_bounds__(kWpThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_d = *tmem_slot;
+  // Epilogue operands that do not depend on this grid's inputs (written before
+  // the planes pass ran): loaded now, consumed after the mainloop.
+  const int q = warp & 3;
+  const int r = q * 32 + lane;  // weight row in the tile = TMEM lane
+  const float xs = ep.extra_scale ? __ldg(ep.extra_scale) : 1.0f;
+  const float bias_v = (tile * 128 + r < a.N && ep.bias_dtype != kBiasNone)
+                           ? load_bias(ep.bias, ep.bias_dtype, tile * 128 + r) : -0.0f;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -335,79 +423,41 @@ __global__ void __launch_bounds__(kWpThreads, 2)
       if (ok) umma_commit(acc_full);
     }
     __syncwarp();
-  } else if (warp >= 4) {
-    // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;
-    const int r = q * 32 + lane;  // weight row in the tile = TMEM lane
-    const uint32_t taddr = tmem_d + (static_cast<uint32_t>(q * 32) << 16);
-    const bool valid = mbar_wait_warp(acc_full, 0u, abort_flag);
-    tc_fence_after();
-    if (split > 0) {
-      // Ranks 1..S-1: accumulators -> own shared memory, [column][row].
+  } else if (split == 0) {
+    // Warps 2..7 stage the plane scales while the mainloop runs.
+    griddep_wait();
+    for (int i = threadIdx.x - 64; i < L::kPlanes * (NT / L::kPlanes); i += kWpThreads - 64)
+      s_pscale[i] = a.pscale[i];
+  }
+
+  // ------------------------------------------------------------ epilogue
+  // All 8 warps, once the accumulator is final: warp w reads TMEM lane quarter
+  // w % 4 (its weight rows) and takes every other 16-column group (w / 4).
+  const int half = warp >> 2;
+  const uint32_t taddr = tmem_d + (static_cast<uint32_t>(q * 32) << 16);
+  const bool valid = mbar_wait_warp(acc_full, 0u, abort_flag);
+  tc_fence_after();
+  if (split > 0 && valid) {
+    // Ranks 1..S-1: accumulators -> own shared memory, [column][row].
 #pragma unroll 1
-      for (int c = 0; valid && c < NT; c += 16) {
-        uint32_t v[16];
-        tmem_ld_cols<16>(taddr + c, v);
-        tmem_ld_wait();
+    for (int c = 16 * half; c < NT; c += 32) {
+      uint32_t v[16];
+      tmem_ld_cols<16>(taddr + c, v);
+      tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) dump[(c + j) * 128 + r] = __uint_as_float(v[j]);
-      }
+      for (int j = 0; j < 16; ++j) dump[(c + j) * 128 + r] = __uint_as_float(v[j]);
     }
   }
 
   if (S > 1) cluster_sync();  // every rank's dump is written and visible
 
-  if (warp >= 4 && split == 0) {
-    griddep_wait();  // plane scales come from the planes pass
-    // Stage the P x bt plane scales in shared memory once: the per-token reads
-    // below are then broadcasts instead of a dependent global load per token.
-    for (int i = threadIdx.x - 128; i < a.planes * a.bt; i += 128) s_pscale[i] = a.pscale[i];
-    named_bar_sync(1, 128);
-    const int q = warp & 3;
-    const int r = q * 32 + lane;
-    const int n = tile * 128 + r;
-    const bool n_ok = n < a.N;
-    const uint32_t taddr = tmem_d + (static_cast<uint32_t>(q * 32) << 16);
-    const bool valid = *abort_flag == 0;
-    const float xs = ep.extra_scale ? __ldg(ep.extra_scale) : 1.0f;
-    const float bias_v = (n_ok && ep.bias_dtype != kBiasNone) ? load_bias(ep.bias, ep.bias_dtype, n) : 0.0f;
-    const int bt = a.bt;
-    const uint32_t dump_base = smem_u32(dump);
-#pragma unroll 1
-    for (int t0 = 0; valid && t0 < a.M; t0 += 16) {
-      float acc[3][16];
-#pragma unroll
-      for (int p = 0; p < 3; ++p) {
-        if (p >= a.planes) break;
-        uint32_t v[16];
-        tmem_ld_cols<16>(taddr + p * bt + t0, v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 16; ++j) acc[p][j] = __uint_as_float(v[j]);
-        for (int s2 = 1; s2 < S; ++s2) {  // rank order: ((D_0 + D_1) + D_2) + ...
-          const uint32_t peer = mapa_shared(dump_base, static_cast<uint32_t>(s2));
-#pragma unroll
-          for (int j = 0; j < 16; ++j)
-            acc[p][j] = __fadd_rn(acc[p][j], ld_dsmem_f32(peer + ((p * bt + t0 + j) * 128 + r) * 4));
-        }
-      }
-      // Tokens t0 .. t0+15 < bt always index valid (if unused) plane columns and
-      // scales; only the stores are limited to tokens < M.
-      float out_v[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        float v = __fmul_rn(acc[0][j], s_pscale[t0 + j]);
-        v = __fadd_rn(v, __fmul_rn(acc[1][j], s_pscale[bt + t0 + j]));
-        if (a.planes > 2) v = __fadd_rn(v, __fmul_rn(acc[2][j], s_pscale[2 * bt + t0 + j]));
-        if (ep.extra_scale) v = __fmul_rn(v, xs);
-        if (ep.bias_dtype != kBiasNone) v = __fadd_rn(v, bias_v);
-        out_v[j] = apply_act(v, ep.act);
-      }
-      if (n_ok) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          if (t0 + j < a.M) store_out(ep, t0 + j, n, out_v[j]);
-      }
+  __syncthreads();  // the staged plane scales are visible
+  if (split == 0 && valid && *abort_flag == 0) {
+    const uint32_t db = smem_u32(dump);
+    switch (ep.act) {
+      case kActGeluTanh: wp_epilogue<NT, kActGeluTanh>(a, ep, tile, r, taddr, half, s_pscale, db, xs, bias_v); break;
+      case kActGeluErf: wp_epilogue<NT, kActGeluErf>(a, ep, tile, r, taddr, half, s_pscale, db, xs, bias_v); break;
+      default: wp_epilogue<NT, kActNone>(a, ep, tile, r, taddr, half, s_pscale, db, xs, bias_v); break;
     }
   }
 
