@@ -540,9 +540,9 @@ def run_b200q(args):
                           "frac": round(achieved_gbs / peaks["hbm_gbs"], 4) if achieved_gbs else None,
                           "traffic": None, "traffic_source": None,
                           "algorithmic_bytes_per_launch": bytes_per_launch // len(spec["layers"]),
-                          "kernel": "x_planes_kernel + w8a16_planes_kernel (activation planes on "
-                                    "kind::f8f6f4, one call = both launches)" if M <= 128 else
-                                    "e4m3_rows_to16_kernel + gemm8 kind::f16",
+                          "kernel": ("w8a16_gemv_kernel" if M <= 16 and spec["layers"][0].K <= 4096 else
+                                     "x_planes_kernel + w8a16_planes_kernel (activation planes on "
+                                     "kind::f8f6f4, one call = both launches)"),
                           "peak_source": f"hbm_gbs of {peaks['source']} MEASURED_PEAKS.json",
                           "timing": ("16 calls back to back in one CUDA graph over 4 weight copies "
                                      "(151 MB > L2), events around the replay, median of 10; per call"

@@ -454,7 +454,7 @@ bool sync_ok(const unsigned int* sync, size_t sync_bytes, int64_t M) {
 // programmatic dependency on the planes pass.
 struct WpPlan {
   bool ok = false;
-  int bt = 0, P = 0, nt = 0, S = 1, stages = 0, smem = 0;
+  int bt = 0, P = 0, nt = 0, ntt = 1, S = 1, stages = 0, smem = 0;
 };
 
 bool env_flag(const char* name, bool dflt) {
@@ -472,36 +472,55 @@ bool w8a16_planes_for(int64_t M, int64_t K) {
   return M > 16 || K > 4096;
 }
 bool pdl_on() { return env_flag("B200Q_PDL", true); }
-int wp_bt(int64_t M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128; }
-size_t wp_plane_bytes(int P, int bt, int64_t K) {
-  return (size_t(P) * size_t(bt) * size_t(K) + 255) & ~size_t(255);
+// Tokens per plane tile: the smallest of 16/32/64/128 holding M (bf16) or
+// 16/32/64 (fp16, three planes: P x bt <= 192 plane rows per MMA); larger M is
+// split into ntt = ceil(M / bt) token tiles.
+constexpr int64_t kWpMaxM = 256;
+int wp_bt(int64_t M, int P) {
+  const int cap = P == 3 ? 64 : 128;
+  const int bt = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
+  return bt < cap ? bt : cap;
 }
-size_t wp_workspace_bytes(int P, int bt, int64_t K) {
-  return wp_plane_bytes(P, bt, K) + size_t(P) * size_t(bt) * sizeof(float);
+int wp_ntt(int64_t M, int bt) { return static_cast<int>((M + bt - 1) / bt); }
+size_t wp_plane_bytes(int P, int bt, int ntt, int64_t K) {
+  return (size_t(ntt) * size_t(P) * size_t(bt) * size_t(K) + 255) & ~size_t(255);
+}
+size_t wp_workspace_bytes(int P, int bt, int ntt, int64_t K) {
+  return wp_plane_bytes(P, bt, ntt, K) + size_t(ntt) * size_t(P) * size_t(bt) * sizeof(float);
 }
 // Workspace of the planes route for either activation type (the size query
 // does not know the type): 0 when M is out of its range.
 size_t wp_workspace_any(int64_t M, int64_t K) {
-  if (!w8a16_planes_for(M, K) || M < 1 || M > 128 || K % 16 != 0 || K > kWpMaxK) return 0;
-  const int bt = wp_bt(M);
-  return wp_workspace_bytes(M <= 64 ? 3 : 2, bt, K);
+  if (!w8a16_planes_for(M, K) || M < 1 || M > kWpMaxM || K % 16 != 0 || K > kWpMaxK) return 0;
+  size_t best = 0;
+  for (int P = 2; P <= 3; ++P) {
+    const int bt = wp_bt(M, P);
+    const size_t b = wp_workspace_bytes(P, bt, wp_ntt(M, bt), K);
+    if (b > best) best = b;
+  }
+  return best;
 }
 
-// Plan: the weight's 128-row tiles times S K-splits (one cluster of S CTAs per
-// tile), with the ring sized for 1 or 2 CTAs per SM.  Cost model, from B200
-// measurements of this kernel: a CTA streams its weight at ~45 GB/s with its
-// ring full, the GPU at ~6 TB/s; every split adds a reduction step.  Only
+// Plan: the weight's 128-row tiles times the token tiles times S K-splits (one
+// cluster of S CTAs per (weight tile, token tile)), with the ring sized for 1 or
+// 2 CTAs per SM.  Cost model, from B200 measurements of this kernel: a CTA
+// streams its weight at ~45 GB/s with its ring full, the GPU at ~6 TB/s (a
+// weight tile is read from HBM once; its other token tiles run next to it and
+// hit L2), the tensor cores at ~1.3e15 e4m3 MAC/s (twice the measured
+// sustained bf16 rate); every split adds a reduction
+// step.  Only
 // plans that are resident in one wave are taken; two CTAs per SM were measured
 // to co-reside (the occupancy calculator reports one), and with clusters of
 // S > 1 about 10% of the slots are lost to cluster placement (S = 3 at 2 per SM
 // did not fit 288 CTAs on 148 SMs).
 WpPlan w8a16_planes_plan(const DeviceInfo* d, int64_t M, int64_t N, int64_t K, bool f16) {
   WpPlan best;
-  if (!w8a16_planes_for(M, K) || M < 1 || M > (f16 ? 64 : 128) || K % 16 != 0 || K > kWpMaxK ||
+  if (!w8a16_planes_for(M, K) || M < 1 || M > kWpMaxM || K % 16 != 0 || K > kWpMaxK ||
       N < 1 || N > (int64_t(1) << 24))
     return best;
   const int P = f16 ? 3 : 2;
-  const int bt = wp_bt(M);
+  const int bt = wp_bt(M, P);
+  const int ntt = wp_ntt(M, bt);
   const int nt = P * bt;
   const int stage = 128 * kWpBK + nt * kWpBK;
   const int dump = nt * 128 * 4;
@@ -515,22 +534,26 @@ WpPlan w8a16_planes_plan(const DeviceInfo* d, int64_t M, int64_t N, int64_t K, b
   const int forced_c = fc ? atoi(fc) : 0;
   const double kb_bytes = 128.0 * kWpBK;
   const double t_hbm = double(tiles) * nkb * kb_bytes / 6.0e6;  // us
+  const double t_mma = double(tiles) * ntt * nkb * 128.0 * nt * kWpBK / 1.3e9;  // us
   double best_cost = 1e30;
   for (int c = 1; c <= 2; ++c) {
     if (c * tmem > 512 || (forced_c > 0 && c != forced_c)) continue;
     const int budget = (c == 1 ? 232448 : 233472 / c - 1024);  // per-CTA dynamic smem
     int stages = (budget - bar) / stage;
     if (stages > kWpMaxStages) stages = kWpMaxStages;
-    if (stages < 2 || dump + bar > budget) continue;
-    const int ring = stages * stage > dump ? stages * stage : dump;
-    const int smem = ring + bar;
+    if (stages < 2) continue;
     for (int S = 1; S <= 8 && S <= nkb; ++S) {
       if (forced_s > 0 && S != forced_s) continue;
-      const int64_t ctas = tiles * S;
+      if (S > 1 && dump + bar > budget) continue;  // split ranks park accumulators in the ring
+      const int ring = (S > 1 && dump > stages * stage) ? dump : stages * stage;
+      const int smem = ring + bar;
+      const int64_t ctas = tiles * ntt * S;
       const double slots = double(c) * d->num_sms * (S > 1 ? 0.9 : 1.0);
       if (double(ctas) > slots && forced_s == 0) continue;
       const double t_cta = double((nkb + S - 1) / S) * kb_bytes / 45.0e3;  // us
-      const double cost = (t_cta > t_hbm ? t_cta : t_hbm) + (S > 1 ? 0.3 : 0.0) + 0.1 * S;
+      double cost = t_cta > t_hbm ? t_cta : t_hbm;
+      if (t_mma > cost) cost = t_mma;
+      cost += (S > 1 ? 0.3 : 0.0) + 0.1 * S;
       if (env_flag("B200Q_DEBUG_PLAN", false))
         fprintf(stderr, "[b200q] planes plan M %lld N %lld K %lld: c %d S %d stages %d smem %d cost %.2f\n",
                 (long long)M, (long long)N, (long long)K, c, S, stages, smem, cost);
@@ -540,6 +563,7 @@ WpPlan w8a16_planes_plan(const DeviceInfo* d, int64_t M, int64_t N, int64_t K, b
         best.bt = bt;
         best.P = P;
         best.nt = nt;
+        best.ntt = ntt;
         best.S = S;
         best.stages = stages;
         best.smem = smem;
@@ -555,7 +579,7 @@ int launch_planes_gemm(const WpPlan& p, const CUtensorMap& tw, const CUtensorMap
   auto kern = w8a16_planes_kernel<NT>;
   if (!set_smem(kern, p.smem)) return B200Q_ERR_CUDA;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>((args.N + 127) / 128 * p.S));
+  cfg.gridDim = dim3(static_cast<unsigned>((args.N + 127) / 128 * p.ntt * p.S));
   cfg.blockDim = dim3(kWpThreads);
   cfg.dynamicSmemBytes = static_cast<size_t>(p.smem);
   cfg.stream = st;
@@ -583,31 +607,43 @@ int launch_w8a16_planes(const WpPlan& p, const void* x, int x_dtype, int64_t ldx
                         int64_t ldw, int64_t M, int64_t N, int64_t K, const EpiArgs& ep,
                         void* workspace, cudaStream_t st) {
   uint8_t* planes = static_cast<uint8_t*>(workspace);
-  float* pscale = reinterpret_cast<float*>(planes + wp_plane_bytes(p.P, p.bt, K));
-  const dim3 pgrid(static_cast<unsigned>(M));
+  float* pscale = reinterpret_cast<float*>(planes + wp_plane_bytes(p.P, p.bt, p.ntt, K));
   const int row_smem = static_cast<int>(K) * 2;
+  // The planes pass is a programmatic dependent of the previous kernel on the
+  // stream too: it waits for it (griddepcontrol.wait) before touching memory.
+  cudaLaunchConfig_t pcfg = {};
+  pcfg.gridDim = dim3(static_cast<unsigned>(M));
+  pcfg.blockDim = dim3(kWpPlaneThreads);
+  pcfg.dynamicSmemBytes = static_cast<size_t>(row_smem);
+  pcfg.stream = st;
+  cudaLaunchAttribute pat[1];
+  pat[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  pat[0].val.programmaticStreamSerializationAllowed = 1;
+  pcfg.attrs = pat;
+  pcfg.numAttrs = pdl_on() ? 1 : 0;
   if (x_dtype == B200Q_F16) {
     if (!set_smem(x_planes_kernel<__half, 3>, row_smem)) return B200Q_ERR_CUDA;
-    x_planes_kernel<__half, 3><<<pgrid, kWpPlaneThreads, row_smem, st>>>(
-        static_cast<const __half*>(x), ldx, int(K), p.bt, planes, pscale);
+    cudaLaunchKernelEx(&pcfg, x_planes_kernel<__half, 3>, static_cast<const __half*>(x), ldx,
+                       int(K), p.bt, planes, pscale);
   } else {
     if (!set_smem(x_planes_kernel<__nv_bfloat16, 2>, row_smem)) return B200Q_ERR_CUDA;
-    x_planes_kernel<__nv_bfloat16, 2><<<pgrid, kWpPlaneThreads, row_smem, st>>>(
-        static_cast<const __nv_bfloat16*>(x), ldx, int(K), p.bt, planes, pscale);
+    cudaLaunchKernelEx(&pcfg, x_planes_kernel<__nv_bfloat16, 2>,
+                       static_cast<const __nv_bfloat16*>(x), ldx, int(K), p.bt, planes, pscale);
   }
   int s = finish_launch();
   if (s != B200Q_OK) return s;
   CUtensorMap tw, tx;
   if (!make_tmap(&tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldw, kWpBK, 128,
                  CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_tmap(&tx, planes, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, uint64_t(p.P) * p.bt, K, kWpBK,
-                 p.nt, CU_TENSOR_MAP_SWIZZLE_128B))
+      !make_tmap(&tx, planes, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, uint64_t(p.ntt) * p.P * p.bt, K,
+                 kWpBK, p.nt, CU_TENSOR_MAP_SWIZZLE_128B))
     return B200Q_ERR_CUDA;
   WpArgs args{};
   args.M = int(M);
   args.N = int(N);
   args.K = int(K);
   args.bt = p.bt;
+  args.ntt = p.ntt;
   args.planes = p.P;
   args.splits = p.S;
   args.stages = p.stages;
@@ -1143,7 +1179,7 @@ int w8a16_linear_impl(const void* x, int x_dtype, int64_t ldx, const uint8_t* w,
   }
   if (workspace && aligned16(workspace)) {
     const WpPlan wp = w8a16_planes_plan(d, M, N, K, x_dtype == B200Q_F16);
-    if (wp.ok && workspace_bytes >= wp_workspace_bytes(wp.P, wp.bt, K))
+    if (wp.ok && workspace_bytes >= wp_workspace_bytes(wp.P, wp.bt, wp.ntt, K))
       return launch_w8a16_planes(wp, x, x_dtype, ldx, w, ldw, M, N, K, ep, workspace, st);
   }
   if (w8a16_gemv_selected(M)) {

@@ -84,7 +84,8 @@ struct WpLayout {
 
 struct WpArgs {
   int M, N, K;
-  int bt;                 // tokens per plane (16, 32, 64 or 128)
+  int bt;                 // tokens per plane and token tile (16, 32, 64 or 128)
+  int ntt;                // token tiles: ceil(M / bt)
   int planes;             // P = 2 (bf16 activations) or 3 (fp16)
   int splits;             // cluster size S
   int stages;             // ring depth (<= kWpMaxStages)
@@ -154,7 +155,9 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return m;
 }
 
-// Grid: one CTA per token row t < M.  planes: [P][bt][K] bytes; pscale [P][bt].
+// Grid: one CTA per token row t < M.  planes: [ntt][P][bt][K] bytes (token tile
+// tt = t / bt holds its P planes' rows contiguously, one TMA box); pscale
+// [ntt][P][bt].
 template <typename XT, int P>
 __global__ void __launch_bounds__(kWpPlaneThreads)
     x_planes_kernel(const XT* __restrict__ x, int64_t ldx, int K, int bt,
@@ -168,9 +171,10 @@ __global__ void __launch_bounds__(kWpPlaneThreads)
   __shared__ float red[kWpPlaneThreads / 32];
   extern __shared__ uint4 srow[];  // the row, K / 8 vectors
   const int t = blockIdx.x;
+  const int tt = t / bt, tl = t - tt * bt;  // token tile, row inside it
   const uint4* row = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(t) * ldx);
   const int64_t plane_stride = static_cast<int64_t>(bt) * K;
-  uint8_t* out0 = planes + static_cast<int64_t>(t) * K;
+  uint8_t* out0 = planes + (static_cast<int64_t>(tt) * P * bt + tl) * K;
   const int nv = K / 8;
 
   // max |x|, and whether the row is finite; the row is kept in shared memory
@@ -236,29 +240,31 @@ __global__ void __launch_bounds__(kWpPlaneThreads)
   if (threadIdx.x == 0) {
     const float nan = __uint_as_float(0x7FC00000u);
 #pragma unroll
-    for (int p = 0; p < P; ++p) pscale[p * bt + t] = all_finite ? exp2i(-e_tot[p]) : nan;
+    for (int p = 0; p < P; ++p) pscale[(tt * P + p) * bt + tl] = all_finite ? exp2i(-e_tot[p]) : nan;
   }
 }
 
 // ---------------------------------------------------------------------------
-// Rank 0's epilogue for one thread (weight row r of the tile): 16-token groups
-// t0 = 16 * (2i + half).  Each group loads its P accumulator column groups with
+// Rank 0's epilogue for one thread (weight row r of the tile, token tile tt):
+// 16-token groups t0 = 16 * (2i + half).  Each group loads its P accumulator column groups with
 // one TMEM wait, adds the peers' accumulators in rank order (distributed shared
 // memory), combines the planes with their scales, applies w_scale (xs), bias
 // and the activation (ACT fixed at compile time, so the 16 tokens are
 // independent straight-line code) and stores tokens < M.  An absent scale is
 // 1.0 and an absent bias -0.0: both exact, so no per-token branches remain.
 template <int NT, int ACT>
-__device__ __forceinline__ void wp_epilogue(const WpArgs& a, const EpiArgs& ep, int tile, int r,
-                                            uint32_t taddr, int half, const float* s_pscale,
+__device__ __forceinline__ void wp_epilogue(const WpArgs& a, const EpiArgs& ep, int tile, int tt,
+                                            int r, uint32_t taddr, int half, const float* s_pscale,
                                             uint32_t dump_base, float xs, float bias_v) {
   constexpr int P = WpLayout<NT>::kPlanes;
   constexpr int BT = NT / P;
   const int n = tile * 128 + r;
   const bool n_ok = n < a.N;
   const int S = a.splits;
+  const int mt = a.M - tt * BT < BT ? a.M - tt * BT : BT;  // tokens of this tile
+  const int64_t row0 = static_cast<int64_t>(tt) * BT;
 #pragma unroll 1
-  for (int t0 = 16 * half; t0 < a.M; t0 += 32) {
+  for (int t0 = 16 * half; t0 < mt; t0 += 32) {
     float acc[P][16];
     {
       uint32_t v[P][16];
@@ -296,17 +302,17 @@ __device__ __forceinline__ void wp_epilogue(const WpArgs& a, const EpiArgs& ep, 
         float* o = static_cast<float*>(ep.out) + n;
 #pragma unroll
         for (int j = 0; j < 16; ++j)
-          if (t0 + j < a.M) o[static_cast<int64_t>(t0 + j) * ep.ldo] = out_v[j];
+          if (t0 + j < mt) o[(row0 + t0 + j) * ep.ldo] = out_v[j];
       } else if (ep.out_dtype == kOutF16) {
         __half* o = static_cast<__half*>(ep.out) + n;
 #pragma unroll
         for (int j = 0; j < 16; ++j)
-          if (t0 + j < a.M) o[static_cast<int64_t>(t0 + j) * ep.ldo] = __float2half_rn(out_v[j]);
+          if (t0 + j < mt) o[(row0 + t0 + j) * ep.ldo] = __float2half_rn(out_v[j]);
       } else {
         __nv_bfloat16* o = static_cast<__nv_bfloat16*>(ep.out) + n;
 #pragma unroll
         for (int j = 0; j < 16; ++j)
-          if (t0 + j < a.M) o[static_cast<int64_t>(t0 + j) * ep.ldo] = __float2bfloat16_rn(out_v[j]);
+          if (t0 + j < mt) o[(row0 + t0 + j) * ep.ldo] = __float2bfloat16_rn(out_v[j]);
       }
     }
   }
@@ -324,7 +330,9 @@ __global__ void __maxnreg__(120)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int stages = a.stages;
-  const int ring = L::ring_bytes(stages);
+  // Ring size exactly as the host sized the allocation: split ranks park their
+  // accumulators in the ring afterwards, so with S > 1 it covers the dump too.
+  const int ring = a.splits > 1 ? L::ring_bytes(stages) : stages * L::kStage;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + ring);
   uint64_t* empty = full + kWpMaxStages;
   uint64_t* acc_full = empty + kWpMaxStages;
@@ -337,7 +345,9 @@ __global__ void __maxnreg__(120)
   const int lane = threadIdx.x & 31;
   const int S = a.splits;
   const int split = S > 1 ? static_cast<int>(cluster_ctarank()) : 0;
-  const int tile = blockIdx.x / S;
+  const int unit = blockIdx.x / S;  // (weight tile, token tile); the cluster's K-splits share it
+  const int tile = unit / a.ntt;
+  const int tt = unit - tile * a.ntt;
   const int nkb = (a.K + kWpBK - 1) / kWpBK;
   const int kb0 = split * nkb / S, kb1 = (split + 1) * nkb / S;
   const int nst = kb1 - kb0;
@@ -383,7 +393,7 @@ __global__ void __maxnreg__(120)
       }
       griddep_wait();
       for (int i = 0; i < pre; ++i)
-        tma_load_2d(&tmX, &full[i], smem + i * L::kStage + L::kWSlot, (kb0 + i) * kWpBK, 0);
+        tma_load_2d(&tmX, &full[i], smem + i * L::kStage + L::kWSlot, (kb0 + i) * kWpBK, tt * NT);
       int issued = pre;
       bool ok = true;
       for (int i = pre; i < nst; ++i) {
@@ -393,7 +403,7 @@ __global__ void __maxnreg__(120)
         mbar_arrive_expect_tx(&full[s], L::kStage);
         uint8_t* dst = smem + s * L::kStage;
         tma_load_2d(&tmW, &full[s], dst, (kb0 + i) * kWpBK, tile * 128);
-        tma_load_2d(&tmX, &full[s], dst + L::kWSlot, (kb0 + i) * kWpBK, 0);
+        tma_load_2d(&tmX, &full[s], dst + L::kWSlot, (kb0 + i) * kWpBK, tt * NT);
         issued = i + 1;
       }
       if (!ok) {
@@ -427,7 +437,7 @@ __global__ void __maxnreg__(120)
     // Warps 2..7 stage the plane scales while the mainloop runs.
     griddep_wait();
     for (int i = threadIdx.x - 64; i < L::kPlanes * (NT / L::kPlanes); i += kWpThreads - 64)
-      s_pscale[i] = a.pscale[i];
+      s_pscale[i] = a.pscale[tt * NT + i];
   }
 
   // ------------------------------------------------------------ epilogue
@@ -455,9 +465,9 @@ __global__ void __maxnreg__(120)
   if (split == 0 && valid && *abort_flag == 0) {
     const uint32_t db = smem_u32(dump);
     switch (ep.act) {
-      case kActGeluTanh: wp_epilogue<NT, kActGeluTanh>(a, ep, tile, r, taddr, half, s_pscale, db, xs, bias_v); break;
-      case kActGeluErf: wp_epilogue<NT, kActGeluErf>(a, ep, tile, r, taddr, half, s_pscale, db, xs, bias_v); break;
-      default: wp_epilogue<NT, kActNone>(a, ep, tile, r, taddr, half, s_pscale, db, xs, bias_v); break;
+      case kActGeluTanh: wp_epilogue<NT, kActGeluTanh>(a, ep, tile, tt, r, taddr, half, s_pscale, db, xs, bias_v); break;
+      case kActGeluErf: wp_epilogue<NT, kActGeluErf>(a, ep, tile, tt, r, taddr, half, s_pscale, db, xs, bias_v); break;
+      default: wp_epilogue<NT, kActNone>(a, ep, tile, tt, r, taddr, half, s_pscale, db, xs, bias_v); break;
     }
   }
 

@@ -7,7 +7,7 @@ Against the oracle's decode-the-weight linear (linear_fp8_w8a16.py:151-196 with
 the per-tensor scale and tanh-GELU): bf16/fp16 outputs within 1 ULP of the fp32
 result, fp32 outputs within the FP8 RMS bound, bit-reproducible across calls
 and across cluster sizes' own reruns.  Shapes cover every plane-tile width
-(bt = 16/32/64/128 tokens), K tails (K % 128 != 0), N tails (N % 128 != 0),
+(bt = 16/32/64/128 tokens), several token tiles (M up to 256), K tails (K % 128 != 0), N tails (N % 128 != 0),
 Wan/Flux projection shapes and strided activations.
 """
 import os
@@ -50,7 +50,7 @@ def _launches(native, fn):
     return out, native.launch_count() - c0
 
 
-@pytest.mark.parametrize("M", [1, 2, 15, 16, 17, 31, 32, 33, 63, 64, 65, 100, 128])
+@pytest.mark.parametrize("M", [1, 2, 15, 16, 17, 31, 32, 33, 63, 64, 65, 100, 128, 129, 200, 256])
 @pytest.mark.parametrize("K,N", [(3072, 12288), (1040, 1000), (5120, 5120)])
 def test_planes_bf16(native, M, K, N):
     x, w, ws, b = _case(M, K, N, torch.bfloat16, M * 31 + K)
@@ -66,7 +66,7 @@ def test_planes_bf16(native, M, K, N):
     assert native.device_status() == 0
 
 
-@pytest.mark.parametrize("M", [1, 16, 17, 33, 64])
+@pytest.mark.parametrize("M", [1, 16, 17, 33, 64, 65, 130, 256])
 @pytest.mark.parametrize("K,N", [(3072, 4096), (1040, 1000)])
 def test_planes_fp16(native, M, K, N):
     x, w, ws, b = _case(M, K, N, torch.float16, M * 17 + K)
