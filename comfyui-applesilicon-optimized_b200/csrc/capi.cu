@@ -464,12 +464,15 @@ bool env_flag(const char* name, bool dflt) {
 // Read per call (a getenv), so tests can switch routes inside one process.
 // B200Q_W8A16_PLANES: unset = where the planes route measured at least level
 // with the decode-in-kernel kernels on B200 (back-to-back calls, weights larger
-// than L2): every M > 16, and M <= 16 when K > 4096 (at K = 3072 the GEMV is
-// ~8% ahead for M <= 16); "1" = every eligible call, "0" = never.
-bool w8a16_planes_for(int64_t M, int64_t K) {
+// than L2): every M > 16; for bf16 activations also M <= 16 when K > 4096 (at
+// K = 3072 the GEMV is ~8% ahead there); fp16 activations keep the GEMV for
+// M <= 16 at every K (its e4m3 -> fp16 decode is one instruction per pair: 10.6
+// vs 13.6 us at 3072 x 12288, 15.1 vs 18.9 us at 5120 x 13824); "1" = every
+// eligible call, "0" = never.
+bool w8a16_planes_for(int64_t M, int64_t K, bool f16) {
   const char* e = getenv("B200Q_W8A16_PLANES");
   if (e) return e[0] != '0';
-  return M > 16 || K > 4096;
+  return M > 16 || (!f16 && K > 4096);
 }
 bool pdl_on() { return env_flag("B200Q_PDL", true); }
 // Tokens per plane tile: the smallest of 16/32/64/128 holding M (bf16) or
@@ -491,9 +494,10 @@ size_t wp_workspace_bytes(int P, int bt, int ntt, int64_t K) {
 // Workspace of the planes route for either activation type (the size query
 // does not know the type): 0 when M is out of its range.
 size_t wp_workspace_any(int64_t M, int64_t K) {
-  if (!w8a16_planes_for(M, K) || M < 1 || M > kWpMaxM || K % 16 != 0 || K > kWpMaxK) return 0;
+  if (M < 1 || M > kWpMaxM || K % 16 != 0 || K > kWpMaxK) return 0;
   size_t best = 0;
   for (int P = 2; P <= 3; ++P) {
+    if (!w8a16_planes_for(M, K, P == 3)) continue;
     const int bt = wp_bt(M, P);
     const size_t b = wp_workspace_bytes(P, bt, wp_ntt(M, bt), K);
     if (b > best) best = b;
@@ -515,7 +519,7 @@ size_t wp_workspace_any(int64_t M, int64_t K) {
 // did not fit 288 CTAs on 148 SMs).
 WpPlan w8a16_planes_plan(const DeviceInfo* d, int64_t M, int64_t N, int64_t K, bool f16) {
   WpPlan best;
-  if (!w8a16_planes_for(M, K) || M < 1 || M > kWpMaxM || K % 16 != 0 || K > kWpMaxK ||
+  if (!w8a16_planes_for(M, K, f16) || M < 1 || M > kWpMaxM || K % 16 != 0 || K > kWpMaxK ||
       N < 1 || N > (int64_t(1) << 24))
     return best;
   const int P = f16 ? 3 : 2;
