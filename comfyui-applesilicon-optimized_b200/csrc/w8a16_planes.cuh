@@ -1,7 +1,7 @@
 // FP8 weight-only W8A16 for small token counts without decoding the weight.
 //
-// At M <= 128 the W8A16 linear is bound by the e4m3 weight stream from HBM (one
-// byte per weight).  Decoding each weight to bf16 on the SMs costs ~4 ALU
+// At small M the W8A16 linear is bound by the e4m3 weight stream from HBM (one
+// byte per weight; at M = 256 the tensor-core side takes over).  Decoding each weight to bf16 on the SMs costs ~4 ALU
 // instructions per pair of weights, which at HBM rate takes about half of every
 // SM's issue slots; instead, the activations (few rows) are split exactly into
 // e4m3 "planes" and the tensor cores multiply the raw weight tile with them
@@ -25,13 +25,17 @@
 //   x_planes_kernel   one CTA per token row: |x| max, planes, plane scales.
 //   w8a16_planes_kernel<NT>
 //     weight-stationary tile: MMA M = 128 weight rows, N = NT = P x BT plane rows
-//     (BT tokens padded to 16/32/64/128), D^T[n, p*BT + t] in TMEM (fp32).
+//     (BT tokens padded to 16/32/64/128; more tokens are split into token tiles,
+//     one CTA per (weight tile, token tile)), D^T[n, p*BT + t] in TMEM (fp32).
 //     warp 0   TMA producer: 128 x 128 B weight tile + NT x 128 B plane tile per
 //              stage, 128-byte swizzle; the weight loads of the first stages are
 //              issued before griddepcontrol.wait, the plane loads after it.
 //     warp 1   MMA issuer: 4 x kind::f8f6f4 (K = 32) per stage.
-//     warp 2   TMEM allocator.
-//     warps 4..7  epilogue, one thread per weight row (TMEM lane).
+//     warp 2   TMEM allocator; warps 2..7 stage the plane scales during the
+//              mainloop.
+//     all 8 warps  epilogue once the accumulator is final: one thread per weight
+//              row (TMEM lane), the two warp halves taking alternate 16-token
+//              groups.  120 registers per thread let two CTAs share an SM.
 //   Split-K for occupancy: a cluster of S CTAs shares a weight tile, CTA rank s
 //   taking K blocks [s*nkb/S, (s+1)*nkb/S).  Ranks 1..S-1 dump their fp32
 //   accumulators into their own (drained) ring memory; rank 0 adds them in rank
@@ -89,7 +93,7 @@ struct WpArgs {
   int planes;             // P = 2 (bf16 activations) or 3 (fp16)
   int splits;             // cluster size S
   int stages;             // ring depth (<= kWpMaxStages)
-  const float* pscale;    // [P][bt]: 2^-e_p[t]
+  const float* pscale;    // [ntt][P][bt]: 2^-e_p[t]
 };
 
 // ---------------------------------------------------------------------------
