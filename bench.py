@@ -103,7 +103,7 @@ def _base_spec(name):
             Layer("up", 3072, 12288, "gelu_tanh"), Layer("down", 12288, 3072)],
             inputs=["x", "attn", "x"], desc="Flux double-stream block INT8 W8A8 (BASELINE config 4)")
     if name == "c1":
-        return dict(route="int8", M=4096, seed=0, hidden=3072, outliers=8,
+        return dict(route="int8", M=4096, seed=0, hidden=3072, outliers=8, recipe="cpu",
                     layers=[Layer("linear", 3072, 3072)],
                     inputs=["x"], desc="INT8 W8A8 single linear (BASELINE config 1)")
     if name == "c3":
@@ -130,15 +130,30 @@ def _flops(spec, M):
 
 
 class B200Block:
-    """Device-resident weights + the step, through the public torch.ops.b200q API."""
+    """Device-resident weights + the step, through the public torch.ops.b200q API.
 
-    def __init__(self, spec, M, dev, rank, fused=False):
+    Inputs follow BASELINE.json.  Config 1 uses its recipe draw for draw on one
+    CPU generator seeded 0: X bf16 [4096, 3072] ~ N(0,1), 8 outlier channels
+    torch.randperm(3072)[:8] scaled x20, W = bf16(N(0, 0.02)) quantized per
+    output channel (s_w = absmax/127, round-half-even), bias bf16 ~ N(0, 0.01);
+    a rank takes its rows [start, start + M) of that X.  The other configs draw
+    on a device generator seeded with the config's seed (their sizes make CPU
+    generation slow): weights N(0, 0.02) (per-channel int8 or per-tensor e4m3),
+    biases N(0, 0.01), activations N(0, 1) per rank shard, 1% outlier channels
+    x20 for the INT8 configs."""
+
+    def __init__(self, spec, M, dev, rank, fused=False, start=0):
         self.spec, self.M, self.dev = spec, M, dev
         self.fused = fused  # activation quant inside the GEMM launch (8-bit routes)
+        self.weights = []
+        self.inputs = {}
+        self.gemm_events = []
+        if spec.get("recipe") == "cpu":
+            self._init_cpu_recipe(spec, M, dev, start)
+            return
         ops = torch.ops.b200q
         g = torch.Generator(device=dev)
         g.manual_seed(spec["seed"])
-        self.weights = []
         for l in spec["layers"]:
             w = torch.randn((l.N, l.K), generator=g, device=dev, dtype=torch.float32) * 0.02
             b = (torch.randn((l.N,), generator=g, device=dev) * 0.01).to(torch.bfloat16)
@@ -153,7 +168,6 @@ class B200Block:
         # Activations: N(0,1) bf16 per rank shard; 1% outlier channels x20 for INT8 configs.
         gx = torch.Generator(device=dev)
         gx.manual_seed(spec["seed"] * 1000 + 17 + rank)
-        self.inputs = {}
         for key in sorted(set(spec["inputs"])):
             K0 = spec["layers"][0].K
             x = torch.randn((M, K0), generator=gx, device=dev, dtype=torch.bfloat16)
@@ -162,7 +176,20 @@ class B200Block:
                 idx = torch.randperm(K0, generator=gx, device=dev)[:n_out]
                 x[:, idx] *= 20
             self.inputs[key] = x
-        self.gemm_events = []
+
+    def _init_cpu_recipe(self, spec, M, dev, start):
+        (l,) = spec["layers"]
+        g = torch.Generator().manual_seed(spec["seed"])
+        x = torch.randn(spec["M"], l.K, generator=g).to(torch.bfloat16)
+        idx = torch.randperm(l.K, generator=g)[: spec["outliers"]]
+        x[:, idx] *= 20
+        w = (torch.randn(l.N, l.K, generator=g) * 0.02).to(torch.bfloat16).float()
+        b = (torch.randn(l.N, generator=g) * 0.01).to(torch.bfloat16)
+        s = (w.abs().amax(dim=1) / 127.0).clamp_min(1e-30)
+        q = torch.clamp(torch.round(w / s[:, None]), -128, 127).to(torch.int8)
+        self.weights.append((q.to(dev), s.float().to(dev), b.to(dev)))
+        self.inputs["x"] = x[start:start + M].contiguous().to(dev)
+        self.outlier_channels = idx
 
     def step(self, inputs, record=False):
         """Runs the block; returns its outputs.  With record=True, CUDA events
@@ -331,6 +358,68 @@ def w8a16_back_to_back_ms(blk, reps=16, copies=4, iters=10):
     return statistics.median(ts)
 
 
+# ----------------------------------------------------------------------------- vendor
+def vendor_baseline(blk, flush, reps=5):
+    """Stock torch on the same device, shapes and operand types, with no b200q
+    code involved: torch._scaled_mm (cuBLASLt FP8, per-tensor scales, bf16 bias,
+    bf16 out) for the FP8 routes, torch._int_mm (cuBLASLt IMMA, int32 out) for
+    the INT8 routes, and for W8A16 the stock route of an e4m3 weight (decode to
+    bf16, then F.linear on cuBLAS).  Epilogue activations are not fused there and
+    are left out.  Each layer: median of `reps` launches, L2 flushed before each,
+    CUDA events on the current stream.  Returns the aggregate and per-layer rates."""
+    spec, M, dev = blk.spec, blk.M, blk.dev
+    route = spec["route"]
+    if route == "mlp":
+        return None
+    per, tot_flops, tot_ms = [], 0.0, 0.0
+    g = torch.Generator(device=dev)
+    g.manual_seed(99)
+    for l, (w, s, b) in zip(spec["layers"], blk.weights):
+        x = torch.randn((M, l.K), generator=g, device=dev, dtype=torch.bfloat16)
+        try:
+            if route == "fp8":
+                sa = (x.abs().amax().float() / 448.0).reshape(())
+                a = (x.float() / sa).clamp(-448, 448).to(torch.float8_e4m3fn)
+                sb = s.reshape(()).float()
+                fn = lambda a=a, w=w, sa=sa, sb=sb, b=b: torch._scaled_mm(
+                    a, w.t(), scale_a=sa, scale_b=sb, bias=b, out_dtype=torch.bfloat16)
+                what = "torch._scaled_mm (cuBLASLt FP8)"
+            elif route == "int8":
+                a = torch.randint(-127, 128, (M, l.K), generator=g, device=dev, dtype=torch.int8)
+                fn = lambda a=a, w=w: torch._int_mm(a, w.t())
+                what = "torch._int_mm (cuBLASLt int8, int32 out, no dequant)"
+            else:
+                fn = lambda x=x, w=w, b=b: torch.nn.functional.linear(x, w.to(torch.bfloat16), b)
+                what = "e4m3 -> bf16 weight decode + F.linear (cuBLAS), per call"
+            fn()
+            torch.cuda.synchronize()
+            ts = []
+            for _ in range(reps):
+                flush.zero_()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record()
+                fn()
+                e1.record()
+                torch.cuda.synchronize()
+                ts.append(e0.elapsed_time(e1))
+            ms = statistics.median(ts)
+        except Exception as e:  # a stock kernel missing for this shape/type
+            per.append({"layer": l.name, "error": repr(e)[:200]})
+            continue
+        fl = 2.0 * M * l.K * l.N
+        tot_flops += fl
+        tot_ms += ms
+        per.append({"layer": l.name, "ms": round(ms, 4), "tflops": round(fl / ms / 1e9, 1)})
+        del x
+    torch.cuda.synchronize()
+    if not tot_ms:
+        return {"per_layer": per}
+    return {"value": round(tot_flops / tot_ms / 1e9, 1), "unit": _unit(spec), "what": what,
+            "timing": f"per layer: median of {reps} launches, L2 flushed before each, CUDA events",
+            "per_layer": per}
+
+
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -398,7 +487,7 @@ def run_b200q(args):
 
     spec = _workload_spec(args.workload, args.m)
     start, M = _split_rows(spec["M"], world, rank)
-    blk = B200Block(spec, M, dev, rank, fused=args.prologue == "fused")
+    blk = B200Block(spec, M, dev, rank, fused=args.prologue == "fused", start=start)
     flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
 
     def barrier():
@@ -459,6 +548,8 @@ def run_b200q(args):
                   and graphs is not None else None)
     t_dev = sum(a.elapsed_time(b) for a, b in step_ms)
     gemm_ms = sum(a.elapsed_time(b) for a, b, _ in blk.gemm_events)
+    # stock torch on the same shapes (outside every timed region above)
+    vendor = vendor_baseline(blk, flush) if args.vendor and world == 1 else None
     gemm_flops = sum(f for _, _, f in blk.gemm_events)
     n_gemm = len(blk.gemm_events)
 
@@ -494,7 +585,10 @@ def run_b200q(args):
     e2e = total_flops * e2e_steps / (t_e2e / 1e3) / 1e12
     peaks = _peaks()
     eight_bit = spec["route"] in ("fp8", "int8", "mlp")
-    peak = (2.0 if eight_bit else 1.0) * peaks["bf16_sustained"]
+    # Each GEMM is timed as its own launch (a few ms), so the burst rate is the
+    # denominator; the sustained one is reported beside it.
+    peak = (2.0 if eight_bit else 1.0) * peaks["bf16"]
+    peak_sus = (2.0 if eight_bit else 1.0) * peaks["bf16_sustained"]
     achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None
     # W8A16 with <= 256 tokens is bound by the FP8 weight stream (an HBM
     # roofline), so its roofline is bytes moved per launch / launch time.
@@ -554,15 +648,11 @@ def run_b200q(args):
                          {"bound": "tensor", "achieved": round(achieved, 1) if achieved else None,
                          "peak": round(peak, 1), "unit": "TFLOP/s",
                          "frac": round(achieved / peak, 4) if achieved else None,
+                         "frac_vs_sustained": round(achieved / peak_sus, 4) if achieved else None,
                          "traffic": traffic, "traffic_source": traffic_src,
                          "algorithmic_flops_per_launch": (round(gemm_flops / n_gemm) if n_gemm else None),
-                         "kernel": ("gemm8_tc2_kernel (FC1: SwiGLU epilogue; FC2: channelwise dequant)"
-                                    if spec["route"] == "mlp" else
-                                    "gemm8_tc_kernel" if eight_bit else
-                                    "e4m3_rows_to16_kernel + gemm8_tc2_kernel<BF16> (weight decoded "
-                                    "once per call, kind::f16 GEMM; both inside the timed launch)"
-                                    if M >= 128 else "w8a16_tc_kernel"),
-                         "peak_source": (f"{'2 x ' if eight_bit else ''}bf16_tflops_sustained of "
+                         "kernel": _gemm_kernel_label(spec, M),
+                         "peak_source": (f"{'2 x ' if eight_bit else ''}bf16_tflops (burst) of "
                                          f"{peaks['source']} MEASURED_PEAKS.json"
                                          + (" (dense FP8/INT8 rate = 2 x BF16 on B200)" if eight_bit else "")),
                          "gemm_launches_timed": n_gemm}),
@@ -572,12 +662,35 @@ def run_b200q(args):
             "gpu_launches": int(launches_max),
             "clocks": clocks,
         }
+        if vendor is not None:
+            line["vendor_baseline"] = vendor
         if args.cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(spec, args)
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
+
+
+def _gemm_kernel_label(spec, M):
+    """Name of the tile kernel the workload's GEMM launches run (the dispatch of
+    csrc/capi.cu gemm8/gemm16: CTA pair for M >= 256 and N > 128)."""
+    names = set()
+    for l in spec["layers"]:
+        if spec["route"] == "w8a16" and M < 128:
+            names.add("w8a16_tc_kernel")
+            continue
+        k = "gemm8_tc2_kernel" if (l.N > 128 and M >= 256) else "gemm8_tc_kernel"
+        names.add(k)
+    label = " + ".join(sorted(names))
+    if spec["route"] == "w8a16":
+        label = "e4m3_rows_to16_kernel + " + label + "<kind::f16> (weight decoded once per call)"
+    elif spec["route"] == "mlp":
+        label += " (FC1: SwiGLU epilogue; FC2: channelwise dequant)"
+    elif "gemm8_tc2_kernel" in names:
+        label += (" (CTA pair, tcgen05.mma.cta_group::2, kind::f8f6f4)" if spec["route"] == "fp8"
+                  else " (CTA pair, tcgen05.mma.cta_group::2, kind::i8)")
+    return label
 
 
 def _committed_traffic(workload):
@@ -592,101 +705,150 @@ def _committed_traffic(workload):
 
 
 # ----------------------------------------------------------------------------- CPU arm
-def cpu_baseline(spec, args, rows=None):
-    """The oracle port of the reference's CPU path on a bounded row sample."""
-    from oracle import oracle
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    rows = rows or args.cpu_rows
+_CPU_CACHE = {}
+
+
+def _cpu_layers(spec):
+    """CPU weights of every layer (made once per process, untimed): int8 codes +
+    per-channel scales for the INT8 routes, e4m3 codes + a per-tensor scale for
+    the FP8 routes, bf16 bias; same distributions as the GPU arm."""
+    key = spec["desc"]
+    if key in _CPU_CACHE:
+        return _CPU_CACHE[key]
+    from oracle import torch_cpu_path as tp
     g = torch.Generator().manual_seed(spec["seed"])
-    ops_total = 0.0
-    elapsed = 0.0
-    h = None
-    if spec["route"] == "mlp":
-        return _cpu_mlp(spec, args, rows, threads, g)
-    for i, l in enumerate(spec["layers"]):
-        if h is not None and i >= len(spec["inputs"]):
-            x = h
-        else:
-            x = torch.randn(rows, l.K, generator=g).to(torch.bfloat16)
+    layers = []
+    for l in spec["layers"]:
         w = torch.randn(l.N, l.K, generator=g) * 0.02
         b = (torch.randn(l.N, generator=g) * 0.01).to(torch.bfloat16)
-        if spec["route"] == "fp8":
-            wq, ws = oracle.quantize_fp8_tensorwise(w)
-            t = time.perf_counter()
-            xq, xs = oracle.quantize_fp8_tensorwise(x)
-            y = oracle.scaled_mm_fp8(xq, wq, xs.reshape(1), ws.reshape(1), None, b, torch.bfloat16, l.act)
-        elif spec["route"] == "int8":
-            wq, ws = oracle.quantize_weight_int8_per_channel(w)
-            t = time.perf_counter()
-            y = oracle.int8_linear(x, wq, ws, b, act=l.act)
+        if spec["route"] in ("int8", "mlp"):
+            s = (w.abs().amax(dim=1) / 127.0).clamp_min(1e-30)
+            q = torch.clamp(torch.round(w / s[:, None]), -128, 127).to(torch.int8)
+            layers.append((q, s, b))
         else:
-            wq, ws = oracle.quantize_fp8_tensorwise(w)
-            t = time.perf_counter()
-            y = oracle.w8a16_linear(x, wq, ws.reshape(1), b, l.act)
+            q, s = tp.quantize_fp8_tensorwise(w.to(torch.bfloat16))
+            layers.append((q, s, b))
+    _CPU_CACHE[key] = layers
+    return layers
+
+
+def _cpu_step(spec, rows, seed=0):
+    """One pass of the reference's CPU route over `rows` token rows of every
+    layer (torch CPU kernels, oracle/torch_cpu_path.py).  Returns (ops, seconds);
+    input generation is outside the timed region, weight decode (part of the
+    reference's per-call route) inside it."""
+    from oracle import torch_cpu_path as tp
+    layers = _cpu_layers(spec)
+    g = torch.Generator().manual_seed(1000 + seed)
+    x0 = None
+    ops = elapsed = 0.0
+    h = None
+    if spec["route"] == "mlp":
+        (l1, l2), ((w1, s1, b1), (w2, s2, b2)) = spec["layers"], layers
+        x = torch.randn(rows, l1.K, generator=g).to(torch.bfloat16)
+        t = time.perf_counter()
+        wide = tp.int8_linear(x, w1, s1, b1)
+        gate, up = wide[:, : l1.N // 2], wide[:, l1.N // 2:]
+        act = (torch.nn.functional.silu(gate.float()).to(torch.bfloat16) * up)
+        grp = act.reshape(rows, -1, 256).float()
+        from oracle import oracle
+        hmat = torch.from_numpy(oracle.hadamard_convrot(256)).float()
+        act = (grp @ hmat).reshape(rows, -1).to(torch.bfloat16)
+        tp.int8_linear(act, w2, s2, b2)
+        elapsed = time.perf_counter() - t
+        return 2.0 * rows * (l1.K * l1.N + l2.K * l2.N), elapsed
+    for i, (l, (w, s, b)) in enumerate(zip(spec["layers"], layers)):
+        if i < len(spec["inputs"]):
+            if x0 is None or spec["inputs"][i] != spec["inputs"][0]:
+                x = torch.randn(rows, l.K, generator=g).to(torch.bfloat16)
+                if spec["route"] == "int8":
+                    n_out = spec.get("outliers", max(1, round(l.K / 100)))
+                    x[:, torch.randperm(l.K, generator=g)[:n_out]] *= 20
+                x0 = x0 if x0 is not None else x
+            else:
+                x = x0
+        else:
+            x = h
+        t = time.perf_counter()
+        if spec["route"] == "fp8":
+            y = tp.fp8_linear(x, w, s, b, torch.bfloat16, l.act)
+        elif spec["route"] == "int8":
+            y = tp.int8_linear(x, w, s, b, torch.bfloat16, l.act)
+        else:
+            y = tp.w8a16_linear(x, w, s, b, l.act)
         elapsed += time.perf_counter() - t
-        ops_total += 2.0 * rows * l.K * l.N
+        ops += 2.0 * rows * l.K * l.N
         h = y
-    return {"value": round(ops_total / elapsed / 1e12, 5),
-            "unit": _unit(spec),
-            "cores": threads, "kind": "port",
-            "sample": f"{rows} token rows through every layer of {args.workload} (oracle port of the "
-                      f"reference fallback: numpy/torch CPU), weight prep untimed"}
+    return ops, elapsed
 
 
-def _cpu_mlp(spec, args, rows, threads, g):
-    """The oracle port of the reference's materialised MLP route on a row sample:
-    eager INT8 FC1 -> SwiGLU -> fp32 convrot butterflies -> rowwise quant -> INT8
-    GEMM -> dequant."""
-    from oracle import oracle
-    (l1, l2) = spec["layers"]
-    x = torch.randn(rows, l1.K, generator=g).to(torch.bfloat16)
-    w1q, s1 = oracle.quantize_weight_int8_per_channel(torch.randn(l1.N, l1.K, generator=g) * 0.02)
-    w2q, s2 = oracle.quantize_weight_int8_per_channel(torch.randn(l2.N, l2.K, generator=g) * 0.02)
-    b1 = (torch.randn(l1.N, generator=g) * 0.01).to(torch.bfloat16)
-    b2 = (torch.randn(l2.N, generator=g) * 0.01).to(torch.bfloat16)
-    t = time.perf_counter()
-    wide = oracle.int8_linear(x, w1q, s1, b1)
-    q, xs = oracle.quantize_int8_rowwise(oracle.rotate_convrot_fwht(oracle.swiglu(wide)))
-    oracle.int8_dequant_epilogue(oracle.int_mm(q, w2q.t()), xs, s2, b2)
-    elapsed = time.perf_counter() - t
-    ops_total = 2.0 * rows * (l1.K * l1.N + l2.K * l2.N)
-    return {"value": round(ops_total / elapsed / 1e12, 5), "unit": _unit(spec),
-            "cores": threads, "kind": "port",
-            "sample": f"{rows} token rows through FC1 -> SwiGLU -> convrot -> FC2 of {args.workload} "
-                      f"(oracle port of the reference's materialised route), weight prep untimed"}
+def _cpu_rows(spec, M, target_s, forced=None):
+    """Token rows for a bounded CPU sample of about `target_s` seconds (multiple
+    of 64, at most the workload's M), from one 64-row calibration pass."""
+    if forced:
+        return min(int(forced), M)
+    _cpu_step(spec, min(64, M))  # warm the weights and torch's CPU kernels
+    _, t64 = _cpu_step(spec, min(64, M))
+    rows = int(64 * target_s / max(t64, 1e-3)) // 64 * 64
+    return max(64, min(rows, M))
+
+
+def _cpu_sample_text(spec, rows, args):
+    what = {"int8": "per-token quant -> torch._int_mm -> chunked fp32 rescale + bias (+ GELU)",
+            "fp8": "per-tensor e4m3 quant -> e4m3->bf16 decode of both operands -> bf16 matmul "
+                   "-> fp32 scales -> fp32 bias (+ GELU)",
+            "w8a16": "e4m3->bf16 weight decode -> F.linear -> scale + bias (+ GELU)",
+            "mlp": "INT8 FC1 -> SwiGLU -> convrot -> INT8 FC2 (eager torch)"}[spec["route"]]
+    return (f"{rows} of {spec['M']} token rows per step through every layer of {args.workload}; "
+            f"the reference's CPU fallback route on torch CPU kernels ({what}; "
+            f"oracle/torch_cpu_path.py); weight prep untimed, weight decode timed")
+
+
+def cpu_baseline(spec, args):
+    """The reference's CPU route on a bounded row sample (about 10 s of work)."""
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    rows = _cpu_rows(spec, spec["M"], 5.0, args.cpu_rows)
+    ops = t = 0.0
+    for rep in range(2):
+        o, e = _cpu_step(spec, rows, seed=rep)
+        ops, t = ops + o, t + e
+    return {"value": round(ops / t / 1e12, 5), "unit": _unit(spec), "cores": threads,
+            "kind": "port", "sample": _cpu_sample_text(spec, rows, args) + "; 2 passes"}
 
 
 def run_reference(args):
+    """The reference arm: the reference's CPU route (its kernels are Metal and do
+    not build here) on the host cores, rank 0 only; every step is a bounded row
+    sample of the workload."""
     world, rank, _ = _dist_env()
     spec = _workload_spec(args.workload, args.m)
     if rank != 0:
         return
-    # warmup steps (bounded samples), then K timed steps
-    for _ in range(args.warmup):
-        cpu_baseline(spec, args, rows=args.cpu_rows)
-    vals = []
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    rows = _cpu_rows(spec, spec["M"], args.cpu_step_s, args.cpu_rows)
+    for w in range(args.warmup):
+        _cpu_step(spec, rows, seed=w)
+    ops = t = 0.0
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        vals.append(cpu_baseline(spec, args, rows=args.cpu_rows)["value"])
+    for k in range(args.steps):
+        o, e = _cpu_step(spec, rows, seed=100 + k)
+        ops, t = ops + o, t + e
     wall = time.perf_counter() - t0
-    value = statistics.mean(vals)
+    value = ops / t / 1e12
     line = {
         "metric": "INT8/FP8 linear TOPS and % of tensor-core peak at 1/2/4/8 B200",
         "value": round(value, 5), "unit": _unit(spec),
         "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(wall / max(1, args.steps) * 1e3, 2), "higher_is_better": True,
+        "ms_per_step": round(t / max(1, args.steps) * 1e3, 2), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None,
         "dtype": {"fp8": "e4m3", "int8": "int8", "mlp": "int8", "w8a16": "e4m3xbf16"}[spec["route"]],
         "data": "synthetic (seeded; BASELINE shapes, bounded row sample per step)",
         "config": {"workload": f"{args.workload}: {spec['desc']}", "M_total": spec["M"],
-                   "sample_rows": args.cpu_rows},
-        "cpu_baseline": {"value": round(value, 5),
-                         "unit": _unit(spec),
-                         "cores": os.cpu_count(), "kind": "port",
-                         "sample": f"{args.cpu_rows} token rows per step through every layer; the "
-                                   f"reference's kernels are Metal (Apple GPU) and do not build here, so "
-                                   f"its CPU path is the oracle port of its fallback semantics"},
+                   "sample_rows": rows, "wall_s": round(wall, 2)},
+        "cpu_baseline": {"value": round(value, 5), "unit": _unit(spec), "cores": threads,
+                         "kind": "port", "sample": _cpu_sample_text(spec, rows, args)},
         "e2e": {"value": round(value, 5), "unit": _unit(spec),
                 "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -706,7 +868,12 @@ def main():
                     help="8-bit routes: activation quant in its own launch before each GEMM "
                          "(default, currently faster), or inside the GEMM launch")
     ap.add_argument("--impl", default="b200q", choices=["b200q", "reference"])
-    ap.add_argument("--cpu-rows", type=int, default=256)
+    ap.add_argument("--cpu-rows", type=int, default=None,
+                    help="token rows of the CPU sample (default: sized to --cpu-step-s)")
+    ap.add_argument("--cpu-step-s", type=float, default=4.0,
+                    help="target seconds of CPU work per reference-arm step")
+    ap.add_argument("--no-vendor", dest="vendor", action="store_false",
+                    help="skip the stock-torch (cuBLASLt) comparison of every layer")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -39,6 +39,33 @@ _act_cache = None  # (x_weakref, convrot, groupsize, x_8, x_scale)
 _LINEAR_MAX_ELEMS = 2 ** 31 - 1
 
 
+def half_epilogue_problem(a, b, row_scale, col_scale, bias=None):
+    """Why i8_matmul2d_nt_fused_cs_half would reject these arguments, or None.
+
+    The checks of the reference's host function (int8_gemm.mm:1965-1980):
+    tensors on the GPU, 2-D int8 A [M,K] and B [N,K] with matching K, both
+    contiguous; contiguous float32 row/column scales of M and N elements;
+    positive M, N, K; a bias, when given, of N elements on the GPU."""
+    ts = (a, b, row_scale, col_scale)
+    if not all(isinstance(t, torch.Tensor) and t.device.type == "cuda" for t in ts):
+        return "inputs must be on cuda"
+    if a.dtype != torch.int8 or b.dtype != torch.int8 or a.dim() != 2 or b.dim() != 2:
+        return "a/b must be 2D int8"
+    if a.shape[1] != b.shape[1]:
+        return "K mismatch: A[M,K], B[N,K]"
+    if not (a.is_contiguous() and b.is_contiguous()):
+        return "a/b must be contiguous"
+    if not all(t.dtype == torch.float32 and t.is_contiguous() for t in (row_scale, col_scale)):
+        return "row_scale / col_scale must be contiguous float32"
+    if row_scale.numel() != a.shape[0] or col_scale.numel() != b.shape[0]:
+        return "row_scale must have M and col_scale N elements"
+    if min(a.shape[0], b.shape[0], a.shape[1]) <= 0:
+        return "matrix dimensions must be positive"
+    if bias is not None and (bias.device.type != "cuda" or bias.numel() != b.shape[0]):
+        return "bias must be N cuda elements"
+    return None
+
+
 class _NativeInt8Kernel:
     """The reference's int8_ext module surface (int8_gemm.mm:2626-2715) on b200q ops."""
 
@@ -64,26 +91,10 @@ class _NativeInt8Kernel:
     @staticmethod
     def i8_matmul2d_nt_fused_cs_half(a, b, row_scale, col_scale, bias=None):
         """FP16 two-rounding epilogue (int8_gemm.mm:1965-2024), with the reference
-        host's argument checks (contiguous 2-D int8 operands, float32 scales of M
-        and N elements on the device, M, N, K > 0)."""
-        for t in (a, b, row_scale, col_scale):
-            if not isinstance(t, torch.Tensor) or t.device.type != "cuda":
-                raise RuntimeError("inputs must be on cuda")
-        if a.dtype != torch.int8 or b.dtype != torch.int8 or a.dim() != 2 or b.dim() != 2:
-            raise RuntimeError("a/b must be 2D int8")
-        if a.shape[1] != b.shape[1]:
-            raise RuntimeError("K mismatch: A[M,K], B[N,K]")
-        if not (a.is_contiguous() and b.is_contiguous()):
-            raise RuntimeError("a/b must be contiguous")
-        if (row_scale.dtype != torch.float32 or col_scale.dtype != torch.float32
-                or not row_scale.is_contiguous() or not col_scale.is_contiguous()):
-            raise RuntimeError("row_scale / col_scale must be contiguous float32")
-        if row_scale.numel() != a.shape[0] or col_scale.numel() != b.shape[0]:
-            raise RuntimeError("row_scale must have M and col_scale N elements")
-        if a.shape[0] <= 0 or b.shape[0] <= 0 or a.shape[1] <= 0:
-            raise RuntimeError("matrix dimensions must be positive")
-        if bias is not None and (bias.device.type != "cuda" or bias.numel() != b.shape[0]):
-            raise RuntimeError("bias must be N cuda elements")
+        host's argument checks (half_epilogue_problem)."""
+        problem = half_epilogue_problem(a, b, row_scale, col_scale, bias)
+        if problem is not None:
+            raise RuntimeError(problem)
         return torch.ops.b200q.i8_matmul_nt_fused_cs(a, b, row_scale, col_scale, bias,
                                                       torch.float16)
 

@@ -1,55 +1,81 @@
 """FP16-output INT8 epilogue for Wan 14B's native INT8 projections.
 
-Mirrors the reference's _patches/wan_fp16.py (:17-45): for the three Wan 14B
-projection shapes, ``_int8_linear_prequant`` with an fp16 output first offers the
-pre-quantized activation to ``maybe_prequant``, which runs the INT8 GEMM with the
-fp16 two-rounding epilogue
+Seam (reference _patches/wan_fp16.py): for the three Wan 14B projection
+shapes, ``_int8_linear_prequant`` with an fp16 output first offers the
+pre-quantized activation to ``maybe_prequant``; a non-None answer is the layer's
+output, None means "take the general route".  Its fp16 epilogue rounds twice,
 
     out = half( half(float(C) * (col_scale[n] * row_scale[m])) + bias[n] )
 
-(``i8_matmul2d_nt_fused_cs_half``, int8_gemm.mm:1159-1243, 1965-2024) -- on B200
-the channelwise tcgen05 epilogue with an fp16 output.  Same switches as the
-reference (ASFP8_DIT_EXT=1 to opt in; ASFP8_WAN_FAST, ASFP8_WAN_EXACT,
-ASFP8_WAN_FP16_GEMM default on), same argument guards, and the same latch: a
-failure disables the route for the process and the caller keeps its own path.
+(the reference's ``i8_matmul2d_nt_fused_cs_half``, int8_gemm.mm:1159-1243,
+1965-2024), which on B200 is the channelwise tcgen05 epilogue with an fp16
+output.  The switches are the reference's (ASFP8_DIT_EXT=1 opts in;
+ASFP8_WAN_FAST, ASFP8_WAN_EXACT and ASFP8_WAN_FP16_GEMM default on).
+
+Which calls are taken is decided by the binding's own argument validation
+(``int8_linear_kernel.half_epilogue_problem``), run on the contiguous operands
+the hook would pass, plus this hook's extra conditions: inference only, exact
+``torch.Tensor`` operands (no tensor subclasses), a Wan weight shape and an
+fp16 bias.  A kernel error switches the hook off for the process and the
+caller keeps its general route.
 """
 import os
 
 import torch
 
-_calls = 0
-_dead = False
-_shapes = {(5120, 5120), (13824, 5120), (5120, 13824)}
+# (N, K) of Wan 14B's projections that take this epilogue.
+WAN_WEIGHT_SHAPES = frozenset({(5120, 5120), (13824, 5120), (5120, 13824)})
+# Environment switches and their defaults; all must read "1".
+SWITCHES = (("ASFP8_DIT_EXT", "0"), ("ASFP8_WAN_FAST", "1"), ("ASFP8_WAN_EXACT", "1"),
+            ("ASFP8_WAN_FP16_GEMM", "1"))
+
+
+class _HookState:
+    calls = 0        # successful fp16 epilogue calls
+    disabled = None  # the exception that switched the hook off, if any
+
+
+state = _HookState()
+
+
+def _enabled():
+    return state.disabled is None and all(os.environ.get(k, d) == "1" for k, d in SWITCHES)
+
+
+def _hook_problem(x, row_scale, weight, col_scale, bias):
+    """Conditions of this hook on top of the binding's argument checks."""
+    if torch.is_grad_enabled():
+        return "autograd is on"
+    if tuple(weight.shape) not in WAN_WEIGHT_SHAPES:
+        return "not a Wan 14B projection"
+    if any(type(t) is not torch.Tensor for t in (x, row_scale, weight, col_scale)):
+        return "tensor subclass operand"
+    if row_scale.dtype != torch.float32 or col_scale.dtype != torch.float32:
+        return "scales are not float32"
+    if bias is not None and (type(bias) not in (torch.Tensor, torch.nn.Parameter)
+                             or bias.dtype != torch.float16
+                             or tuple(bias.shape) != (weight.shape[0],)):
+        return "bias is not an fp16 [N] tensor"
+    return None
 
 
 def maybe_prequant(kernel, x, row_scale, weight, col_scale, bias, shape):
     """FP16 output of the pre-quantized Wan projection, or None."""
-    global _calls, _dead
-    if (_dead or torch.is_grad_enabled()
-            or os.environ.get("ASFP8_DIT_EXT") != "1"
-            or os.environ.get("ASFP8_WAN_FAST", "1") != "1"
-            or os.environ.get("ASFP8_WAN_EXACT", "1") != "1"
-            or os.environ.get("ASFP8_WAN_FP16_GEMM", "1") != "1"
-            or kernel is None or not hasattr(kernel, "i8_matmul2d_nt_fused_cs_half")
-            or tuple(weight.shape) not in _shapes
-            or any(type(t) is not torch.Tensor or t.device.type != "cuda"
-                   for t in (x, row_scale, weight, col_scale))
-            or x.dtype != torch.int8 or weight.dtype != torch.int8
-            or row_scale.dtype != torch.float32 or col_scale.dtype != torch.float32
-            or x.ndim != 2 or x.shape[1] != weight.shape[1]
-            or row_scale.numel() != x.shape[0] or col_scale.numel() != weight.shape[0]
-            or (bias is not None and (type(bias) not in (torch.Tensor, torch.nn.Parameter)
-                                      or bias.device.type != "cuda"
-                                      or bias.dtype != torch.float16
-                                      or bias.shape != (weight.shape[0],)))):
+    fn = getattr(kernel, "i8_matmul2d_nt_fused_cs_half", None)
+    if fn is None or not _enabled():
+        return None
+    if _hook_problem(x, row_scale, weight, col_scale, bias) is not None:
+        return None
+    from .int8_linear_kernel import half_epilogue_problem
+    args = (x.contiguous(), weight.contiguous(), row_scale.reshape(-1).contiguous(),
+            col_scale.reshape(-1).contiguous(), bias)
+    if half_epilogue_problem(*args) is not None:
         return None
     try:
-        out = kernel.i8_matmul2d_nt_fused_cs_half(
-            x.contiguous(), weight.contiguous(), row_scale.reshape(-1).contiguous(),
-            col_scale.reshape(-1).contiguous(), bias)
+        out = fn(*args)
     except Exception as exc:
-        _dead = True
-        print(f"[b200q/wan_fp16] keeping the general fp16 route ({exc!r}).")
+        state.disabled = exc
+        print(f"[b200q/wan_fp16] fp16 epilogue off for this process, general route kept ({exc!r}).")
         return None
-    _calls += 1
+    state.calls += 1
     return out.reshape(*shape[:-1], weight.shape[0])

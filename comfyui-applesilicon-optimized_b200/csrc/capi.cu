@@ -1152,15 +1152,26 @@ size_t b200q_w8a16_workspace_size(int64_t M, int64_t N, int64_t K) {
 
 }  // extern "C"
 namespace {
+bool w8a16_args_valid(const void* x, int x_dtype, int64_t ldx, const uint8_t* w, int64_t ldw,
+                      const void* bias, int bias_dtype, int act, const void* out, int out_dtype,
+                      int64_t ldo, int64_t M, int64_t N, int64_t K) {
+  return x && w && out && valid_dims(M, N, K) && K > 0 && ldx >= K && ldw >= K && ldo >= N &&
+         (x_dtype == B200Q_BF16 || x_dtype == B200Q_F16) &&
+         (out_dtype == B200Q_BF16 || out_dtype == B200Q_F16 || out_dtype == B200Q_F32) &&
+         bias_dtype >= B200Q_BIAS_NONE && bias_dtype <= B200Q_BIAS_F32 &&
+         (bias_dtype == B200Q_BIAS_NONE || bias) && act >= B200Q_ACT_NONE &&
+         act <= B200Q_ACT_GELU_ERF;
+}
+
+bool w8a16_tc_operands(const void* x, int64_t ldx, const uint8_t* w, int64_t ldw, int64_t K) {
+  return (K % 16 == 0) && (ldw % 16 == 0) && (ldx % 8 == 0) && aligned16(x) && aligned16(w);
+}
+
 int w8a16_linear_impl(const void* x, int x_dtype, int64_t ldx, const uint8_t* w, int64_t ldw,
                       const float* w_scale, const void* bias, int bias_dtype, int act, void* out,
                       int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K, void* workspace,
                       size_t workspace_bytes, bool allow_decode, void* stream) {
-  if (!x || !w || !out || !valid_dims(M, N, K) || K == 0 || ldx < K || ldw < K || ldo < N ||
-      (x_dtype != B200Q_BF16 && x_dtype != B200Q_F16) ||
-      (out_dtype != B200Q_BF16 && out_dtype != B200Q_F16 && out_dtype != B200Q_F32) ||
-      bias_dtype < B200Q_BIAS_NONE || bias_dtype > B200Q_BIAS_F32 || (bias_dtype != B200Q_BIAS_NONE && !bias) ||
-      act < B200Q_ACT_NONE || act > B200Q_ACT_GELU_ERF)
+  if (!w8a16_args_valid(x, x_dtype, ldx, w, ldw, bias, bias_dtype, act, out, out_dtype, ldo, M, N, K))
     return B200Q_ERR_INVALID;
   const DeviceInfo* d = current_device();
   if (!d) return B200Q_ERR_UNSUPPORTED;
@@ -1171,7 +1182,7 @@ int w8a16_linear_impl(const void* x, int x_dtype, int64_t ldx, const uint8_t* w,
   ep.bias = bias;
   ep.bias_dtype = bias ? bias_dtype : kBiasNone;
   ep.act = act;
-  const bool tc = (K % 16 == 0) && (ldw % 16 == 0) && (ldx % 8 == 0) && aligned16(x) && aligned16(w);
+  const bool tc = w8a16_tc_operands(x, ldx, w, ldw, K);
   if (!tc) {
     dim3 grid((N + 31) / 32, (M + 31) / 32);
     if (grid.y > 65535u) return B200Q_ERR_INVALID;
@@ -1248,14 +1259,37 @@ int b200q_w8a16_linear(const void* x, int x_dtype, int64_t ldx, const uint8_t* w
 static __device__ __align__(256) unsigned char g_noalloc_scratch[B200Q_NOALLOC_SCRATCH_BYTES];
 
 namespace {
-void* g_noalloc_addr[64] = {};
+// Per device: the context the address was looked up in, and the address.  A
+// device reset (or a torn-down and re-created primary context) reloads the
+// module, so a cached address is only reused inside the context it came from.
+struct NoallocSlot {
+  CUcontext ctx = nullptr;
+  void* addr = nullptr;
+};
+NoallocSlot g_noalloc_slot[64];
 std::mutex g_noalloc_mu;
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CtxGetCurrentFn ctx_get_current_fn() {
+  static CtxGetCurrentFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<CtxGetCurrentFn>(nullptr);
+    return reinterpret_cast<CtxGetCurrentFn>(p);
+  }();
+  return fn;
+}
 
 int noalloc_scratch(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return B200Q_ERR_CUDA;
+  CUcontext ctx = nullptr;
+  if (CtxGetCurrentFn f = ctx_get_current_fn()) f(&ctx);
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_addr[dev]) {
+  NoallocSlot& slot = g_noalloc_slot[dev];
+  if (!slot.addr || slot.ctx != ctx) {
     void* p = nullptr;
     const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || !p) {
@@ -1263,10 +1297,32 @@ int noalloc_scratch(void** out) {
               cudaGetErrorString(e));
       return B200Q_ERR_CUDA;
     }
-    g_noalloc_addr[dev] = p;
+    slot.addr = p;
+    slot.ctx = ctx;
   }
-  *out = g_noalloc_addr[dev];
+  *out = slot.addr;
   return B200Q_OK;
+}
+
+// Scratch bytes the call will use, following w8a16_linear_impl's route order
+// with the decoded-weight route off: SIMT kernel (unaligned operands) -> none;
+// planes route when planned and its planes fit the static array; GEMV (M <= 32)
+// -> none; otherwise the weight-stationary kernel's split-K partials + tile
+// counters (0 when it runs unsplit).  B200Q_NOALLOC_SCRATCH_BYTES + 1 means the
+// route needs more than the array holds.
+size_t noalloc_route_bytes(const DeviceInfo* d, const void* x, int x_dtype, int64_t ldx,
+                           const uint8_t* w, int64_t ldw, int64_t M, int64_t N, int64_t K) {
+  if (M == 0 || N == 0 || !w8a16_tc_operands(x, ldx, w, ldw, K)) return 0;
+  const WpPlan wp = w8a16_planes_plan(d, M, N, K, x_dtype == B200Q_F16);
+  if (wp.ok) {
+    const size_t b = wp_workspace_bytes(wp.P, wp.bt, wp.ntt, K);
+    if (b <= B200Q_NOALLOC_SCRATCH_BYTES) return b;
+  }
+  if (w8a16_gemv_selected(M)) return 0;
+  const W16Plan p = w8a16_plan(d->num_sms, M, N, K);
+  if (p.splits <= 1) return 0;
+  const size_t need = ((p.partial_bytes + 255) & ~size_t(255)) + p.counter_bytes;
+  return need <= B200Q_NOALLOC_SCRATCH_BYTES ? need : size_t(B200Q_NOALLOC_SCRATCH_BYTES) + 1;
 }
 }  // namespace
 
@@ -1276,18 +1332,22 @@ int b200q_w8a16_linear_noalloc(const void* x, int x_dtype, int64_t ldx, const ui
                                int64_t ldw, const float* w_scale, const void* bias, int bias_dtype,
                                int act, void* out, int out_dtype, int64_t ldo, int64_t M, int64_t N,
                                int64_t K, void* stream) {
-  if (!x || !w || !out || !valid_dims(M, N, K) || K == 0) return B200Q_ERR_INVALID;
-  size_t need = w8a16_kernel_workspace(M, N, K);
+  if (!w8a16_args_valid(x, x_dtype, ldx, w, ldw, bias, bias_dtype, act, out, out_dtype, ldo, M, N, K))
+    return B200Q_ERR_INVALID;
+  const DeviceInfo* d = current_device();
+  if (!d) return B200Q_ERR_UNSUPPORTED;
+  const size_t need = noalloc_route_bytes(d, x, x_dtype, ldx, w, ldw, M, N, K);
   if (need > B200Q_NOALLOC_SCRATCH_BYTES) return B200Q_ERR_TOO_LARGE;
-  const size_t planes = wp_workspace_any(M, K);  // optional: used when it fits
-  if (planes > need && planes <= B200Q_NOALLOC_SCRATCH_BYTES) need = planes;
   void* scratch = nullptr;
   if (need) {
     const int st = noalloc_scratch(&scratch);
     if (st != B200Q_OK) return st;
   }
-  // The shared path clears the tile counters on `stream` before the kernel
-  // (the partials need no clearing: every split writes its slice first).
+  // Nothing in the array needs clearing by this entry: the split-K route clears
+  // its tile counters on `stream` before the kernel and every split writes its
+  // partial slice before it is read; the planes pass writes the planes and
+  // plane scales of every token the GEMM's epilogue uses (the padding rows of a
+  // token tile feed only accumulator columns that are never read).
   return w8a16_linear_impl(x, x_dtype, ldx, w, ldw, w_scale, bias, bias_dtype, act, out,
                            out_dtype, ldo, M, N, K, scratch,
                            need ? size_t(B200Q_NOALLOC_SCRATCH_BYTES) : 0, false, stream);

@@ -288,12 +288,16 @@ B200Q_API int b200q_w8a16_linear(const void* x, int x_dtype, int64_t ldx, const 
  * cannot allocate device memory themselves -- a host that reaches this library
  * only through the C ABI with buffers it registered up front (no device
  * allocator of its own), or a runtime with a fixed device-memory budget in which
- * every allocation must be planned before the model runs.  The split-K scratch
- * lives in a static device array of B200Q_NOALLOC_SCRATCH_BYTES that every GPU
- * loading this library holds until exit; shapes whose plan needs more scratch
- * are rejected with B200Q_ERR_TOO_LARGE and nothing is launched.  The first
- * call on each device looks up that array's device address (once per device;
- * make that first call before any stream capture).  All calls share the array:
+ * every allocation must be planned before the model runs.  Its scratch (the
+ * small-M planes route's activation planes, or the split-K partials and tile
+ * counters of the weight-stationary kernel) lives in a static device array of
+ * B200Q_NOALLOC_SCRATCH_BYTES that every GPU loading this library holds until
+ * exit.  The route is the one b200q_w8a16_linear would take without the
+ * decoded-weight route; when that route's scratch exceeds the array the call
+ * returns B200Q_ERR_TOO_LARGE and launches nothing (invalid arguments give
+ * B200Q_ERR_INVALID first).  The first call on each device (and again after a
+ * device reset re-creates its context) looks up the array's device address;
+ * make that first call before any stream capture.  All calls share the array:
  * calls whose kernels overlap on the GPU (other streams, other threads) race on
  * it and must be serialised by the caller.  Never calls cudaMalloc/cudaFree. */
 #define B200Q_NOALLOC_SCRATCH_BYTES (16u << 20)

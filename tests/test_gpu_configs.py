@@ -1,0 +1,151 @@
+"""GPU parity at the BASELINE.json configurations, built by bench.py's own
+``B200Block`` (the same seeds, recipes and weight quantization as the timed
+run), checked against the CPU oracle on a sample of token rows.
+
+Rows of these linears are independent (per-token quant, GEMM rows, epilogue),
+so each layer's output rows are compared with the oracle evaluated on the same
+input rows: the first and last 64 rows, the rows of the ragged last 128-row
+tile, and 128 random rows.  The per-tensor FP8 activation scale depends on the
+whole tensor: it is checked against the exact formula (max|x| / 448 computed
+on the device, which is exact), and the sampled rows' e4m3 codes against the
+oracle's quantization with that scale.
+
+Tolerances (north star): INT8 codes, scales and outputs bit-exact (the GELU
+layer within 1 ULP: the GELU is evaluated in fp32 on the GPU and in float64 by
+the oracle); FP8 W8A8 and W8A16 outputs within 1 bf16 ULP of the oracle's fp32
+value (plus 0.1% RMS slack near zero), and the whole sample within 2% of the
+oracle output's RMS.
+
+Pattern: the reference's bit-exact-vs-eager tests at realistic shapes
+(tests/test_int8_linear_kernel.py:151-207 of ComfyUI-AppleSilicon-Optimized).
+"""
+import numpy as np
+import pytest
+import torch
+
+import bench
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+FP8_RMS_TOL = 0.02
+
+
+def _sample_rows(M, seed, n_random=128):
+    g = torch.Generator().manual_seed(seed)
+    rows = set(range(min(64, M))) | set(range(max(0, M - 64), M))
+    tail = (M // 128) * 128
+    rows |= set(range(tail, M)) if tail < M else set()
+    rows |= set(torch.randperm(M, generator=g)[:n_random].tolist())
+    return torch.tensor(sorted(rows), dtype=torch.long)
+
+
+def _block(name, m=None):
+    bench._load_pack()
+    spec = bench._workload_spec(name, m)
+    return spec, bench.B200Block(spec, spec["M"], torch.device("cuda:0"), 0)
+
+
+def _ulp16(a, b):
+    ia = a.view(torch.int16).to(torch.int32)
+    ib = b.view(torch.int16).to(torch.int32)
+    ia = torch.where(ia < 0, -(ia & 0x7FFF), ia)
+    ib = torch.where(ib < 0, -(ib & 0x7FFF), ib)
+    return (ia - ib).abs()
+
+
+def _check_int8_block(spec, blk, seed):
+    ops = torch.ops.b200q
+    outs = blk.step(blk.inputs)
+    torch.cuda.synchronize()
+    h = None
+    for i, (l, (w, s, b), y) in enumerate(zip(spec["layers"], blk.weights, outs)):
+        x = blk.inputs[spec["inputs"][i]] if i < len(spec["inputs"]) else h
+        rows = _sample_rows(blk.M, seed + i)
+        xr = x[rows.cuda()].cpu()
+        # per-token codes and scales of the sampled rows, bit-exact
+        q, xs = ops.quant_rowwise_i8(x)
+        q_ref, xs_ref = oracle.quantize_int8_rowwise(xr)
+        assert torch.equal(q[rows.cuda()].cpu(), q_ref), f"{l.name}: int8 codes"
+        assert torch.equal(xs[rows.cuda()].cpu(), xs_ref), f"{l.name}: row scales"
+        ref = oracle.int8_linear(xr, w.cpu(), s.cpu(), b.cpu(), torch.bfloat16, l.act)
+        got = y[rows.cuda()].cpu()
+        if l.act is None:
+            assert torch.equal(got, ref), (l.name, int(_ulp16(got, ref).max()))
+        else:
+            assert int(_ulp16(got, ref).max()) <= 1, l.name
+        h = y
+
+
+def _check_fp8_block(spec, blk, seed):
+    ops = torch.ops.b200q
+    outs = blk.step(blk.inputs)
+    torch.cuda.synchronize()
+    h = None
+    for i, (l, (w, s, b), y) in enumerate(zip(spec["layers"], blk.weights, outs)):
+        x = blk.inputs[spec["inputs"][i]] if i < len(spec["inputs"]) else h
+        q, xs = ops.fp8_quant_tensorwise(x)
+        amax = float(x.abs().amax().float())
+        want = np.float32(max(np.float32(amax) / np.float32(448.0), np.float32(1e-30)))
+        assert float(xs) == float(want), f"{l.name}: per-tensor scale"
+        rows = _sample_rows(blk.M, seed + i)
+        xr = x[rows.cuda()].cpu()
+        qr = q[rows.cuda()].cpu()
+        v = np.clip(oracle.to_f32(xr) / want, -448.0, 448.0).astype(np.float32)
+        q_ref = torch.from_numpy(v).to(torch.float8_e4m3fn)
+        assert torch.equal(qr.view(torch.uint8), q_ref.view(torch.uint8)), f"{l.name}: e4m3 codes"
+        ref = oracle.scaled_mm_fp8(qr, w.cpu(), xs.reshape(1).cpu(), s.cpu(), None, b.cpu(), None,
+                                   l.act)
+        got = y[rows.cuda()].cpu()
+        assert oracle.elementwise_ulp_ratio(got, ref) <= 1.0, l.name
+        assert oracle.fp8_errors(got, ref)[0] <= FP8_RMS_TOL, l.name
+        h = y
+
+
+def test_config1_int8_linear_recipe():
+    """C1: X [4096, 3072] with 8 outlier channels x20, W per-channel int8, bias."""
+    spec, blk = _block("c1")
+    x = blk.inputs["x"]
+    assert tuple(x.shape) == (4096, 3072) and x.dtype == torch.bfloat16
+    # the outlier recipe: the 8 chosen channels carry ~20x the others' magnitude
+    cols = x.float().abs().mean(dim=0).cpu()
+    idx = blk.outlier_channels
+    assert idx.numel() == 8 and float(cols[idx].min()) > 10 * float(cols.median())
+    _check_int8_block(spec, blk, seed=100)
+
+
+def test_config4_flux_block_int8():
+    """C4: M = 9216; qkv 3072->9216, out 3072->3072, up 3072->12288 + GELU, down 12288->3072."""
+    spec, blk = _block("c4")
+    _check_int8_block(spec, blk, seed=400)
+
+
+def test_config3_fp8_scaled_mm():
+    """C3: M = 8192, K = 12288 -> N = 3072, per-tensor e4m3 scales, bias."""
+    spec, blk = _block("c3")
+    _check_fp8_block(spec, blk, seed=300)
+
+
+def test_config5_wan_block_fp8():
+    """C5: the Wan-14B block at M = 65,520 (qkv, out, up + GELU, down)."""
+    spec, blk = _block("c5")
+    _check_fp8_block(spec, blk, seed=500)
+
+
+@pytest.mark.parametrize("m", [1, 16, 256, 4096])
+def test_config2_w8a16(m):
+    """C2: x [M, 3072] bf16, W e4m3 [12288, 3072] with a per-tensor scale, bias +
+    tanh-GELU, at every M of the config (M = 1, 16, 256 is the HBM-bound regime)."""
+    spec, blk = _block("c2", m)
+    (l,) = spec["layers"]
+    assert (l.K, l.N) == (3072, 12288)
+    (y,) = blk.step(blk.inputs)
+    torch.cuda.synchronize()
+    w, s, b = blk.weights[0]
+    rows = _sample_rows(m, 200 + m)
+    xr = blk.inputs["x"][rows.cuda()].cpu()
+    ref = oracle.w8a16_linear(xr, w.cpu(), s.cpu(), b.cpu(), "gelu_tanh", "fp32")
+    got = y[rows.cuda()].cpu()
+    assert got.dtype == torch.bfloat16 and tuple(y.shape) == (m, 12288)
+    assert oracle.elementwise_ulp_ratio(got, ref) <= 1.0
+    assert oracle.fp8_errors(got, ref)[0] <= FP8_RMS_TOL

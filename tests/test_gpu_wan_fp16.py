@@ -46,9 +46,9 @@ def test_wan_fp16_scaled_integer_output(seam, monkeypatch, rows, width, inner, w
         monkeypatch.setenv("ASFP8_WAN_EXACT", "0")
         general = seam._int8_linear_prequant(xd, rsd, wd, csd, bd, torch.float16, shape)
         monkeypatch.setenv("ASFP8_WAN_EXACT", "1")
-        before = wan_fp16._calls
+        before = wan_fp16.state.calls
         got = seam._int8_linear_prequant(xd, rsd, wd, csd, bd, torch.float16, shape)
-        assert wan_fp16._calls == before + 1 and not wan_fp16._dead
+        assert wan_fp16.state.calls == before + 1 and wan_fp16.state.disabled is None
         assert got.shape == (1, rows, width) and got.dtype == torch.float16
         assert torch.equal(got.view(torch.int16), general.view(torch.int16))
         ref = oracle.int8_dequant_epilogue(oracle.int_mm(x[1:], w[1:].t()), rs[1:], cs[1:], bias,

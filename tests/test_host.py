@@ -384,15 +384,46 @@ def test_linear_fp8_fast_path_untouched():
 
 def test_int8_fast_hook_patches_module(monkeypatch):
     mod = ModuleType("int8_quant")
-    mod.int8_forward_dynamic = lambda *a: "dyn"
+    dyn = lambda *a: "dyn"
+    mod.int8_forward_dynamic = dyn
     mod.int8_forward_dynamic_per_row = lambda *a: "dyn_pr"
     monkeypatch.setattr(int8_linear, "_patched", False)
-    int8_linear._apply(mod)
-    assert mod.int8_forward_dynamic is int8_linear._dyn
+    assert int8_linear.patch_module(mod)
+    assert mod.int8_forward_dynamic.__wrapped__ is dyn
+    assert not int8_linear.patch_module(mod)  # once per process
     # CPU call goes to the node's own function
     x, w, ws = torch.zeros(2, 4), torch.zeros(3, 4, dtype=torch.int8), torch.ones(1)
     assert mod.int8_forward_dynamic(x, w, ws, None, torch.bfloat16) == "dyn"
     assert mod.int8_forward_dynamic_per_row(x, w, ws, None, torch.bfloat16) == "dyn_pr"
+
+
+def test_after_import_patches_a_module_imported_later(monkeypatch, tmp_path):
+    """The deferred path: the target module is imported after the hook is set
+    (int8-fast loading after this pack), from a package directory on disk."""
+    pkg = tmp_path / "fake_int8_fast_pkg"
+    pkg.mkdir()
+    (pkg / "__init__.py").write_text("")
+    (pkg / "int8_quant.py").write_text(
+        "def int8_forward_dynamic(*a):\n    return 'dyn'\n"
+        "def int8_forward_dynamic_per_row(*a):\n    return 'dyn_pr'\n")
+    monkeypatch.syspath_prepend(str(tmp_path))
+    monkeypatch.setattr(int8_linear, "_patched", False)
+    monkeypatch.setattr(_common._HOOK, "pending", {})
+    seen = []
+    ran_now = _common.after_import("int8_quant", lambda m: seen.append(m) or
+                                   int8_linear.patch_module(m), required=int8_linear.TARGETS)
+    assert ran_now is False and seen == []
+    try:
+        import fake_int8_fast_pkg.int8_quant as iq
+        assert seen == [iq] and iq.int8_forward_dynamic.__wrapped__.__name__ == "int8_forward_dynamic"
+        assert iq.__loader__.__class__.__name__ != "_PatchingLoader"
+        x, w, ws = torch.zeros(2, 4), torch.zeros(3, 4, dtype=torch.int8), torch.ones(1)
+        assert iq.int8_forward_dynamic_per_row(x, w, ws, None, torch.bfloat16) == "dyn_pr"
+    finally:
+        for name in ("fake_int8_fast_pkg.int8_quant", "fake_int8_fast_pkg"):
+            sys.modules.pop(name, None)
+        if _common._HOOK in sys.meta_path:
+            sys.meta_path.remove(_common._HOOK)
 
 
 def test_abi_limits_match_the_bindings():
@@ -420,3 +451,15 @@ def test_wan_fp16_hook_eligibility(monkeypatch):
         w2 = torch.zeros(4096, 5120, dtype=torch.int8)
         assert wan_fp16.maybe_prequant(k, x, torch.ones(1), w2, torch.ones(4096), None,
                                        (1, 1, 5120)) is None  # not a Wan shape
+
+
+def test_library_source_makes_no_device_allocation():
+    """The C ABI never allocates device memory (the caller passes every buffer;
+    the allocation-free entry uses a static array): no allocation or free call
+    appears in the library's sources."""
+    csrc = os.path.join(ROOT, "comfyui-applesilicon-optimized_b200", "csrc")
+    pat = re.compile(r"\b(cudaMalloc\w*|cudaFree\w*|cuMemAlloc\w*|cuMemFree\w*|cudaMallocAsync)\s*\(")
+    for name in sorted(os.listdir(csrc)):
+        if name.endswith((".cu", ".cuh", ".h")):
+            text = open(os.path.join(csrc, name)).read()
+            assert not pat.search(text), f"{name} allocates device memory"
