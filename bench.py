@@ -784,12 +784,20 @@ def _cpu_step(spec, rows, seed=0):
 
 def _cpu_rows(spec, M, target_s, forced=None):
     """Token rows for a bounded CPU sample of about `target_s` seconds (multiple
-    of 64, at most the workload's M), from one 64-row calibration pass."""
+    of 64, at most the workload's M).  A step costs a fixed part (the per-call
+    weight decode) plus a part per row: both are fitted from a 64-row and a
+    256-row pass."""
     if forced:
         return min(int(forced), M)
-    _cpu_step(spec, min(64, M))  # warm the weights and torch's CPU kernels
-    _, t64 = _cpu_step(spec, min(64, M))
-    rows = int(64 * target_s / max(t64, 1e-3)) // 64 * 64
+    r0, r1 = min(64, M), min(256, M)
+    _cpu_step(spec, r0)  # warm the weights and torch's CPU kernels
+    _, t0 = _cpu_step(spec, r0)
+    if r1 == r0:
+        return r0
+    _, t1 = _cpu_step(spec, r1)
+    per_row = max((t1 - t0) / (r1 - r0), 1e-7)
+    fixed = max(t0 - r0 * per_row, 0.0)
+    rows = int((target_s - fixed) / per_row) // 64 * 64
     return max(64, min(rows, M))
 
 

@@ -226,8 +226,13 @@ def quantize_fp8_tensorwise(x):
 
 
 def gelu_tanh(v):
+    """tanh-GELU 0.5 v (1 + tanh u), u = sqrt(2/pi) (v + 0.044715 v^3), in float64
+    as the equal form v / (1 + exp(-2u)): 1 + tanh(u) cancels for v below about
+    -5 (where the result is a tiny negative number), this form does not."""
     v = np.asarray(v, dtype=np.float64)
-    return (0.5 * v * (1.0 + np.tanh(0.7978845608028654 * (v + 0.044715 * v ** 3)))).astype(np.float32)
+    u = 0.7978845608028654 * (v + 0.044715 * v ** 3)
+    with np.errstate(over="ignore"):
+        return (v / (1.0 + np.exp(-2.0 * u))).astype(np.float32)
 
 
 def _apply_scale(acc, scale, axis):

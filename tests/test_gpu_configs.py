@@ -12,9 +12,12 @@ oracle's quantization with that scale.
 
 Tolerances (north star): INT8 codes, scales and outputs bit-exact (the GELU
 layer within 1 ULP: the GELU is evaluated in fp32 on the GPU and in float64 by
-the oracle); FP8 W8A8 and W8A16 outputs within 1 bf16 ULP of the oracle's fp32
-value (plus 0.1% RMS slack near zero), and the whole sample within 2% of the
-oracle output's RMS.
+the oracle); FP8 W8A8 and W8A16 bf16 outputs within 1 bf16 ULP of the oracle's
+fp32 value (plus 0.1% RMS slack near zero), and the same launch with an fp32
+output within 2% of the oracle output's RMS, the bf16 output being its RNE
+rounding.  (The 2% bound is not applied to the bf16 tensor itself: rounding a
+4-8 sigma element to bf16 alone moves it by up to 1.6% of sigma, and GELU
+outputs have an RMS well below sigma.)
 
 Pattern: the reference's bit-exact-vs-eager tests at realistic shapes
 (tests/test_int8_linear_kernel.py:151-207 of ComfyUI-AppleSilicon-Optimized).
@@ -98,7 +101,11 @@ def _check_fp8_block(spec, blk, seed):
                                    l.act)
         got = y[rows.cuda()].cpu()
         assert oracle.elementwise_ulp_ratio(got, ref) <= 1.0, l.name
-        assert oracle.fp8_errors(got, ref)[0] <= FP8_RMS_TOL, l.name
+        y32 = ops.fp8_scaled_mm(q, w, xs.reshape(1), s, None, b, torch.float32, l.act or "none")
+        got32 = y32[rows.cuda()].cpu()
+        del y32
+        assert oracle.fp8_errors(got32, ref)[0] <= FP8_RMS_TOL, l.name
+        assert torch.equal(got, got32.to(torch.bfloat16)), l.name
         h = y
 
 
@@ -148,4 +155,7 @@ def test_config2_w8a16(m):
     got = y[rows.cuda()].cpu()
     assert got.dtype == torch.bfloat16 and tuple(y.shape) == (m, 12288)
     assert oracle.elementwise_ulp_ratio(got, ref) <= 1.0
-    assert oracle.fp8_errors(got, ref)[0] <= FP8_RMS_TOL
+    y32 = torch.ops.b200q.w8a16_linear(blk.inputs["x"], w, s, b, "gelu_tanh", torch.float32)
+    got32 = y32[rows.cuda()].cpu()
+    assert oracle.fp8_errors(got32, ref)[0] <= FP8_RMS_TOL
+    assert torch.equal(got, got32.to(torch.bfloat16))
