@@ -422,26 +422,69 @@ def vendor_baseline(blk, flush, reps=5):
 
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
+    """SM clock, power and clock-event reasons of the given CUDA devices, sampled
+    every 5 ms by a thread through NVML (read-only queries) while the context is
+    open; nvidia-smi polling (50 ms) when NVML is unavailable.  Devices are
+    matched to NVML handles by UUID, so CUDA_VISIBLE_DEVICES remapping is
+    honoured."""
+    REASONS = (("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20),
+               ("hw_thermal_slowdown", 0x40), ("hw_power_brake_slowdown", 0x80),
+               ("sw_power_cap", 0x4))
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpus):
-        self.gpus = gpus
-        self.proc = None
+    def __init__(self, cuda_devices, period_s=0.005):
+        self.devices, self.period = list(cuda_devices), period_s
+        self.samples, self.proc, self.thread, self.out = [], None, None, ""
+
+    def _nvml_handles(self):
+        import pynvml
+        pynvml.nvmlInit()
+        hs = []
+        for d in self.devices:
+            uuid = str(torch.cuda.get_device_properties(d).uuid)
+            uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            hs.append(pynvml.nvmlDeviceGetHandleByUUID(uuid))
+        return pynvml, hs
 
     def __enter__(self):
+        if not self.devices:
+            return self
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", ",".join(str(g) for g in self.gpus), "-lms", "50"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            nv, hs = self._nvml_handles()
+            import threading
+            self._stop = threading.Event()
+
+            def run():
+                while not self._stop.is_set():
+                    for h in hs:
+                        try:
+                            self.samples.append((
+                                nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM),
+                                nv.nvmlDeviceGetCurrentClocksEventReasons(h),
+                                nv.nvmlDeviceGetPowerUsage(h) / 1000.0))
+                        except Exception:
+                            pass
+                    self._stop.wait(self.period)
+
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
         except Exception:
-            self.proc = None
+            self.thread = None
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                     "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            except Exception:
+                self.proc = None
         return self
 
     def __exit__(self, *a):
-        self.out = ""
+        if self.thread is not None:
+            self._stop.set()
+            self.thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -450,9 +493,15 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in (getattr(self, "out", "") or "").splitlines():
+        sm, mx, reasons, power = [], None, set(), []
+        for clk, cmax, bits, watts in self.samples:
+            sm.append(float(clk))
+            mx = float(cmax)
+            power.append(watts)
+            for name, bit in self.REASONS:
+                if bits & bit:
+                    reasons.add(name)
+        for line in (self.out or "").splitlines():  # nvidia-smi fallback
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
                 continue
@@ -461,13 +510,17 @@ class ClockSampler:
                 mx = float(f[2])
             except ValueError:
                 continue
-            for n, v in zip(names, f[5:9]):
+            for n, v in zip(["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                             "sw_power_cap"], f[5:9]):
                 if v.lower().startswith("active"):
                     reasons.add(n)
         if not sm:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        out = {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+               "samples": len(sm), "source": "nvml 5 ms" if self.samples else "nvidia-smi 50 ms"}
+        if power:
+            out["power_w_max"] = round(max(power), 1)
+        return out
 
 
 # ----------------------------------------------------------------------------- b200q arm
@@ -514,7 +567,7 @@ def run_b200q(args):
     launches0 = _native.launch_count()
     step_ms = []
     blk.gemm_events = []
-    with ClockSampler(list(range(world)) if rank == 0 else []) as clk:
+    with ClockSampler([dev]) as clk:
         barrier()
         for _ in range(args.steps):
             flush.zero_()
@@ -664,7 +717,7 @@ def run_b200q(args):
         }
         if vendor is not None:
             line["vendor_baseline"] = vendor
-        if args.cpu_baseline:
+        if args.cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(spec, args)
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -196,28 +196,41 @@ __device__ __forceinline__ void epilogue_math(const uint32_t (&r)[32], const flo
                                               float xs, const EpiArgs& e, float (&v)[32]) {
   if constexpr (EPI == kEpiI8Dequant || EPI == kEpiI8SwiGLU || EPI == kEpiI8QkvNormRope) {
     // Reference order (int8_gemm.mm:417-443): s = cs*rs; T(C*s); T(r + bias).
+    // Without an activation the second rounding T(r + bias) is left to the
+    // store's packed conversion (the same nearest-even rounding; every caller
+    // of this path stores through store_chunk), saving a conversion per element.
+    const bool round_bias = e.act != kActNone;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      v[j] = __fmul_rn(i2f_rn(static_cast<int32_t>(r[j])), __fmul_rn(cs[j], rs));
     if (e.out_dtype == kOutF16) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
-        v[j] = round_f16(__fmul_rn(__int2float_rn(static_cast<int32_t>(r[j])), __fmul_rn(cs[j], rs)));
+      for (int j = 0; j < 32; j += 2) round_f16x2(v[j], v[j + 1]);
       if (has_bias) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = round_f16(__fadd_rn(v[j], bi[j]));
+        for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], bi[j]);
+        if (round_bias) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) round_f16x2(v[j], v[j + 1]);
+        }
       }
     } else {
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
-        v[j] = round_bf16(__fmul_rn(__int2float_rn(static_cast<int32_t>(r[j])), __fmul_rn(cs[j], rs)));
+      for (int j = 0; j < 32; j += 2) round_bf16x2(v[j], v[j + 1]);
       if (has_bias) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = round_bf16(__fadd_rn(v[j], bi[j]));
+        for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], bi[j]);
+        if (round_bias) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) round_bf16x2(v[j], v[j + 1]);
+        }
       }
     }
   } else {
     // FP8 route order (scaled_mm_fp8.py:136-146): ((acc*sa)*sb)*sr + bias, fp32.
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-      const float acc = ACC_INT ? __int2float_rn(static_cast<int32_t>(r[j])) : __uint_as_float(r[j]);
+      const float acc = ACC_INT ? i2f_rn(static_cast<int32_t>(r[j])) : __uint_as_float(r[j]);
       v[j] = __fmul_rn(__fmul_rn(__fmul_rn(acc, rs), cs[j]), xs);
     }
     if (has_bias) {
@@ -304,8 +317,8 @@ __device__ __forceinline__ void swiglu_tile_epilogue(uint32_t taddr, int half, i
       uint32_t slow = 0;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        g[j] = round_bf16(__fmul_rn(__int2float_rn(static_cast<int32_t>(rg[j])), __fmul_rn(csg[j], rs)));
-        u[j] = round_bf16(__fmul_rn(__int2float_rn(static_cast<int32_t>(ru[j])), __fmul_rn(csu[j], rs)));
+        g[j] = round_bf16(__fmul_rn(i2f_rn(static_cast<int32_t>(rg[j])), __fmul_rn(csg[j], rs)));
+        u[j] = round_bf16(__fmul_rn(i2f_rn(static_cast<int32_t>(ru[j])), __fmul_rn(csu[j], rs)));
         if (hb) {
           g[j] = round_bf16(__fadd_rn(g[j], big[j]));
           u[j] = round_bf16(__fadd_rn(u[j], biu[j]));
@@ -358,7 +371,7 @@ __device__ __forceinline__ void dequant8_bf16(uint32_t taddr, int n0, float rs, 
   tmem_ld_wait();
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    v[j] = round_bf16(__fmul_rn(__int2float_rn(static_cast<int32_t>(r[j])), __fmul_rn(cs[j], rs)));
+    v[j] = round_bf16(__fmul_rn(i2f_rn(static_cast<int32_t>(r[j])), __fmul_rn(cs[j], rs)));
     if (hb) v[j] = round_bf16(__fadd_rn(v[j], bi[j]));
   }
 }

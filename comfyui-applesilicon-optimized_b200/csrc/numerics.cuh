@@ -24,6 +24,19 @@ __device__ __forceinline__ float round_bf16(float v) {
 }
 __device__ __forceinline__ float round_f16(float v) { return __half2float(__float2half_rn(v)); }
 
+// int32 -> fp32, round to nearest even, on the ALU/FMA pipes instead of the
+// conversion unit (the INT8 epilogues are bound by that unit otherwise):
+// c = hi * 2^11 + lo with |hi| < 2^20 and 0 <= lo < 2^11; both parts convert
+// exactly through the 1.5 * 2^23 / 2^23 magic numbers, and one fma rounds the
+// exact sum once -- the same value as __int2float_rn(c) for every int32.
+__device__ __forceinline__ float i2f_rn(int32_t c) {
+  const int32_t hi = c >> 11;
+  const int32_t lo = c & 0x7FF;
+  const float fh = __fsub_rn(__int_as_float(hi + 0x4B400000), 12582912.0f);
+  const float fl = __fsub_rn(__int_as_float(lo + 0x4B000000), 8388608.0f);
+  return __fmaf_rn(fh, 2048.0f, fl);
+}
+
 template <typename T>
 __device__ __forceinline__ float to_float(T v);
 template <>
@@ -61,15 +74,20 @@ __device__ __forceinline__ uint32_t e4m3x2_to_bf16x2(uint16_t two) {
 // written without cancellation: for negative x the textbook forms
 // 0.5 x (1 + tanh(u)) and 0.5 x (1 + erf(x / sqrt 2)) subtract two numbers close
 // to 1 and lose most of fp32's digits (several fp16 ULPs at x ~ -4).  Identities
-// used: 1 + tanh(u) = 2 / (1 + exp(-2u)) and 1 + erf(z) = erfc(-z).
+// used: 1 + tanh(u) = 2 / (1 + exp(-2u)) and 1 + erf(z) = erfc(-z).  For u < 0
+// the tanh form is evaluated as x t / (1 + t) with t = exp(2u) <= 1, so nothing
+// overflows: x / (1 + exp(-2u)) turned the tiny negative tail (x below about
+// -10, results near 1e-38) into -0.  The divide is the IEEE one (the fast
+// __fdividef returns 0 once the divisor passes 2^126).
 __device__ __forceinline__ float gelu_tanh(float x) {
   const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
   const float k1 = 0.044715f;
   const float u = k0 * (x + k1 * x * x * x);
-  return __fdividef(x, 1.0f + expf(-2.0f * u));
+  const float t = expf(-2.0f * fabsf(u));
+  return __fdiv_rn(u >= 0.0f ? x : x * t, 1.0f + t);
 }
 __device__ __forceinline__ float gelu_erf(float x) {
-  return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f));
+  return 0.5f * x * erfcf(-x * 0.7071067811865476f);
 }
 // SiLU of the reference's SwiGLU kernels (silu_mul_split_bf16,
 // dit_kernels.mm:724-737; i8_swiglu_rot_bf16, int8_gemm.mm:1521-1540):
@@ -198,7 +216,7 @@ __device__ __forceinline__ uint16_t* out_ptr16(const EpiArgs& e, int64_t m, int 
 __device__ __forceinline__ float epi_i8_dequant(int32_t c, float rs, float cs, const EpiArgs& e,
                                                 int n) {
   const float s = __fmul_rn(cs, rs);
-  float v = __fmul_rn(__int2float_rn(c), s);
+  float v = __fmul_rn(i2f_rn(c), s);
   if (e.out_dtype == kOutF16) {
     v = round_f16(v);
     if (e.bias_dtype != kBiasNone) v = round_f16(__fadd_rn(v, load_bias(e.bias, e.bias_dtype, n)));
@@ -249,4 +267,20 @@ __device__ __forceinline__ uint32_t pack_f16x2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&p);
 }
 
+}  // namespace b200q
+
+namespace b200q {
+// Round two floats to bf16 / fp16 (nearest even) with one packed conversion and
+// widen them back exactly (bit moves).
+__device__ __forceinline__ void round_bf16x2(float& a, float& b) {
+  const uint32_t p = pack_bf16x2(a, b);  // low half = a, high half = b
+  a = __uint_as_float(p << 16);
+  b = __uint_as_float(p & 0xFFFF0000u);
+}
+__device__ __forceinline__ void round_f16x2(float& a, float& b) {
+  const uint32_t p = pack_f16x2(a, b);
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&p));
+  a = f.x;
+  b = f.y;
+}
 }  // namespace b200q
