@@ -139,18 +139,42 @@ int launch_gemm8_tc(const DeviceInfo* d, const void* a, int64_t lda, const void*
 }
 
 // CTA-pair kernel: clusters of 2, grid = 2 x min(tiles, SMs / 2).
-template <MmaKind KIND, int STAGES, int EPI, int PRO>
+// B200Q_TMA_STORE=0 keeps the per-thread global stores in the pair kernel's
+// epilogue (A/B runs).
+bool tma_store_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("B200Q_TMA_STORE");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+template <MmaKind KIND, int STAGES, int EPI, int PRO, int KATOMS = 1>
 int launch_gemm8_tc2(const DeviceInfo* d, const void* a, int64_t lda, const void* w, int64_t ldw,
-                     int M, int N, int K, const EpiArgs& ep, const Prologue& pro, cudaStream_t st) {
-  CUtensorMap ta, tb;
+                     int M, int N, int K, const EpiArgs& ep_in, const Prologue& pro, cudaStream_t st) {
+  using L = Gemm8PairLayout<STAGES, KATOMS>;
+  CUtensorMap ta, tb, to;
   if (!make_tmap(&ta, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M, lda, kGemmBK, 128,
                  CU_TENSOR_MAP_SWIZZLE_128B) ||
       !make_tmap(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldw, kGemmBK, 128,
                  CU_TENSOR_MAP_SWIZZLE_128B))
     return B200Q_ERR_CUDA;
-  auto kern = gemm8_tc2_kernel<KIND, STAGES, EPI, PRO>;
-  constexpr int smem = PRO != kProNone ? Gemm8PairLayout<STAGES>::kSmemBytesPro
-                                       : Gemm8PairLayout<STAGES>::kSmemBytes;
+  // 16-bit row-major outputs leave through TMA stores of 32 x 32 blocks
+  EpiArgs ep = ep_in;
+  constexpr bool kStoreEpi = (EPI == kEpiI8Dequant || EPI == kEpiScaled) && PRO == kProNone;
+  ep.tma_store = 0;
+  if (kStoreEpi && tma_store_enabled() && ep.qkv_heads == 0 &&
+      (ep.out_dtype == kOutBF16 || ep.out_dtype == kOutF16) && aligned16(ep.out) &&
+      (ep.ldo * 2) % 16 == 0 &&
+      make_tmap(&to, ep.out,
+                ep.out_dtype == kOutF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                uint64_t(N), uint64_t(M), uint64_t(ep.ldo) * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+    ep.tma_store = 1;
+  if (!ep.tma_store) to = ta;  // unused by the kernel
+  auto kern = gemm8_tc2_kernel<KIND, STAGES, EPI, PRO, KATOMS>;
+  constexpr int smem = PRO != kProNone ? L::kSmemBytesPro
+                       : kStoreEpi     ? L::kSmemBytesStore
+                                       : L::kSmemBytes;
   if (!set_smem(kern, smem)) return B200Q_ERR_CUDA;
   const int64_t tiles = int64_t((M + 255) / 256) * ((N + 255) / 256);
   const int64_t pairs = tiles < d->num_sms / 2 ? tiles : d->num_sms / 2;
@@ -167,7 +191,7 @@ int launch_gemm8_tc2(const DeviceInfo* d, const void* a, int64_t lda, const void
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const cudaError_t le =
-      cudaLaunchKernelEx(&cfg, kern, ta, tb, M, N, K, raster_group_m(lda, ldw, M, N, K), ep, pro);
+      cudaLaunchKernelEx(&cfg, kern, ta, tb, to, M, N, K, raster_group_m(lda, ldw, M, N, K), ep, pro);
   if (le != cudaSuccess) {
     cudaGetLastError();
     fprintf(stderr, "[b200q] cluster launch failed: %s\n", cudaGetErrorString(le));
@@ -185,6 +209,25 @@ int launch_gemm8_simt(const void* a, int64_t lda, const void* w, int64_t ldw, in
                                                         static_cast<const uint8_t*>(w), ldw, M, N,
                                                         K, ep);
   return finish_launch();
+}
+
+// Pair-kernel stage shape: two K atoms (256 bytes, 8 MMAs) per stage in three
+// stages by default; B200Q_PAIR_KATOMS=1 selects six one-atom stages (A/B runs).
+bool pair_two_atoms() {
+  static const bool on = [] {
+    const char* e = getenv("B200Q_PAIR_KATOMS");
+    return !(e && e[0] == '1');
+  }();
+  return on;
+}
+template <MmaKind KIND, int EPI, int PRO>
+int launch_pair(const DeviceInfo* d, const void* a, int64_t lda, const void* w, int64_t ldw,
+                int M, int N, int K, const EpiArgs& ep, const Prologue& pro, cudaStream_t st) {
+  if constexpr (PRO == kProNone) {
+    if (pair_two_atoms())
+      return launch_gemm8_tc2<KIND, 3, EPI, kProNone, 2>(d, a, lda, w, ldw, M, N, K, ep, pro, st);
+  }
+  return launch_gemm8_tc2<KIND, 6, EPI, PRO, 1>(d, a, lda, w, ldw, M, N, K, ep, pro, st);
 }
 
 // B200Q_PAIR_GEMM=0 selects the single-CTA kernel everywhere (A/B measurements).
@@ -216,7 +259,7 @@ int gemm8(const void* a, int64_t lda, const void* w, int64_t ldw, int64_t M, int
   if (N <= 128)
     return launch_gemm8_tc<KIND, 128, 6, EPI, PRO>(d, a, lda, w, ldw, int(M), int(N), int(K), ep, pro, st);
   if (M >= 256 && pair_kernels_enabled())
-    return launch_gemm8_tc2<KIND, 6, EPI, PRO>(d, a, lda, w, ldw, int(M), int(N), int(K), ep, pro, st);
+    return launch_pair<KIND, EPI, PRO>(d, a, lda, w, ldw, int(M), int(N), int(K), ep, pro, st);
   return launch_gemm8_tc<KIND, 256, 4, EPI, PRO>(d, a, lda, w, ldw, int(M), int(N), int(K), ep, pro, st);
 }
 
@@ -229,7 +272,7 @@ int gemm8_swiglu(const void* a, int64_t lda, const void* w, int64_t ldw, int64_t
   if (M == 0 || N2 == 0) return B200Q_OK;
   if (!gemm8_tc_eligible(a, lda, w, ldw, K)) return B200Q_ERR_INVALID;
   if (M >= 256 && pair_kernels_enabled())
-    return launch_gemm8_tc2<MmaKind::I8, 6, kEpiI8SwiGLU, kProNone>(d, a, lda, w, ldw, int(M), int(N2), int(K), ep, Prologue{}, st);
+    return launch_pair<MmaKind::I8, kEpiI8SwiGLU, kProNone>(d, a, lda, w, ldw, int(M), int(N2), int(K), ep, Prologue{}, st);
   return launch_gemm8_tc<MmaKind::I8, 256, 4, kEpiI8SwiGLU, kProNone>(d, a, lda, w, ldw, int(M), int(N2), int(K), ep, Prologue{}, st);
 }
 
@@ -270,7 +313,7 @@ int gemm16(const DeviceInfo* d, const void* a, int64_t lda, const void* w, int64
   if (N <= 128)
     return launch_gemm8_tc<KIND, 128, 6, EPI, kProNone>(d, a, la, w, lw, int(M), int(N), int(kb), ep, Prologue{}, st);
   if (M >= 256 && pair_kernels_enabled())
-    return launch_gemm8_tc2<KIND, 6, EPI, kProNone>(d, a, la, w, lw, int(M), int(N), int(kb), ep, Prologue{}, st);
+    return launch_pair<KIND, EPI, kProNone>(d, a, la, w, lw, int(M), int(N), int(kb), ep, Prologue{}, st);
   return launch_gemm8_tc<KIND, 256, 4, EPI, kProNone>(d, a, la, w, lw, int(M), int(N), int(kb), ep, Prologue{}, st);
 }
 
@@ -941,7 +984,7 @@ int b200q_i8_matmul_nt_dequant_qkv_rms_rope(
   ep.norm_eps = eps;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (M >= 256 && pair_kernels_enabled())
-    return launch_gemm8_tc2<MmaKind::I8, 6, kEpiI8QkvNormRope, kProNone>(d, a, lda, w, ldw, int(M), int(N), int(K), ep, Prologue{}, st);
+    return launch_pair<MmaKind::I8, kEpiI8QkvNormRope, kProNone>(d, a, lda, w, ldw, int(M), int(N), int(K), ep, Prologue{}, st);
   return launch_gemm8_tc<MmaKind::I8, 256, 4, kEpiI8QkvNormRope, kProNone>(d, a, lda, w, ldw, int(M), int(N), int(K), ep, Prologue{}, st);
 }
 

@@ -701,24 +701,41 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // loads complete on the even CTA's `full` barrier; each MMA batch's commit
 // signals both CTAs' `empty` barriers; accumulators land in each CTA's own TMEM
 // (its 128 rows x 256 columns) and each CTA runs its own epilogue.
-template <int STAGES>
+// KATOMS 128-byte swizzle atoms of K per stage: one TMA box per atom and operand,
+// 4 MMAs (K = 32 bytes each) per atom.  Measured on B200: the pipeline costs a
+// roughly fixed ~1.1k cycles per stage hand-off beyond its MMAs, so a stage of
+// one atom (4 MMAs = 512 tensor cycles) left the tensor pipe idle half the time;
+// two atoms per stage (8 MMAs) amortise it.
+template <int STAGES, int KATOMS = 1>
 struct Gemm8PairLayout {
-  static constexpr int kATile = 128 * kGemmBK;  // this CTA's A rows
-  static constexpr int kBTile = 128 * kGemmBK;  // this CTA's half of the W rows
+  static constexpr int kAtom = 128 * kGemmBK;            // one 128-row x 128-byte box
+  static constexpr int kATile = KATOMS * kAtom;          // this CTA's A rows
+  static constexpr int kBTile = KATOMS * kAtom;          // this CTA's half of the W rows
   static constexpr int kStageBytes = kATile + kBTile;
   static constexpr int kBarOffset = STAGES * kStageBytes;
   static constexpr int kBarBytes = (2 * STAGES + 4) * 8 + 16;
   static constexpr int kSmemBytes = kBarOffset + kBarBytes + 1024;
   static constexpr int kQuantOffset = (kBarOffset + kBarBytes + 127) & ~127;
   static constexpr int kSmemBytesPro = kQuantOffset + kQSmemBytes + 1024;
+  // TMA-store epilogue: one 32 x 32 16-bit staging block per epilogue warp
+  // (512-byte aligned for the 64-byte swizzle), then the tile's column scales
+  // and biases as floats, double-buffered by tile.
+  static constexpr int kEpiOffset = (kBarOffset + kBarBytes + 511) & ~511;
+  static constexpr int kEpiBlock = 32 * 32 * 2;
+  static constexpr int kParOffset = kEpiOffset + 8 * kEpiBlock;
+  static constexpr int kParBarOffset = kParOffset + 2 * 2 * 256 * 4;  // 2 mbarriers
+  static constexpr int kSmemBytesStore = kParBarOffset + 16 + 1024;
   static constexpr uint32_t kTmemCols = 512;  // 2 x 256-column accumulators
 };
 
-template <MmaKind KIND, int STAGES, int EPI, int PRO>
+template <MmaKind KIND, int STAGES, int EPI, int PRO, int KATOMS = 1>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm8_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     int M, int N, int K, int group_m, EpiArgs ep, Prologue pro) {
-  using L = Gemm8PairLayout<STAGES>;
+                     const __grid_constant__ CUtensorMap tmOut, int M, int N, int K, int group_m,
+                     EpiArgs ep, Prologue pro) {
+  static_assert(KATOMS == 1 || PRO == kProNone, "the quant prologue bands use one-atom stages");
+  using L = Gemm8PairLayout<STAGES, KATOMS>;
+  constexpr int kStageK = KATOMS * kGemmBK;  // K bytes per pipeline stage
   constexpr int BM = 256, BN = 256;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -745,7 +762,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int num_m = (M + BM - 1) / BM;
   const int num_n = ((kSwiGLU ? F : N) + kTileN - 1) / kTileN;
   const int num_tiles = num_m * num_n;
-  const int num_kb = (K + kGemmBK - 1) / kGemmBK;
+  const int num_kb = (K + kStageK - 1) / kStageK;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -755,6 +772,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 2 * 8);  // 8 epilogue warps in each CTA
+    }
+    if constexpr ((EPI == kEpiI8Dequant || EPI == kEpiScaled) && PRO == kProNone) {
+      if (ep.tma_store) {
+        uint64_t* par_full = reinterpret_cast<uint64_t*>(smem + L::kParBarOffset);
+        mbar_init(&par_full[0], 256);  // every epilogue thread stores one column's params
+        mbar_init(&par_full[1], 256);
+      }
     }
     *abort_flag = 0;
     if constexpr (PRO != kProNone) {
@@ -808,8 +832,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) { ok = false; break; }
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * L::kStageBytes);
           const uint32_t bar = leader_full0 + stage * 8;
-          tma_load_2d_pair(&tmA, bar, sA + stage * L::kATile, kb * kGemmBK, a_row);
-          tma_load_2d_pair(&tmB, bar, sB + stage * L::kBTile, kb * kGemmBK, b_row);
+#pragma unroll
+          for (int a = 0; a < KATOMS; ++a) {
+            // K past the end (a ragged last stage) reads as zeros
+            const int x = kb * kStageK + a * kGemmBK;
+            tma_load_2d_pair(&tmA, bar, sA + stage * L::kATile + a * L::kAtom, x, a_row);
+            tma_load_2d_pair(&tmB, bar, sB + stage * L::kBTile + a * L::kAtom, x, b_row);
+          }
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
       }
@@ -836,11 +865,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
           tc_fence_after();
-          const uint64_t adesc = make_sw128_desc(smem_u32(sA + stage * L::kATile));
-          const uint64_t bdesc = make_sw128_desc(smem_u32(sB + stage * L::kBTile));
 #pragma unroll
-          for (int k = 0; k < kGemmBK / 32; ++k)
-            umma_ss_pair<KIND>(d_tmem, adesc + 2 * k, bdesc + 2 * k, kIdesc, (kb | k) != 0 ? 1u : 0u);
+          for (int a = 0; a < KATOMS; ++a) {
+            const uint64_t adesc = make_sw128_desc(smem_u32(sA + stage * L::kATile + a * L::kAtom));
+            const uint64_t bdesc = make_sw128_desc(smem_u32(sB + stage * L::kBTile + a * L::kAtom));
+#pragma unroll
+            for (int k = 0; k < kGemmBK / 32; ++k)
+              umma_ss_pair<KIND>(d_tmem, adesc + 2 * k, bdesc + 2 * k, kIdesc,
+                                 (kb | a | k) != 0 ? 1u : 0u);
+          }
           umma_commit_pair(empty_self + stage * 8);
           umma_commit_pair(empty_peer + stage * 8);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
@@ -874,12 +907,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint32_t acce_leader = mapa_shared(smem_u32(&acc_empty[0]), 0);
     constexpr bool kAccInt = KIND == MmaKind::I8;
     constexpr int kChunks = BN / 64;
+    constexpr bool kStoreEpi = (EPI == kEpiI8Dequant || EPI == kEpiScaled) && PRO == kProNone;
     int it = 0;
     for (int tile = pair; tile < num_tiles; tile += num_pairs, ++it) {
       int mb, nb;
       gemm_tile_coords(tile, num_m, num_n, group_m, mb, nb);
       const int buf = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
+      if constexpr (kStoreEpi) {
+        if (ep.tma_store) {
+          // this tile's 256 column scales and biases (as floats) into shared memory;
+          // the buffer written here was last read two tiles ago, before every
+          // epilogue warp passed the previous tile's barrier
+          float* par = reinterpret_cast<float*>(smem + L::kParOffset) + (it & 1) * 512;
+          uint64_t* par_full = reinterpret_cast<uint64_t*>(smem + L::kParBarOffset);
+          const int et = threadIdx.x - 128;
+          const int n = min(nb * BN + et, N - 1);
+          par[et] = ep.col_scale ? __ldg(ep.col_scale + (ep.col_scale_vec ? n : 0)) : 1.0f;
+          par[256 + et] = load_bias(ep.bias, ep.bias_dtype, n);
+          mbar_arrive(&par_full[it & 1]);
+          if (!mbar_wait_warp(&par_full[it & 1], (it >> 1) & 1, abort_flag)) break;
+        }
+      }
       if (!mbar_wait_warp(&acc_full[buf], acc_phase, abort_flag)) break;
       tc_fence_after();
       const int64_t m = static_cast<int64_t>(mb) * BM + static_cast<int64_t>(rank) * 128 + row_local;
@@ -895,6 +944,54 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (EPI != kEpiInt32 && ep.row_scale && row_ok) rs = __ldcg(ep.row_scale + (ep.row_scale_vec ? m : 0));
       }
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+      if constexpr (kStoreEpi) {
+        if (ep.tma_store) {
+          // Column params of the tile were staged above; each chunk goes
+          // TMEM -> registers -> epilogue math -> 64B-swizzled staging block ->
+          // TMA store of the warp's 32 rows x 32 columns (clipped at M and N).
+          const float* par = reinterpret_cast<const float*>(smem + L::kParOffset) + (it & 1) * 512;
+          uint8_t* stg = smem + L::kEpiOffset + (warp - 4) * L::kEpiBlock;
+          const int y0 = mb * BM + static_cast<int>(rank) * 128 + q * 32;
+          const bool has_bias = ep.bias_dtype != kBiasNone;
+#pragma unroll 1
+          for (int c = half * kChunks; c < (half + 1) * kChunks; ++c) {
+            uint32_t r[32];
+            float cs[32], bi[32], v[32];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 a = reinterpret_cast<const float4*>(par + c * 32)[j];
+              cs[4 * j] = a.x; cs[4 * j + 1] = a.y; cs[4 * j + 2] = a.z; cs[4 * j + 3] = a.w;
+              const float4 b = reinterpret_cast<const float4*>(par + 256 + c * 32)[j];
+              bi[4 * j] = b.x; bi[4 * j + 1] = b.y; bi[4 * j + 2] = b.z; bi[4 * j + 3] = b.w;
+            }
+            tmem_ld32(taddr + c * 32, r);
+            tmem_ld_wait();
+            epilogue_math<EPI, kAccInt>(r, cs, bi, has_bias, rs, xs, ep, v);
+            uint32_t pk[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              pk[j] = ep.out_dtype == kOutF16 ? pack_f16x2(v[2 * j], v[2 * j + 1])
+                                              : pack_bf16x2(v[2 * j], v[2 * j + 1]);
+            if (lane == 0) bulk_wait_read_all();  // the previous block has left the buffer
+            __syncwarp();
+            uint8_t* row = stg + lane * 64;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              *reinterpret_cast<uint4*>(row + ((j ^ ((lane >> 1) & 3)) << 4)) =
+                  make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmOut, stg, nb * BN + c * 32, y0);
+              bulk_commit_group();
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(acce_leader + buf * 8);
+          continue;
+        }
+      }
       if constexpr (kSwiGLU) {
         swiglu_tile_epilogue<BN>(taddr, half, nb * kTileN, F, m, row_ok, rs, ep);
       } else if constexpr (EPI == kEpiI8QkvNormRope) {
@@ -924,6 +1021,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acce_leader + buf * 8);
+    }
+    if constexpr (kStoreEpi) {
+      if (ep.tma_store && lane == 0) bulk_wait_all();  // stores done before the CTA exits
     }
   }
 

@@ -188,6 +188,10 @@ struct EpiArgs {
   const float* k_norm_w;
   int rope_r;
   float norm_eps;
+  // Pair kernel, 16-bit row-major output: stage each 32 x 32 output block in
+  // shared memory and write it with a TMA store (set by the host when the
+  // output is 16-byte aligned with a row stride that is a multiple of 16 bytes).
+  int tma_store;
 };
 
 // Element pointer of output (m, n) for 16-bit outputs, in either layout.
