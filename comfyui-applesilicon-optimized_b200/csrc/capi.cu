@@ -149,6 +149,16 @@ bool tma_store_enabled() {
   return on;
 }
 
+// B200Q_EPI_SLEEP_NS: nanoseconds the pair kernel's epilogue warps sleep between
+// probes of the accumulator barrier (default 0: spin).
+unsigned int epilogue_sleep_ns() {
+  static const unsigned int v = [] {
+    const char* e = getenv("B200Q_EPI_SLEEP_NS");
+    return e ? static_cast<unsigned int>(atoi(e)) : 0u;
+  }();
+  return v;
+}
+
 template <MmaKind KIND, int STAGES, int EPI, int PRO, int KATOMS = 1>
 int launch_gemm8_tc2(const DeviceInfo* d, const void* a, int64_t lda, const void* w, int64_t ldw,
                      int M, int N, int K, const EpiArgs& ep_in, const Prologue& pro, cudaStream_t st) {
@@ -171,6 +181,7 @@ int launch_gemm8_tc2(const DeviceInfo* d, const void* a, int64_t lda, const void
                 uint64_t(N), uint64_t(M), uint64_t(ep.ldo) * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
     ep.tma_store = 1;
   if (!ep.tma_store) to = ta;  // unused by the kernel
+  ep.wait_sleep_ns = epilogue_sleep_ns();
   auto kern = gemm8_tc2_kernel<KIND, STAGES, EPI, PRO, KATOMS>;
   constexpr int smem = PRO != kProNone ? L::kSmemBytesPro
                        : kStoreEpi     ? L::kSmemBytesStore
@@ -497,7 +508,7 @@ bool sync_ok(const unsigned int* sync, size_t sync_bytes, int64_t M) {
 // programmatic dependency on the planes pass.
 struct WpPlan {
   bool ok = false;
-  int bt = 0, P = 0, nt = 0, ntt = 1, S = 1, stages = 0, smem = 0;
+  int bt = 0, P = 0, nt = 0, ntt = 1, S = 1, stages = 0, smem = 0, katoms = 1;
 };
 
 bool env_flag(const char* name, bool dflt) {
@@ -569,51 +580,60 @@ WpPlan w8a16_planes_plan(const DeviceInfo* d, int64_t M, int64_t N, int64_t K, b
   const int bt = wp_bt(M, P);
   const int ntt = wp_ntt(M, bt);
   const int nt = P * bt;
-  const int stage = 128 * kWpBK + nt * kWpBK;
   const int dump = nt * 128 * 4;
   const int tmem = nt <= 32 ? 32 : nt <= 64 ? 64 : nt <= 128 ? 128 : 256;
   const int bar = (2 * kWpMaxStages + 1) * 8 + 16 + 1024;
   const int64_t tiles = (N + 127) / 128;
-  const int nkb = static_cast<int>((K + kWpBK - 1) / kWpBK);
   const char* fs = getenv("B200Q_W8A16_PLANES_SPLITS");
   const int forced_s = fs ? atoi(fs) : 0;
   const char* fc = getenv("B200Q_W8A16_PLANES_CTAS");  // CTAs per SM the ring is sized for
   const int forced_c = fc ? atoi(fc) : 0;
-  const double kb_bytes = 128.0 * kWpBK;
-  const double t_hbm = double(tiles) * nkb * kb_bytes / 6.0e6;  // us
-  const double t_mma = double(tiles) * ntt * nkb * 128.0 * nt * kWpBK / 1.3e9;  // us
+  // K atoms per stage (1 or 2): B200Q_W8A16_PLANES_KATOMS forces one, otherwise
+  // both are costed.  A stage hand-off costs a CTA ~0.36 us whatever the stage
+  // holds (measured: one 16 KB atom per stage streamed ~45 GB/s per CTA), so
+  // two atoms halve the hand-offs but need twice the ring per stage.
+  const char* fk = getenv("B200Q_W8A16_PLANES_KATOMS");
+  const int forced_k = fk ? atoi(fk) : 0;
   double best_cost = 1e30;
-  for (int c = 1; c <= 2; ++c) {
-    if (c * tmem > 512 || (forced_c > 0 && c != forced_c)) continue;
-    const int budget = (c == 1 ? 232448 : 233472 / c - 1024);  // per-CTA dynamic smem
-    int stages = (budget - bar) / stage;
-    if (stages > kWpMaxStages) stages = kWpMaxStages;
-    if (stages < 2) continue;
-    for (int S = 1; S <= 8 && S <= nkb; ++S) {
-      if (forced_s > 0 && S != forced_s) continue;
-      if (S > 1 && dump + bar > budget) continue;  // split ranks park accumulators in the ring
-      const int ring = (S > 1 && dump > stages * stage) ? dump : stages * stage;
-      const int smem = ring + bar;
-      const int64_t ctas = tiles * ntt * S;
-      const double slots = double(c) * d->num_sms * (S > 1 ? 0.9 : 1.0);
-      if (double(ctas) > slots && forced_s == 0) continue;
-      const double t_cta = double((nkb + S - 1) / S) * kb_bytes / 45.0e3;  // us
-      double cost = t_cta > t_hbm ? t_cta : t_hbm;
-      if (t_mma > cost) cost = t_mma;
-      cost += (S > 1 ? 0.3 : 0.0) + 0.1 * S;
-      if (env_flag("B200Q_DEBUG_PLAN", false))
-        fprintf(stderr, "[b200q] planes plan M %lld N %lld K %lld: c %d S %d stages %d smem %d cost %.2f\n",
-                (long long)M, (long long)N, (long long)K, c, S, stages, smem, cost);
-      if (cost < best_cost - 1e-9) {
-        best_cost = cost;
-        best.ok = true;
-        best.bt = bt;
-        best.P = P;
-        best.nt = nt;
-        best.ntt = ntt;
-        best.S = S;
-        best.stages = stages;
-        best.smem = smem;
+  for (int KA = 1; KA <= 2; ++KA) {
+    if (forced_k > 0 && KA != forced_k) continue;
+    const int stage = KA * (128 * kWpBK + nt * kWpBK);
+    const int nkb = static_cast<int>((K + KA * kWpBK - 1) / (KA * kWpBK));  // stages along K
+    const double t_hbm = double(tiles) * double(K) * 128.0 / 6.0e6;        // us
+    const double t_mma = double(tiles) * ntt * double(K) * 128.0 * nt / 1.3e9;  // us
+    for (int c = 1; c <= 2; ++c) {
+      if (c * tmem > 512 || (forced_c > 0 && c != forced_c)) continue;
+      const int budget = (c == 1 ? 232448 : 233472 / c - 1024);  // per-CTA dynamic smem
+      int stages = (budget - bar) / stage;
+      if (stages > kWpMaxStages) stages = kWpMaxStages;
+      if (stages < 2) continue;
+      for (int S = 1; S <= 8 && S <= nkb; ++S) {
+        if (forced_s > 0 && S != forced_s) continue;
+        if (S > 1 && dump + bar > budget) continue;  // split ranks park accumulators in the ring
+        const int ring = (S > 1 && dump > stages * stage) ? dump : stages * stage;
+        const int smem = ring + bar;
+        const int64_t ctas = tiles * ntt * S;
+        const double slots = double(c) * d->num_sms * (S > 1 ? 0.9 : 1.0);
+        if (double(ctas) > slots && forced_s == 0) continue;
+        const double t_cta = double((nkb + S - 1) / S) * 0.364;  // us: stage hand-offs
+        double cost = t_cta > t_hbm ? t_cta : t_hbm;
+        if (t_mma > cost) cost = t_mma;
+        cost += (S > 1 ? 0.3 : 0.0) + 0.1 * S;
+        if (env_flag("B200Q_DEBUG_PLAN", false))
+          fprintf(stderr, "[b200q] planes plan M %lld N %lld K %lld: ka %d c %d S %d stages %d smem %d cost %.2f\n",
+                  (long long)M, (long long)N, (long long)K, KA, c, S, stages, smem, cost);
+        if (cost < best_cost - 1e-9) {
+          best_cost = cost;
+          best.ok = true;
+          best.bt = bt;
+          best.P = P;
+          best.nt = nt;
+          best.ntt = ntt;
+          best.S = S;
+          best.stages = stages;
+          best.smem = smem;
+          best.katoms = KA;
+        }
       }
     }
   }
@@ -694,6 +714,7 @@ int launch_w8a16_planes(const WpPlan& p, const void* x, int x_dtype, int64_t ldx
   args.planes = p.P;
   args.splits = p.S;
   args.stages = p.stages;
+  args.katoms = p.katoms;
   args.pscale = pscale;
   switch (p.nt) {
     case 32: return launch_planes_gemm<32>(p, tw, tx, args, ep, st);

@@ -929,7 +929,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (!mbar_wait_warp(&par_full[it & 1], (it >> 1) & 1, abort_flag)) break;
         }
       }
-      if (!mbar_wait_warp(&acc_full[buf], acc_phase, abort_flag)) break;
+      if (ep.wait_sleep_ns) {
+        if (!__all_sync(0xffffffffu, mbar_wait_sleepy(&acc_full[buf], acc_phase, abort_flag,
+                                                       ep.wait_sleep_ns)))
+          break;
+      } else if (!mbar_wait_warp(&acc_full[buf], acc_phase, abort_flag)) {
+        break;
+      }
       tc_fence_after();
       const int64_t m = static_cast<int64_t>(mb) * BM + static_cast<int64_t>(rank) * 128 + row_local;
       const bool row_ok = m < M;

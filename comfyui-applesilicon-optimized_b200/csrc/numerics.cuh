@@ -192,6 +192,9 @@ struct EpiArgs {
   // shared memory and write it with a TMA store (set by the host when the
   // output is 16-byte aligned with a row stride that is a multiple of 16 bytes).
   int tma_store;
+  // Pair kernel: the epilogue warps sleep this long between probes of the
+  // accumulator barrier (0 = spin on try_wait).
+  unsigned int wait_sleep_ns;
 };
 
 // Element pointer of output (m, n) for 16-bit outputs, in either layout.

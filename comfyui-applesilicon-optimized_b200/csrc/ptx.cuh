@@ -111,6 +111,27 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) 
   return true;
 }
 
+// Bounded wait for roles that are not on the tensor pipe's critical path (the
+// epilogue waiting for an accumulator that takes microseconds to fill): after a
+// failed probe the thread sleeps `sleep_ns` instead of probing again at once,
+// which keeps waiting warps from spending issue slots and power.
+__device__ __forceinline__ bool mbar_wait_sleepy(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                                 uint32_t sleep_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  uint32_t polls = 0;
+  while (true) {
+    if (*abort) return false;
+    __nanosleep(sleep_ns);
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((++polls & 63u) == 0u && globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      atomicOr(&g_device_status, kStatusWaitTimeout);
+      *abort = 1;
+      return false;
+    }
+  }
+}
+
 // Warp-uniform variant: every lane waits, and the warp proceeds only if all
 // lanes saw the phase complete (so .sync.aligned tcgen05 ops stay uniform).
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort) {

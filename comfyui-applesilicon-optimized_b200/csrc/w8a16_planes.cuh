@@ -93,6 +93,7 @@ struct WpArgs {
   int planes;             // P = 2 (bf16 activations) or 3 (fp16)
   int splits;             // cluster size S
   int stages;             // ring depth (<= kWpMaxStages)
+  int katoms;             // 128-byte K atoms per stage (1 or 2): 4 MMAs per atom
   const float* pscale;    // [ntt][P][bt]: 2^-e_p[t]
 };
 
@@ -334,9 +335,13 @@ __global__ void __maxnreg__(120)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int stages = a.stages;
+  const int KA = a.katoms;
+  // A stage holds KA weight atoms (128 rows x 128 bytes each) followed by KA
+  // plane atoms (NT rows x 128 bytes each); every atom starts 1024-aligned.
+  const int stage_bytes = KA * L::kStage;
   // Ring size exactly as the host sized the allocation: split ranks park their
   // accumulators in the ring afterwards, so with S > 1 it covers the dump too.
-  const int ring = a.splits > 1 ? L::ring_bytes(stages) : stages * L::kStage;
+  const int ring = (a.splits > 1 && L::kDump > stages * stage_bytes) ? L::kDump : stages * stage_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + ring);
   uint64_t* empty = full + kWpMaxStages;
   uint64_t* acc_full = empty + kWpMaxStages;
@@ -352,7 +357,7 @@ __global__ void __maxnreg__(120)
   const int unit = blockIdx.x / S;  // (weight tile, token tile); the cluster's K-splits share it
   const int tile = unit / a.ntt;
   const int tt = unit - tile * a.ntt;
-  const int nkb = (a.K + kWpBK - 1) / kWpBK;
+  const int nkb = (a.K + KA * kWpBK - 1) / (KA * kWpBK);  // stages of KA atoms along K
   const int kb0 = split * nkb / S, kb1 = (split + 1) * nkb / S;
   const int nst = kb1 - kb0;
 
@@ -391,23 +396,31 @@ __global__ void __maxnreg__(120)
       const int pre = nst < stages ? nst : stages;
       // The weights were written before the planes pass started, so they may be
       // read before this grid's dependency on that pass resolves.
+      // K past the end (a ragged last stage) reads as zeros.
       for (int i = 0; i < pre; ++i) {
-        mbar_arrive_expect_tx(&full[i], L::kStage);
-        tma_load_2d(&tmW, &full[i], smem + i * L::kStage, (kb0 + i) * kWpBK, tile * 128);
+        mbar_arrive_expect_tx(&full[i], stage_bytes);
+        for (int at = 0; at < KA; ++at)
+          tma_load_2d(&tmW, &full[i], smem + i * stage_bytes + at * L::kWSlot,
+                      ((kb0 + i) * KA + at) * kWpBK, tile * 128);
       }
       griddep_wait();
       for (int i = 0; i < pre; ++i)
-        tma_load_2d(&tmX, &full[i], smem + i * L::kStage + L::kWSlot, (kb0 + i) * kWpBK, tt * NT);
+        for (int at = 0; at < KA; ++at)
+          tma_load_2d(&tmX, &full[i], smem + i * stage_bytes + KA * L::kWSlot + at * L::kXSlot,
+                      ((kb0 + i) * KA + at) * kWpBK, tt * NT);
       int issued = pre;
       bool ok = true;
       for (int i = pre; i < nst; ++i) {
         const int s = i % stages;
         const uint32_t ph = static_cast<uint32_t>(i / stages) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag)) { ok = false; break; }
-        mbar_arrive_expect_tx(&full[s], L::kStage);
-        uint8_t* dst = smem + s * L::kStage;
-        tma_load_2d(&tmW, &full[s], dst, (kb0 + i) * kWpBK, tile * 128);
-        tma_load_2d(&tmX, &full[s], dst + L::kWSlot, (kb0 + i) * kWpBK, tt * NT);
+        mbar_arrive_expect_tx(&full[s], stage_bytes);
+        uint8_t* dst = smem + s * stage_bytes;
+        for (int at = 0; at < KA; ++at) {
+          const int x = ((kb0 + i) * KA + at) * kWpBK;
+          tma_load_2d(&tmW, &full[s], dst + at * L::kWSlot, x, tile * 128);
+          tma_load_2d(&tmX, &full[s], dst + KA * L::kWSlot + at * L::kXSlot, x, tt * NT);
+        }
         issued = i + 1;
       }
       if (!ok) {
@@ -426,12 +439,15 @@ __global__ void __maxnreg__(120)
         const int s = i % stages;
         if (!mbar_wait(&full[s], static_cast<uint32_t>(i / stages) & 1u, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        const uint64_t adesc = make_sw128_desc(smem_u32(smem + s * L::kStage));
-        const uint64_t bdesc = make_sw128_desc(smem_u32(smem + s * L::kStage + L::kWSlot));
+        for (int at = 0; at < KA; ++at) {
+          const uint64_t adesc = make_sw128_desc(smem_u32(smem + s * stage_bytes + at * L::kWSlot));
+          const uint64_t bdesc =
+              make_sw128_desc(smem_u32(smem + s * stage_bytes + KA * L::kWSlot + at * L::kXSlot));
 #pragma unroll
-        for (int k = 0; k < 4; ++k)  // K = 32 bytes per MMA = +2 in the >>4 address field
-          umma_ss<MmaKind::F8F6F4>(tmem_d, adesc + 2 * k, bdesc + 2 * k, kIdesc,
-                                   (i > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < 4; ++k)  // K = 32 bytes per MMA = +2 in the >>4 address field
+            umma_ss<MmaKind::F8F6F4>(tmem_d, adesc + 2 * k, bdesc + 2 * k, kIdesc,
+                                     (i > 0 || at > 0 || k > 0) ? 1u : 0u);
+        }
         umma_commit(&empty[s]);
       }
       if (ok) umma_commit(acc_full);
