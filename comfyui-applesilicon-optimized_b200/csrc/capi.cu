@@ -112,10 +112,23 @@ bool valid_dims(int64_t M, int64_t N, int64_t K) {
 // panels.  The threshold is measured, not derived: B200's L2 is split between
 // the two dies, and a 70-80 MB weight swept N-fastest was re-read 4-5x from HBM
 // (C5 qkv/up/down), while <= 38 MB weights (C3, C4, C5 out-proj) gained.
+// For the grouped order the group is at most 16 M-tiles and at most ~28 MB of
+// A panels (256 rows x K bytes each), so the group's A stays in L2 while the
+// weight streams past it: at K = 13,824 a 16-tile group (56 MB of A next to a
+// 71 MB weight) re-read its A panels about 3x.  B200Q_GROUP_M overrides.
 int raster_group_m(int64_t lda, int64_t ldw, int64_t M, int64_t N, int64_t K) {
-  (void)lda; (void)M; (void)K;
+  (void)M;
+  static const int forced = [] {
+    const char* e = getenv("B200Q_GROUP_M");
+    return e ? atoi(e) : 0;
+  }();
+  if (forced > 0) return forced;
   const double w_bytes = double(N) * double(ldw);
-  return w_bytes <= 40.0 * 1024 * 1024 ? 1 : kGemmGroupM;
+  if (w_bytes <= 40.0 * 1024 * 1024) return 1;
+  const double a_panel = 256.0 * double(lda > K ? lda : K);
+  int g = kGemmGroupM;
+  while (g > 4 && g * a_panel > 28.0 * 1024 * 1024) g >>= 1;
+  return g;
 }
 
 // ------------------------------------------------------------ 8-bit GEMM dispatch
