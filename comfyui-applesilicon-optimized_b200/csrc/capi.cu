@@ -172,14 +172,14 @@ unsigned int epilogue_sleep_ns() {
   return v;
 }
 
-template <MmaKind KIND, int STAGES, int EPI, int PRO, int KATOMS = 1>
+template <MmaKind KIND, int STAGES, int EPI, int PRO, int KATOMS = 1, int BN = 256>
 int launch_gemm8_tc2(const DeviceInfo* d, const void* a, int64_t lda, const void* w, int64_t ldw,
                      int M, int N, int K, const EpiArgs& ep_in, const Prologue& pro, cudaStream_t st) {
-  using L = Gemm8PairLayout<STAGES, KATOMS>;
+  using L = Gemm8PairLayout<STAGES, KATOMS, BN>;
   CUtensorMap ta, tb, to;
   if (!make_tmap(&ta, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M, lda, kGemmBK, 128,
                  CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_tmap(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldw, kGemmBK, 128,
+      !make_tmap(&tb, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldw, kGemmBK, BN / 2,
                  CU_TENSOR_MAP_SWIZZLE_128B))
     return B200Q_ERR_CUDA;
   // 16-bit row-major outputs leave through TMA stores of 32 x 32 blocks
@@ -195,12 +195,12 @@ int launch_gemm8_tc2(const DeviceInfo* d, const void* a, int64_t lda, const void
     ep.tma_store = 1;
   if (!ep.tma_store) to = ta;  // unused by the kernel
   ep.wait_sleep_ns = epilogue_sleep_ns();
-  auto kern = gemm8_tc2_kernel<KIND, STAGES, EPI, PRO, KATOMS>;
+  auto kern = gemm8_tc2_kernel<KIND, STAGES, EPI, PRO, KATOMS, BN>;
   constexpr int smem = PRO != kProNone ? L::kSmemBytesPro
                        : kStoreEpi     ? L::kSmemBytesStore
                                        : L::kSmemBytes;
   if (!set_smem(kern, smem)) return B200Q_ERR_CUDA;
-  const int64_t tiles = int64_t((M + 255) / 256) * ((N + 255) / 256);
+  const int64_t tiles = int64_t((M + 255) / 256) * ((N + BN - 1) / BN);
   const int64_t pairs = tiles < d->num_sms / 2 ? tiles : d->num_sms / 2;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs), 1, 1);
@@ -244,12 +244,40 @@ bool pair_two_atoms() {
   }();
   return on;
 }
+// Tile width of the pair kernel: 192 instead of 256 columns when its tile count
+// fills the last wave of CTA pairs clearly better (e.g. 8192 x 3072: 384 tiles =
+// 5.19 waves at 256, 512 tiles = 6.92 waves at 192).  B200Q_PAIR_BN=256/192 forces.
+int pair_tile_n(const DeviceInfo* d, int M, int N) {
+  static const int forced = [] {
+    const char* e = getenv("B200Q_PAIR_BN");
+    return e ? atoi(e) : 0;
+  }();
+  if (forced == 256 || forced == 192) return forced;
+  const int pairs = d->num_sms / 2;
+  auto eff = [&](int bn) {
+    const int64_t nt = (N + bn - 1) / bn;
+    const int64_t tiles = int64_t((M + 255) / 256) * nt;
+    const int64_t waves = (tiles + pairs - 1) / pairs;
+    // useful fraction of the launched tile slots, times the column fill of the
+    // last (ragged) N tile, times a small charge for 192's extra operand bytes
+    const double fill = double(N) / double(nt * bn);
+    return double(tiles) / double(waves * pairs) * fill * (bn == 192 ? 0.97 : 1.0);
+  };
+  return eff(192) > eff(256) + 0.02 ? 192 : 256;
+}
+
 template <MmaKind KIND, int EPI, int PRO>
 int launch_pair(const DeviceInfo* d, const void* a, int64_t lda, const void* w, int64_t ldw,
                 int M, int N, int K, const EpiArgs& ep, const Prologue& pro, cudaStream_t st) {
   if constexpr (PRO == kProNone) {
-    if (pair_two_atoms())
+    if (pair_two_atoms()) {
+      if constexpr (EPI == kEpiInt32 || EPI == kEpiI8Dequant || EPI == kEpiScaled) {
+        if (pair_tile_n(d, M, N) == 192)
+          return launch_gemm8_tc2<KIND, 3, EPI, kProNone, 2, 192>(d, a, lda, w, ldw, M, N, K, ep,
+                                                                   pro, st);
+      }
       return launch_gemm8_tc2<KIND, 3, EPI, kProNone, 2>(d, a, lda, w, ldw, M, N, K, ep, pro, st);
+    }
   }
   return launch_gemm8_tc2<KIND, 6, EPI, PRO, 1>(d, a, lda, w, ldw, M, N, K, ep, pro, st);
 }

@@ -706,11 +706,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // roughly fixed ~1.1k cycles per stage hand-off beyond its MMAs, so a stage of
 // one atom (4 MMAs = 512 tensor cycles) left the tensor pipe idle half the time;
 // two atoms per stage (8 MMAs) amortise it.
-template <int STAGES, int KATOMS = 1>
+// BN: output columns per tile (256, or 192 where the tile count fills the
+// last wave better); each CTA stages BN / 2 of the tile's weight rows.
+template <int STAGES, int KATOMS = 1, int BN = 256>
 struct Gemm8PairLayout {
-  static constexpr int kAtom = 128 * kGemmBK;            // one 128-row x 128-byte box
+  static constexpr int kAtom = 128 * kGemmBK;            // one 128-row x 128-byte box (A)
+  static constexpr int kBAtom = (BN / 2) * kGemmBK;      // this CTA's weight rows, one atom
   static constexpr int kATile = KATOMS * kAtom;          // this CTA's A rows
-  static constexpr int kBTile = KATOMS * kAtom;          // this CTA's half of the W rows
+  static constexpr int kBTile = KATOMS * kBAtom;         // this CTA's half of the W rows
   static constexpr int kStageBytes = kATile + kBTile;
   static constexpr int kBarOffset = STAGES * kStageBytes;
   static constexpr int kBarBytes = (2 * STAGES + 4) * 8 + 16;
@@ -728,15 +731,18 @@ struct Gemm8PairLayout {
   static constexpr uint32_t kTmemCols = 512;  // 2 x 256-column accumulators
 };
 
-template <MmaKind KIND, int STAGES, int EPI, int PRO, int KATOMS = 1>
+template <MmaKind KIND, int STAGES, int EPI, int PRO, int KATOMS = 1, int BN_ = 256>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm8_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmOut, int M, int N, int K, int group_m,
                      EpiArgs ep, Prologue pro) {
   static_assert(KATOMS == 1 || PRO == kProNone, "the quant prologue bands use one-atom stages");
-  using L = Gemm8PairLayout<STAGES, KATOMS>;
+  static_assert(BN_ == 256 || (BN_ == 192 && (EPI == kEpiInt32 || EPI == kEpiI8Dequant ||
+                                               EPI == kEpiScaled)),
+                "the SwiGLU and QKV epilogues use 256-column tiles");
+  using L = Gemm8PairLayout<STAGES, KATOMS, BN_>;
   constexpr int kStageK = KATOMS * kGemmBK;  // K bytes per pipeline stage
-  constexpr int BM = 256, BN = 256;
+  constexpr int BM = 256, BN = BN_;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -820,7 +826,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // SwiGLU: the even CTA loads the gate rows, the odd one the matching up
         // rows, so accumulator columns [0,128) are gate and [128,256) up.
         const int b_row = kSwiGLU ? (rank == 0 ? nb * kTileN : F + nb * kTileN)
-                                  : nb * BN + static_cast<int>(rank) * 128;
+                                  : nb * BN + static_cast<int>(rank) * (BN / 2);
         if constexpr (PRO != kProNone) {
           const int band = a_row / kBandRows;
           if (band != ready_band) {
@@ -837,7 +843,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             // K past the end (a ragged last stage) reads as zeros
             const int x = kb * kStageK + a * kGemmBK;
             tma_load_2d_pair(&tmA, bar, sA + stage * L::kATile + a * L::kAtom, x, a_row);
-            tma_load_2d_pair(&tmB, bar, sB + stage * L::kBTile + a * L::kAtom, x, b_row);
+            tma_load_2d_pair(&tmB, bar, sB + stage * L::kBTile + a * L::kBAtom, x, b_row);
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
@@ -861,14 +867,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t acc_phase = (it >> 1) & 1;
         if (!mbar_wait(&acc_empty[buf], acc_phase ^ 1u, abort_flag)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + buf * BN;
+        const uint32_t d_tmem = tmem_base + buf * 256u;  // accumulators 256 columns apart
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
           for (int a = 0; a < KATOMS; ++a) {
             const uint64_t adesc = make_sw128_desc(smem_u32(sA + stage * L::kATile + a * L::kAtom));
-            const uint64_t bdesc = make_sw128_desc(smem_u32(sB + stage * L::kBTile + a * L::kAtom));
+            const uint64_t bdesc = make_sw128_desc(smem_u32(sB + stage * L::kBTile + a * L::kBAtom));
 #pragma unroll
             for (int k = 0; k < kGemmBK / 32; ++k)
               umma_ss_pair<KIND>(d_tmem, adesc + 2 * k, bdesc + 2 * k, kIdesc,
@@ -949,7 +955,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       } else {
         if (EPI != kEpiInt32 && ep.row_scale && row_ok) rs = __ldcg(ep.row_scale + (ep.row_scale_vec ? m : 0));
       }
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * BN;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + buf * 256u;
       if constexpr (kStoreEpi) {
         if (ep.tma_store) {
           // Column params of the tile were staged above; each chunk goes
