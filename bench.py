@@ -108,7 +108,8 @@ def _base_spec(name):
                     inputs=["x"], desc="INT8 W8A8 single linear (BASELINE config 1)")
     if name == "c3":
         return dict(route="fp8", M=8192, seed=2, hidden=12288, layers=[Layer("down", 12288, 3072)],
-                    inputs=["x"], desc="FP8 W8A8 scaled_mm (BASELINE config 3)")
+                    inputs=["x"], w_std=0.01, x_gelu=True,
+                    desc="FP8 W8A8 scaled_mm (BASELINE config 3)")
     if name == "c2":
         return dict(route="w8a16", M=4096, seed=1, hidden=3072,
                     layers=[Layer("up", 3072, 12288, "gelu_tanh")], inputs=["x"],
@@ -140,7 +141,8 @@ class B200Block:
     on a device generator seeded with the config's seed (their sizes make CPU
     generation slow): weights N(0, 0.02) (per-channel int8 or per-tensor e4m3),
     biases N(0, 0.01), activations N(0, 1) per rank shard, 1% outlier channels
-    x20 for the INT8 configs."""
+    x20 for the INT8 configs.  Config 3 follows its own recipe: weights
+    N(0, 0.01) and the activation GELU(N(0,1))."""
 
     def __init__(self, spec, M, dev, rank, fused=False, start=0):
         self.spec, self.M, self.dev = spec, M, dev
@@ -155,7 +157,7 @@ class B200Block:
         g = torch.Generator(device=dev)
         g.manual_seed(spec["seed"])
         for l in spec["layers"]:
-            w = torch.randn((l.N, l.K), generator=g, device=dev, dtype=torch.float32) * 0.02
+            w = torch.randn((l.N, l.K), generator=g, device=dev, dtype=torch.float32) * spec.get("w_std", 0.02)
             b = (torch.randn((l.N,), generator=g, device=dev) * 0.01).to(torch.bfloat16)
             if spec["route"] in ("int8", "mlp"):
                 s = (w.abs().amax(dim=1) / 127.0).clamp_min(1e-30)
@@ -171,6 +173,8 @@ class B200Block:
         for key in sorted(set(spec["inputs"])):
             K0 = spec["layers"][0].K
             x = torch.randn((M, K0), generator=gx, device=dev, dtype=torch.bfloat16)
+            if spec.get("x_gelu"):  # config 3: the down-projection's input is GELU(N(0,1))
+                x = torch.nn.functional.gelu(x.float()).to(torch.bfloat16)
             if spec["route"] in ("int8", "mlp"):
                 n_out = spec.get("outliers", max(1, round(K0 / 100)))
                 idx = torch.randperm(K0, generator=gx, device=dev)[:n_out]
@@ -713,7 +717,8 @@ def run_b200q(args):
             "ms_per_step": round(t_dev / args.steps, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None,
             "dtype": {"fp8": "e4m3", "int8": "int8", "mlp": "int8", "w8a16": "e4m3xbf16"}[spec["route"]],
-            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights; BASELINE shapes)",
+            "data": (f"synthetic (seeded {'GELU(N(0,1))' if spec.get('x_gelu') else 'N(0,1)'} "
+                     f"activations, N(0,{spec.get('w_std', 0.02)}) weights; BASELINE shapes)"),
             "config": {"workload": f"{args.workload}: {spec['desc']}", "M_total": spec["M"],
                        "M_per_rank": M, "layers": [(l.name, l.K, l.N, l.act) for l in spec["layers"]],
                        "parallelism": f"token-rows split over {world} rank(s), weights replicated, no collective",
@@ -819,7 +824,7 @@ def _cpu_layers(spec):
     g = torch.Generator().manual_seed(spec["seed"])
     layers = []
     for l in spec["layers"]:
-        w = torch.randn(l.N, l.K, generator=g) * 0.02
+        w = torch.randn(l.N, l.K, generator=g) * spec.get("w_std", 0.02)
         b = (torch.randn(l.N, generator=g) * 0.01).to(torch.bfloat16)
         if spec["route"] in ("int8", "mlp"):
             s = (w.abs().amax(dim=1) / 127.0).clamp_min(1e-30)
@@ -861,6 +866,8 @@ def _cpu_step(spec, rows, seed=0):
         if i < len(spec["inputs"]):
             if x0 is None or spec["inputs"][i] != spec["inputs"][0]:
                 x = torch.randn(rows, l.K, generator=g).to(torch.bfloat16)
+                if spec.get("x_gelu"):
+                    x = torch.nn.functional.gelu(x.float()).to(torch.bfloat16)
                 if spec["route"] == "int8":
                     n_out = spec.get("outliers", max(1, round(l.K / 100)))
                     x[:, torch.randperm(l.K, generator=g)[:n_out]] *= 20
