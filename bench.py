@@ -777,6 +777,174 @@ def run_b200q(args):
         torch.distributed.destroy_process_group()
 
 
+NVLINK_GBS = 770.0  # measured peer copy per direction per GPU on this pool's B200s
+
+
+def run_nsplit(args):
+    """--split n: the Wan-shaped block column-parallel.  Every rank holds 1/g of
+    each layer's weight rows (its output columns), computes them for all tokens,
+    and the GEMM epilogue writes each output block into every rank's full-width
+    output (peer mappings over NVLink), so each layer's output is all-gathered
+    inside the GEMM.  A one-element NCCL all-reduce orders the ranks where a
+    layer reads another's gathered output (down after up) and at the end of the
+    step.  The activation quant of each layer input runs on every rank (the
+    inputs are replicated)."""
+    world, rank, local = _dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import datetime
+    pg_kw = dict(timeout=datetime.timedelta(seconds=120), device_id=dev)
+    if world == 1:  # not under torchrun: a one-rank group on an in-process store
+        pg_kw.update(store=torch.distributed.HashStore(), rank=0, world_size=1)
+    torch.distributed.init_process_group("nccl", **pg_kw)
+    _load_pack()
+    from b200q import nsplit
+    from b200q._patches import _native
+    if not _native.available():
+        raise SystemExit("b200q library not built or device is not a B200")
+    if args.workload != "c5":
+        raise SystemExit("--split n is the Wan-shaped block's option (--workload c5)")
+    spec = _workload_spec(args.workload, args.m)
+    M = spec["M"]
+    ops = torch.ops.b200q
+    blk = B200Block(spec, M, dev, 0)   # full weights and inputs, identical on every rank
+    layers = [nsplit.ColumnParallelFP8Linear(w, s, b, l.act)
+              for l, (w, s, b) in zip(spec["layers"], blk.weights)]
+    blk.weights = []                   # keep only this rank's column blocks
+    torch.cuda.empty_cache()
+    outs = [nsplit.PeerOutput(M, l.N, torch.bfloat16, dev) for l in spec["layers"]]
+    n_in = len(spec["inputs"])
+    gemm_events = []
+
+    def step(inputs, record=False):
+        h = None
+        for i, (l, lay, out) in enumerate(zip(spec["layers"], layers, outs)):
+            x = inputs[spec["inputs"][i]] if i < n_in else h
+            xq, xs = ops.fp8_quant_tensorwise(x)
+            if record:
+                ea = torch.cuda.Event(enable_timing=True)
+                ea.record()
+            lay(xq, xs, out)
+            if record:
+                eb = torch.cuda.Event(enable_timing=True)
+                eb.record()
+                gemm_events.append((ea, eb, l, lay.n))
+            if i + 1 < len(layers) and i + 1 >= n_in:
+                nsplit.stream_barrier(device=dev)   # the next layer reads this gathered output
+            h = out.buf
+        nsplit.stream_barrier(device=dev)           # next step rewrites every rank's buffers
+        return [o.buf for o in outs]
+
+    def barrier():
+        torch.cuda.synchronize()
+        torch.distributed.barrier()
+
+    for _ in range(args.warmup):
+        step(blk.inputs)
+    barrier()
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
+    launches0 = _native.launch_count()
+    step_ev = []
+    with ClockSampler([dev]) as clk:
+        barrier()
+        for _ in range(args.steps):
+            flush.zero_()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            step(blk.inputs, record=True)
+            e1.record()
+            step_ev.append((e0, e1))
+        barrier()
+    launches = _native.launch_count() - launches0
+    t_dev = sum(a.elapsed_time(b) for a, b in step_ev)
+    gemm_ms = sum(a.elapsed_time(b) for a, b, _, _ in gemm_events)
+    peaks = _peaks()
+    peak = 2.0 * peaks["bf16"]
+    # Fused compute + all-gather roofline: per launch the slower of the local
+    # GEMM at the tensor peak and the bytes this rank sends over NVLink.
+    t_target = 0.0
+    nvl_bytes = 0.0
+    flops_local = 0.0
+    for _, _, l, n in gemm_events:
+        f = 2.0 * M * l.K * n
+        b = float(M) * n * 2 * (world - 1)
+        flops_local += f
+        nvl_bytes += b
+        t_target += max(f / (peak * 1e12), b / (NVLINK_GBS * 1e9))
+    bound = ("nvlink" if nvl_bytes / (NVLINK_GBS * 1e9) > flops_local / (peak * 1e12)
+             else "tensor")
+
+    # end to end: inputs from pinned host memory, each rank copies its own
+    # column blocks of every output back
+    host_in = {k: v.cpu().pin_memory() for k, v in blk.inputs.items()}
+    host_out = [torch.empty((M, lay.n), dtype=torch.bfloat16).pin_memory() for lay in layers]
+    h2d = sum(t.numel() * t.element_size() for t in host_in.values())
+    d2h = sum(t.numel() * t.element_size() for t in host_out)
+    e2e_steps = max(1, min(args.steps, 3))
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        dev_in = {k: v.to(dev, non_blocking=True) for k, v in host_in.items()}
+        res = step(dev_in)
+        for ho, o, lay in zip(host_out, res, layers):
+            ho.copy_(o[:, lay.c0:lay.c0 + lay.n], non_blocking=True)
+        del dev_in
+    e1.record()
+    barrier()
+    t_e2e = e0.elapsed_time(e1)
+    vals = torch.tensor([t_dev, t_e2e, gemm_ms, float(launches), t_target * 1e3], dtype=torch.float64,
+                        device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(vals, op=torch.distributed.ReduceOp.MAX)
+    t_dev, t_e2e, gemm_ms, launches, t_target_ms = vals.tolist()
+    total_flops = _flops(spec, M)
+    value = total_flops * args.steps / (t_dev / 1e3) / 1e12
+    e2e = total_flops * e2e_steps / (t_e2e / 1e3) / 1e12
+    # per GPU (this rank's column blocks; the slowest rank's GEMM time)
+    achieved = flops_local / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None
+    if rank == 0:
+        line = {
+            "metric": "INT8/FP8 linear TOPS and % of tensor-core peak at 1/2/4/8 B200",
+            "value": round(value, 2), "unit": _unit(spec), "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(t_dev / args.steps, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "e4m3",
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights; BASELINE shapes)",
+            "config": {"workload": f"c5: {spec['desc']}", "M_total": M, "M_per_rank": M,
+                       "layers": [(l.name, l.K, l.N, l.act) for l in spec["layers"]],
+                       "parallelism": (f"column-parallel N-split over {world} rank(s): weight rows "
+                                       "sharded, every layer's output all-gathered inside its "
+                                       "GEMM epilogue over NVLink peer mappings"),
+                       "l2": "flushed (256 MB write) between timed steps, outside the events",
+                       "activation_quant": "own launches before each GEMM, on every rank",
+                       "launch": "eager torch.ops calls; NCCL one-element all-reduce as the "
+                                 "inter-rank barrier (after up, end of step)"},
+            "roofline": {"bound": bound,
+                         "achieved": round(achieved, 1) if achieved else None,
+                         "peak": round(peak, 1), "unit": "TFLOP/s",
+                         "frac": round(t_target_ms / gemm_ms, 4) if gemm_ms > 0 else None,
+                         "frac_definition": ("sum over GEMM launches of max(local FLOPs / "
+                                             "2 x bf16_tflops, NVLink bytes sent / 770 GB/s) "
+                                             "divided by their event-timed duration (max over "
+                                             "ranks)"),
+                         "nvlink_bytes_per_rank_per_step": nvl_bytes / args.steps,
+                         "kernel": "gemm8_tc2_kernel (FP8, TMA-store epilogue to every rank's copy)",
+                         "traffic": None, "gemm_launches_timed": len(gemm_events)},
+            "e2e": {"value": round(e2e, 3), "unit": _unit(spec),
+                    "h2d_bytes_per_step": int(h2d) * world, "d2h_bytes_per_step": int(d2h) * world,
+                    "steps": e2e_steps},
+            "gpu_launches": int(launches),
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    for o in outs:
+        o.close()
+    torch.distributed.barrier()
+    torch.distributed.destroy_process_group()
+
+
 def _gemm_kernel_label(spec, M):
     """Name of the tile kernel the workload's GEMM launches run (the dispatch of
     csrc/capi.cu gemm8/gemm16: CTA pair for M >= 256 and N > 128)."""
@@ -982,6 +1150,10 @@ def main():
     ap.add_argument("--prologue", default="separate", choices=["fused", "separate"],
                     help="8-bit routes: activation quant in its own launch before each GEMM "
                          "(default, currently faster), or inside the GEMM launch")
+    ap.add_argument("--split", default="m", choices=["m", "n"],
+                    help="multi-GPU layout: token rows (default, no communication) or the "
+                         "column-parallel N-split with the all-gather fused into each GEMM "
+                         "(config 5 only)")
     ap.add_argument("--impl", default="b200q", choices=["b200q", "reference"])
     ap.add_argument("--cpu-rows", type=int, default=None,
                     help="token rows of the CPU sample (default: sized to --cpu-step-s)")
@@ -995,6 +1167,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.split == "n":
+        run_nsplit(args)
     else:
         run_b200q(args)
 

@@ -80,6 +80,12 @@ _SIGNATURES = {
                          _i64, _i64, _vp, _vp, _vp], _int),
     "b200q_fp8_scaled_mm": ([_vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _int, _int, _vp,
                              _int, _i64, _i64, _i64, _i64, _vp], _int),
+    "b200q_fp8_scaled_mm_allgather": ([_vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _int,
+                                       _int, _vp, _vp, _int, _int, _i64, _i64, _i64, _i64, _vp],
+                                      _int),
+    "b200q_ipc_export": ([_vp, _vp, ctypes.POINTER(ctypes.c_uint64)], _int),
+    "b200q_ipc_import": ([_vp, ctypes.c_uint64, ctypes.POINTER(_vp), ctypes.POINTER(_vp)], _int),
+    "b200q_ipc_close": ([_vp], _int),
     "b200q_fp8_quant_tensorwise": ([_vp, _int, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp], _int),
     "b200q_prologue_sync_bytes": ([_i64], _sz),
     "b200q_i8_linear_fused": ([_vp, _int, _i64, _vp, _i64, _vp, _i64, _vp, _int, _vp, _int, _i64,
@@ -542,6 +548,66 @@ def fp8_scaled_mm(a, w, scale_a=None, scale_b=None, scale_result=None, bias=None
                                      nb, _p(sr), _p(bias), bdt, ACTS[act], _p(out), code, N, M, N,
                                      K, _stream(a)))
     return out
+
+
+def fp8_scaled_mm_allgather(a, w, scale_a, scale_b, scale_result, bias, out, col0, peer_ptrs,
+                            act=None):
+    """Column-parallel fp8_scaled_mm: w [N,K] e4m3 holds this rank's output
+    columns [col0, col0 + N) of the full-width bf16/f16 ``out`` [M, N_total];
+    the result goes into ``out`` and, at the same position, into each peer copy
+    whose device pointer (already at column col0, from ipc_import) is in
+    ``peer_ptrs``.  Returns ``out``."""
+    _require_cuda(a, w, scale_a, scale_b, scale_result, bias, out)
+    a, w = _rows_2d(a, "a"), _rows_2d(w, "w")
+    M, K = a.shape
+    N = w.shape[0]
+    if w.shape[1] != K or out.dim() != 2 or out.shape[0] != M or out.stride(1) != 1:
+        raise RuntimeError(f"{TAG} fp8_scaled_mm_allgather: shape mismatch")
+    if not 0 <= col0 <= out.shape[1] - N:
+        raise RuntimeError(f"{TAG} fp8_scaled_mm_allgather: columns [{col0}, {col0 + N}) "
+                           f"outside the output's {out.shape[1]}")
+    if len(peer_ptrs) > 7:
+        raise RuntimeError(f"{TAG} fp8_scaled_mm_allgather: at most 7 peer outputs")
+    sa, na = _scale_arg(scale_a, (1, M))
+    sb, nb = _scale_arg(scale_b, (1, N))
+    sr, _ = _scale_arg(scale_result, (1,))
+    code = _out_dtype_code(out.dtype, (torch.bfloat16, torch.float16))
+    bdt = BIAS_NONE
+    if bias is not None:
+        bias = bias.contiguous()
+        if bias.dtype not in _BIAS_DT:
+            bias = bias.float()
+        bdt = _BIAS_DT[bias.dtype]
+    view = out[:, col0:]
+    peers = (ctypes.c_void_p * max(1, len(peer_ptrs)))(*[int(p) for p in peer_ptrs])
+    _check(lib().b200q_fp8_scaled_mm_allgather(
+        _p(a), a.stride(0), _p(w), w.stride(0), _p(sa), na, _p(sb), nb, _p(sr), _p(bias), bdt,
+        ACTS[act], ctypes.c_void_p(view.data_ptr()), peers, len(peer_ptrs), code, out.stride(0),
+        M, N, K, _stream(a)))
+    return out
+
+
+def ipc_export(t):
+    """(64-byte IPC handle, byte offset of t in its allocation) for a CUDA tensor."""
+    _require_cuda(t)
+    h = ctypes.create_string_buffer(64)
+    off = ctypes.c_uint64(0)
+    _check(lib().b200q_ipc_export(_p(t), h, ctypes.byref(off)))
+    return h.raw, int(off.value)
+
+
+def ipc_import(handle, offset):
+    """Maps a peer process's allocation: (device pointer at offset, mapping base)."""
+    if len(handle) != 64:
+        raise RuntimeError(f"{TAG} IPC handles are 64 bytes")
+    ptr, base = ctypes.c_void_p(0), ctypes.c_void_p(0)
+    _check(lib().b200q_ipc_import(ctypes.create_string_buffer(bytes(handle), 64), int(offset),
+                                  ctypes.byref(ptr), ctypes.byref(base)))
+    return int(ptr.value), int(base.value)
+
+
+def ipc_close(base):
+    _check(lib().b200q_ipc_close(ctypes.c_void_p(int(base))))
 
 
 def fp8_linear(x, w, w_scale=None, bias=None, out_dtype=torch.bfloat16, act=None,

@@ -9,6 +9,7 @@
 #include <atomic>
 #include <cstdlib>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 
 #include "../../include/b200q.h"
@@ -174,7 +175,8 @@ unsigned int epilogue_sleep_ns() {
 
 template <MmaKind KIND, int STAGES, int EPI, int PRO, int KATOMS = 1, int BN = 256>
 int launch_gemm8_tc2(const DeviceInfo* d, const void* a, int64_t lda, const void* w, int64_t ldw,
-                     int M, int N, int K, const EpiArgs& ep_in, const Prologue& pro, cudaStream_t st) {
+                     int M, int N, int K, const EpiArgs& ep_in, const Prologue& pro, cudaStream_t st,
+                     const PeerOuts* peers = nullptr) {
   using L = Gemm8PairLayout<STAGES, KATOMS, BN>;
   CUtensorMap ta, tb, to;
   if (!make_tmap(&ta, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M, lda, kGemmBK, 128,
@@ -186,14 +188,23 @@ int launch_gemm8_tc2(const DeviceInfo* d, const void* a, int64_t lda, const void
   EpiArgs ep = ep_in;
   constexpr bool kStoreEpi = (EPI == kEpiI8Dequant || EPI == kEpiScaled) && PRO == kProNone;
   ep.tma_store = 0;
+  // The TMA store clips a box at the row's end only to 16-byte granularity (a
+  // 16-bit row of N = 300 got columns 300..303 written), so ragged widths keep
+  // the per-thread stores.
   if (kStoreEpi && tma_store_enabled() && ep.qkv_heads == 0 &&
       (ep.out_dtype == kOutBF16 || ep.out_dtype == kOutF16) && aligned16(ep.out) &&
-      (ep.ldo * 2) % 16 == 0 &&
+      (ep.ldo * 2) % 16 == 0 && (int64_t(N) * 2) % 16 == 0 &&
       make_tmap(&to, ep.out,
                 ep.out_dtype == kOutF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                 uint64_t(N), uint64_t(M), uint64_t(ep.ldo) * 2, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
     ep.tma_store = 1;
   if (!ep.tma_store) to = ta;  // unused by the kernel
+  PeerOuts po;
+  po.n = 0;
+  if (peers && peers->n > 0) {
+    if (!ep.tma_store) return B200Q_ERR_INVALID;  // peer copies leave through the TMA stores
+    po = *peers;
+  }
   ep.wait_sleep_ns = epilogue_sleep_ns();
   auto kern = gemm8_tc2_kernel<KIND, STAGES, EPI, PRO, KATOMS, BN>;
   constexpr int smem = PRO != kProNone ? L::kSmemBytesPro
@@ -215,7 +226,7 @@ int launch_gemm8_tc2(const DeviceInfo* d, const void* a, int64_t lda, const void
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   const cudaError_t le =
-      cudaLaunchKernelEx(&cfg, kern, ta, tb, to, M, N, K, raster_group_m(lda, ldw, M, N, K), ep, pro);
+      cudaLaunchKernelEx(&cfg, kern, ta, tb, to, po, M, N, K, raster_group_m(lda, ldw, M, N, K), ep, pro);
   if (le != cudaSuccess) {
     cudaGetLastError();
     fprintf(stderr, "[b200q] cluster launch failed: %s\n", cudaGetErrorString(le));
@@ -268,18 +279,20 @@ int pair_tile_n(const DeviceInfo* d, int M, int N) {
 
 template <MmaKind KIND, int EPI, int PRO>
 int launch_pair(const DeviceInfo* d, const void* a, int64_t lda, const void* w, int64_t ldw,
-                int M, int N, int K, const EpiArgs& ep, const Prologue& pro, cudaStream_t st) {
+                int M, int N, int K, const EpiArgs& ep, const Prologue& pro, cudaStream_t st,
+                const PeerOuts* peers = nullptr) {
   if constexpr (PRO == kProNone) {
     if (pair_two_atoms()) {
       if constexpr (EPI == kEpiInt32 || EPI == kEpiI8Dequant || EPI == kEpiScaled) {
         if (pair_tile_n(d, M, N) == 192)
           return launch_gemm8_tc2<KIND, 3, EPI, kProNone, 2, 192>(d, a, lda, w, ldw, M, N, K, ep,
-                                                                   pro, st);
+                                                                   pro, st, peers);
       }
-      return launch_gemm8_tc2<KIND, 3, EPI, kProNone, 2>(d, a, lda, w, ldw, M, N, K, ep, pro, st);
+      return launch_gemm8_tc2<KIND, 3, EPI, kProNone, 2>(d, a, lda, w, ldw, M, N, K, ep, pro, st,
+                                                         peers);
     }
   }
-  return launch_gemm8_tc2<KIND, 6, EPI, PRO, 1>(d, a, lda, w, ldw, M, N, K, ep, pro, st);
+  return launch_gemm8_tc2<KIND, 6, EPI, PRO, 1>(d, a, lda, w, ldw, M, N, K, ep, pro, st, peers);
 }
 
 // B200Q_PAIR_GEMM=0 selects the single-CTA kernel everywhere (A/B measurements).
@@ -1200,6 +1213,131 @@ int b200q_fp8_scaled_mm(const uint8_t* a, int64_t lda, const uint8_t* w, int64_t
   ep.bias_dtype = bias ? bias_dtype : kBiasNone;
   ep.act = act;
   return gemm8<MmaKind::F8F6F4, kEpiScaled>(a, lda, w, ldw, M, N, K, ep, static_cast<cudaStream_t>(stream));
+}
+
+// Column-parallel FP8 GEMM with the all-gather in its epilogue.  This rank owns
+// output columns [c0, c0 + N) of an [M, N_total] output held in full by every
+// rank; `out` and peer_outs[i] point at column c0 of this rank's and of the
+// peers' copies.  On the CTA-pair route with TMA stores every 32 x 32 output
+// block leaves shared memory once per copy, so the NVLink transfer of a tile
+// overlaps the MMAs of the next; other shapes run the plain GEMM into `out` and
+// then copy the block to each peer (one cudaMemcpy2DAsync per peer).
+int b200q_fp8_scaled_mm_allgather(const uint8_t* a, int64_t lda, const uint8_t* w, int64_t ldw,
+                                  const float* scale_a, int64_t scale_a_numel, const float* scale_b,
+                                  int64_t scale_b_numel, const float* scale_result, const void* bias,
+                                  int bias_dtype, int act, void* out, void* const* peer_outs,
+                                  int n_peer_outs, int out_dtype, int64_t ldo, int64_t M, int64_t N,
+                                  int64_t K, void* stream) {
+  if (n_peer_outs < 0 || n_peer_outs > kMaxPeerOuts || (n_peer_outs > 0 && !peer_outs) ||
+      (out_dtype != B200Q_BF16 && out_dtype != B200Q_F16))
+    return B200Q_ERR_INVALID;
+  for (int i = 0; i < n_peer_outs; ++i)
+    if (!peer_outs[i]) return B200Q_ERR_INVALID;
+  if (n_peer_outs == 0)
+    return b200q_fp8_scaled_mm(a, lda, w, ldw, scale_a, scale_a_numel, scale_b, scale_b_numel,
+                               scale_result, bias, bias_dtype, act, out, out_dtype, ldo, M, N, K,
+                               stream);
+  if (!a || !w || !out || !valid_dims(M, N, K) || K == 0 || lda < K || ldw < K || ldo < N ||
+      (scale_a && scale_a_numel != 1 && scale_a_numel != M) ||
+      (scale_b && scale_b_numel != 1 && scale_b_numel != N) ||
+      bias_dtype < B200Q_BIAS_NONE || bias_dtype > B200Q_BIAS_F32 ||
+      (bias_dtype != B200Q_BIAS_NONE && !bias) || act < B200Q_ACT_NONE || act > B200Q_ACT_GELU_ERF)
+    return B200Q_ERR_INVALID;
+  const DeviceInfo* d = current_device();
+  if (!d) return B200Q_ERR_UNSUPPORTED;
+  if (M == 0 || N == 0) return B200Q_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  EpiArgs ep = make_epi(out, ldo, out_dtype, M, N);
+  ep.row_scale = scale_a;
+  ep.row_scale_vec = scale_a && scale_a_numel == M && M != 1 ? 1 : 0;
+  ep.col_scale = scale_b;
+  ep.col_scale_vec = scale_b && scale_b_numel == N && N != 1 ? 1 : 0;
+  ep.extra_scale = scale_result;
+  ep.bias = bias;
+  ep.bias_dtype = bias ? bias_dtype : kBiasNone;
+  ep.act = act;
+  bool fused = gemm8_tc_eligible(a, lda, w, ldw, K) && N > 128 && M >= 256 &&
+               pair_kernels_enabled() && tma_store_enabled() && aligned16(out) &&
+               (ldo * 2) % 16 == 0 && (N * 2) % 16 == 0;
+  PeerOuts po;
+  po.n = n_peer_outs;
+  const CUtensorMapDataType odt =
+      out_dtype == B200Q_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  for (int i = 0; i < n_peer_outs && fused; ++i)
+    fused = aligned16(peer_outs[i]) &&
+            make_tmap(&po.map[i], peer_outs[i], odt, uint64_t(N), uint64_t(M), uint64_t(ldo) * 2,
+                      32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (fused)
+    return launch_pair<MmaKind::F8F6F4, kEpiScaled, kProNone>(d, a, lda, w, ldw, int(M), int(N),
+                                                              int(K), ep, Prologue{}, st, &po);
+  const int s = gemm8<MmaKind::F8F6F4, kEpiScaled>(a, lda, w, ldw, M, N, K, ep, st);
+  if (s != B200Q_OK) return s;
+  const size_t row_bytes = size_t(ldo) * 2;
+  for (int i = 0; i < n_peer_outs; ++i)
+    if (cudaMemcpy2DAsync(peer_outs[i], row_bytes, out, row_bytes, size_t(N) * 2, size_t(M),
+                          cudaMemcpyDefault, st) != cudaSuccess)
+      return B200Q_ERR_CUDA;
+  return B200Q_OK;
+}
+
+// Peer mappings for the column-parallel all-gather: the 64-byte CUDA IPC
+// handle of the allocation holding a device pointer, and the pointer's offset
+// in it; opening a handle maps that allocation into this process (peer access
+// over NVLink enabled lazily).
+namespace {
+using MemGetAddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+MemGetAddressRangeFn address_range_fn() {
+  static MemGetAddressRangeFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<MemGetAddressRangeFn>(nullptr);
+    return reinterpret_cast<MemGetAddressRangeFn>(p);
+  }();
+  return fn;
+}
+}  // namespace
+
+int b200q_ipc_export(const void* dev_ptr, void* handle_out, uint64_t* offset_out) {
+  if (!dev_ptr || !handle_out || !offset_out) return B200Q_ERR_INVALID;
+  MemGetAddressRangeFn range = address_range_fn();
+  if (!range) return B200Q_ERR_CUDA;
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (range(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS)
+    return B200Q_ERR_INVALID;  // not a device allocation
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) {
+    cudaGetLastError();
+    return B200Q_ERR_CUDA;
+  }
+  memcpy(handle_out, &h, sizeof(h));
+  *offset_out = static_cast<uint64_t>(reinterpret_cast<CUdeviceptr>(dev_ptr) - base);
+  return B200Q_OK;
+}
+
+int b200q_ipc_import(const void* handle, uint64_t offset, void** dev_ptr_out, void** base_out) {
+  if (!handle || !dev_ptr_out || !base_out) return B200Q_ERR_INVALID;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  if (cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    cudaGetLastError();
+    return B200Q_ERR_CUDA;
+  }
+  *base_out = base;
+  *dev_ptr_out = static_cast<uint8_t*>(base) + offset;
+  return B200Q_OK;
+}
+
+int b200q_ipc_close(void* base) {
+  if (!base) return B200Q_ERR_INVALID;
+  if (cudaIpcCloseMemHandle(base) != cudaSuccess) {
+    cudaGetLastError();
+    return B200Q_ERR_CUDA;
+  }
+  return B200Q_OK;
 }
 
 int b200q_fp8_quant_tensorwise(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,

@@ -708,6 +708,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // two atoms per stage (8 MMAs) amortise it.
 // BN: output columns per tile (256, or 192 where the tile count fills the
 // last wave better); each CTA stages BN / 2 of the tile's weight rows.
+// Column-parallel all-gather in the pair kernel's TMA-store epilogue: every
+// 32 x 32 output block also goes to up to kMaxPeerOuts more copies of the
+// output (the other ranks' full-width buffers, reached over NVLink through
+// peer mappings), each described by its own tensor map whose origin is this
+// rank's first column there.  n = 0: a plain single-output GEMM.
+constexpr int kMaxPeerOuts = 7;
+struct PeerOuts {
+  CUtensorMap map[kMaxPeerOuts];
+  int n;
+};
+
 template <int STAGES, int KATOMS = 1, int BN = 256>
 struct Gemm8PairLayout {
   static constexpr int kAtom = 128 * kGemmBK;            // one 128-row x 128-byte box (A)
@@ -734,8 +745,8 @@ struct Gemm8PairLayout {
 template <MmaKind KIND, int STAGES, int EPI, int PRO, int KATOMS = 1, int BN_ = 256>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm8_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const __grid_constant__ CUtensorMap tmOut, int M, int N, int K, int group_m,
-                     EpiArgs ep, Prologue pro) {
+                     const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ PeerOuts peers,
+                     int M, int N, int K, int group_m, EpiArgs ep, Prologue pro) {
   static_assert(KATOMS == 1 || PRO == kProNone, "the quant prologue bands use one-atom stages");
   static_assert(BN_ == 256 || (BN_ == 192 && (EPI == kEpiInt32 || EPI == kEpiI8Dequant ||
                                                EPI == kEpiScaled)),
@@ -995,6 +1006,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             __syncwarp();
             if (lane == 0) {
               tma_store_2d(&tmOut, stg, nb * BN + c * 32, y0);
+              for (int p = 0; p < peers.n; ++p)  // the same block into the peers' copies
+                tma_store_2d(&peers.map[p], stg, nb * BN + c * 32, y0);
               bulk_commit_group();
             }
           }
@@ -1035,7 +1048,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (lane == 0) mbar_arrive_cluster(acce_leader + buf * 8);
     }
     if constexpr (kStoreEpi) {
-      if (ep.tma_store && lane == 0) bulk_wait_all();  // stores done before the CTA exits
+      if (ep.tma_store && lane == 0) {
+        bulk_wait_all();  // stores done before the CTA exits
+        if (peers.n > 0) __threadfence_system();  // peer writes performed system-wide
+      }
     }
   }
 

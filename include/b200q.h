@@ -125,6 +125,39 @@ B200Q_API int b200q_fp8_scaled_mm(const uint8_t* a, int64_t lda, const uint8_t* 
                         int bias_dtype, int act, void* out, int out_dtype, int64_t ldo,
                         int64_t M, int64_t N, int64_t K, void* stream);
 
+/* Column-parallel (N-split) b200q_fp8_scaled_mm with its all-gather fused in:
+ * this rank holds the weight rows of output columns [c0, c0 + N) and computes
+ * them for all M tokens; `out` and each of the n_peer_outs (<= 7) peer_outs[i]
+ * point at column c0 of a full-width [M, N_total] output with row stride ldo
+ * (this rank's copy and the other ranks' copies, the latter mapped from them
+ * with b200q_ipc_import).  Each output block is written to every copy (on the
+ * CTA-pair route straight from the epilogue's shared-memory staging block over
+ * NVLink; otherwise the GEMM writes `out` and one 2-D copy per peer follows on
+ * the stream).  bf16/f16 output only.  The peers' copies are complete once the
+ * peers' calls have finished: synchronise the ranks (e.g. a one-element NCCL
+ * all-reduce on this stream) before reading columns other ranks own.  The
+ * reference is single-GPU; this serves the optional N-split of the Wan-shaped
+ * block (its token rows, _patches/int8_linear_kernel_mps.py:75-94, are the
+ * default split, which needs no communication). */
+B200Q_API int b200q_fp8_scaled_mm_allgather(const uint8_t* a, int64_t lda, const uint8_t* w,
+                                            int64_t ldw, const float* scale_a, int64_t scale_a_numel,
+                                            const float* scale_b, int64_t scale_b_numel,
+                                            const float* scale_result, const void* bias,
+                                            int bias_dtype, int act, void* out,
+                                            void* const* peer_outs, int n_peer_outs, int out_dtype,
+                                            int64_t ldo, int64_t M, int64_t N, int64_t K,
+                                            void* stream);
+
+/* Peer mappings for b200q_fp8_scaled_mm_allgather (no reference counterpart).
+ * export: the 64-byte CUDA IPC handle of the device allocation holding dev_ptr
+ * and dev_ptr's byte offset in it.  import (in another process): maps that
+ * allocation (peer access enabled lazily) and returns the pointer at the offset
+ * plus the mapping's base for b200q_ipc_close. */
+B200Q_API int b200q_ipc_export(const void* dev_ptr, void* handle_out, uint64_t* offset_out);
+B200Q_API int b200q_ipc_import(const void* handle, uint64_t offset, void** dev_ptr_out,
+                               void** base_out);
+B200Q_API int b200q_ipc_close(void* base);
+
 /* Per-tensor FP8 activation quantization: amax = max|x|, scale = max(amax/448, 1e-30),
  * q = e4m3 saturating RNE of x/scale.  amax_scratch: one caller-owned device word
  * (overwritten).  No reference counterpart (comfy's quant ops produce the e4m3

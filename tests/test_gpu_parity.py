@@ -117,6 +117,45 @@ def test_dequant_epilogue_channelwise_bit_exact(native, M, K, N, bias, out_dtype
     assert torch.equal(out, ref), f"mismatch M={M} K={K} N={N}"
 
 
+@pytest.mark.parametrize("N", [300, 1001, 129])
+def test_ragged_width_outputs_stay_in_their_columns(native, N):
+    """CTA-pair route (M >= 256) with a row of N 16-bit outputs that is not a
+    multiple of 16 bytes, written into a wider buffer (row stride N + 40): the
+    N columns equal the contiguous call's and no column past N is touched, for
+    the FP8-scaled and the INT8-dequant epilogues."""
+    import ctypes
+    M, K, ldo = 512, 640, N + 40
+    g = _gen(N)
+    L = native.lib()
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    # FP8 scaled, bias + GELU
+    a = (torch.randn(M, K, generator=g) * 8).to(torch.float8_e4m3fn).to(DEV)
+    w = (torch.randn(N, K, generator=g) * 8).to(torch.float8_e4m3fn).to(DEV)
+    sa, sb = torch.tensor([0.01], device=DEV), torch.tensor([0.02], device=DEV)
+    b = torch.randn(N, generator=g).to(torch.bfloat16).to(DEV)
+    ref = native.fp8_scaled_mm(a, w, sa, sb, None, b, torch.bfloat16, "gelu_tanh")
+    out = torch.full((M, ldo), float("nan"), dtype=torch.bfloat16, device=DEV)
+    assert L.b200q_fp8_scaled_mm(a.data_ptr(), K, w.data_ptr(), K, sa.data_ptr(), 1, sb.data_ptr(),
+                                 1, None, b.data_ptr(), 1, 1, out.data_ptr(), 0, ldo, M, N, K,
+                                 st) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(out[:, :N], ref)
+    assert torch.isnan(out[:, N:].float()).all()
+    # INT8 dequant (two roundings), bf16 bias
+    a8 = torch.randint(-128, 128, (M, K), generator=g, dtype=torch.int8).to(DEV)
+    w8 = torch.randint(-128, 128, (N, K), generator=g, dtype=torch.int8).to(DEV)
+    rs = (torch.rand(M, generator=g) * 0.01).to(DEV)
+    cs = (torch.rand(N, generator=g) * 0.01 + 0.001).to(DEV)
+    ref8 = native.i8_matmul_nt_fused_cs(a8, w8, rs, cs, b, torch.bfloat16)
+    out8 = torch.full((M, ldo), float("nan"), dtype=torch.bfloat16, device=DEV)
+    assert L.b200q_i8_matmul_nt_dequant(a8.data_ptr(), K, w8.data_ptr(), K, rs.data_ptr(),
+                                        cs.data_ptr(), N, b.data_ptr(), 0, out8.data_ptr(), 0,
+                                        ldo, M, N, K, st) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(out8[:, :N], ref8)
+    assert torch.isnan(out8[:, N:].float()).all()
+
+
 def test_dequant_epilogue_tensorwise_bit_exact(native):
     g = _gen(7)
     M, K, N = 256, 2560, 1024
