@@ -706,6 +706,18 @@ def run_b200q(args):
             if gemm_ms > 0 else None
         achieved_gbs = (bytes_per_launch / len(spec["layers"]) / (b2b_ms / 1e3) / 1e9
                         if b2b_ms else per_launch_event_gbs)
+    # W8A16 at M <= 256: the roofline is the slower of the weight stream at the
+    # HBM rate and the product at the dense bf16 tensor rate (at 3072 x 12288
+    # the tensor side takes over above M ~ 140).
+    small_bound, small_tflops = "hbm", None
+    if hbm_bound and n_gemm:
+        l0 = spec["layers"][0]
+        t_hbm = bytes_per_launch / len(spec["layers"]) / (peaks["hbm_gbs"] * 1e9)
+        t_ten = 2.0 * M * l0.K * l0.N / (peaks["bf16"] * 1e12)
+        if t_ten > t_hbm:
+            small_bound = "tensor"
+            t_call = (b2b_ms / 1e3) if b2b_ms else (gemm_ms / 1e3 / n_gemm)
+            small_tflops = 2.0 * M * l0.K * l0.N / t_call / 1e12
     traffic, traffic_src = _committed_traffic(args.workload) if args.m is None else (None, None)
 
     if rank == 0:
@@ -734,15 +746,25 @@ def run_b200q(args):
                                   "each op also captured as its own graph for the per-GEMM events "
                                   "(roofline), timed in a second loop"
                                   if args.launch == "graph" else "eager torch.ops calls")},
-            "roofline": ({"bound": "hbm", "achieved": round(achieved_gbs, 1) if achieved_gbs else None,
-                          "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                          "frac": round(achieved_gbs / peaks["hbm_gbs"], 4) if achieved_gbs else None,
+            "roofline": ({"bound": small_bound,
+                          "achieved": (round(small_tflops, 1) if small_bound == "tensor" else
+                                       round(achieved_gbs, 1) if achieved_gbs else None),
+                          "peak": peaks["bf16"] if small_bound == "tensor" else peaks["hbm_gbs"],
+                          "unit": "TFLOP/s" if small_bound == "tensor" else "GB/s",
+                          "frac": (round(small_tflops / peaks["bf16"], 4) if small_bound == "tensor"
+                                   else round(achieved_gbs / peaks["hbm_gbs"], 4)
+                                   if achieved_gbs else None),
+                          "frac_of_hbm": (round(achieved_gbs / peaks["hbm_gbs"], 4)
+                                          if achieved_gbs else None),
+                          "bound_rule": ("slower of the FP8 weight stream at hbm_gbs and 2*M*K*N "
+                                         "at bf16_tflops (burst)"),
                           "traffic": None, "traffic_source": None,
                           "algorithmic_bytes_per_launch": bytes_per_launch // len(spec["layers"]),
                           "kernel": ("w8a16_gemv_kernel" if M <= 16 and spec["layers"][0].K <= 4096 else
                                      "x_planes_kernel + w8a16_planes_kernel (activation planes on "
                                      "kind::f8f6f4, one call = both launches)"),
-                          "peak_source": f"hbm_gbs of {peaks['source']} MEASURED_PEAKS.json",
+                          "peak_source": (f"{'bf16_tflops (burst)' if small_bound == 'tensor' else 'hbm_gbs'}"
+                                          f" of {peaks['source']} MEASURED_PEAKS.json"),
                           "timing": ("16 calls back to back in one CUDA graph over 4 weight copies "
                                      "(151 MB > L2), events around the replay, median of 10; per call"
                                      if b2b_ms else "CUDA events around each launch"),

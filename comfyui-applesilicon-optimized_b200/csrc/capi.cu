@@ -616,7 +616,8 @@ size_t wp_workspace_any(int64_t M, int64_t K) {
 // Plan: the weight's 128-row tiles times the token tiles times S K-splits (one
 // cluster of S CTAs per (weight tile, token tile)), with the ring sized for 1 or
 // 2 CTAs per SM.  Cost model, from B200 measurements of this kernel: a CTA
-// streams its weight at ~45 GB/s with its ring full, the GPU at ~6 TB/s (a
+// streams its share at ~45 GB/s with its ring full (so 96 weight tiles stream
+// faster as 192 half-K CTAs than as 96), the GPU at ~6 TB/s (a
 // weight tile is read from HBM once; its other token tiles run next to it and
 // hit L2), the tensor cores at ~1.3e15 e4m3 MAC/s (twice the measured
 // sustained bf16 rate); every split adds a reduction
@@ -649,7 +650,7 @@ WpPlan w8a16_planes_plan(const DeviceInfo* d, int64_t M, int64_t N, int64_t K, b
   const char* fk = getenv("B200Q_W8A16_PLANES_KATOMS");
   const int forced_k = fk ? atoi(fk) : 0;
   double best_cost = 1e30;
-  for (int KA = 1; KA <= 2; ++KA) {
+  for (int KA = 2; KA >= 1; --KA) {  // two-atom stages first: they win ties (fewer hand-offs)
     if (forced_k > 0 && KA != forced_k) continue;
     const int stage = KA * (128 * kWpBK + nt * kWpBK);
     const int nkb = static_cast<int>((K + KA * kWpBK - 1) / (KA * kWpBK));  // stages along K
@@ -669,10 +670,21 @@ WpPlan w8a16_planes_plan(const DeviceInfo* d, int64_t M, int64_t N, int64_t K, b
         const int64_t ctas = tiles * ntt * S;
         const double slots = double(c) * d->num_sms * (S > 1 ? 0.9 : 1.0);
         if (double(ctas) > slots && forced_s == 0) continue;
-        const double t_cta = double((nkb + S - 1) / S) * 0.364;  // us: stage hand-offs
+        // a second CTA per SM only pays when one per SM cannot hold the grid
+        // (its ring is half as deep)
+        if (c == 2 && ctas <= d->num_sms && forced_c == 0) continue;
+        // A CTA streams its share at ~45 GB/s whatever its stage size (measured:
+        // 96 CTAs of two-atom stages moved the 37.7 MB of 3072 x 12288 in ~9.7 us),
+        // and pays ~0.36 us per stage hand-off.
+        const double t_bytes = 128.0 * double(K) / S / 45.0e3;  // us, weight bytes (planes hit L2)
+        const double t_handoff = double((nkb + S - 1) / S) * 0.364;          // us
+        const double t_cta = t_bytes > t_handoff ? t_bytes : t_handoff;
         double cost = t_cta > t_hbm ? t_cta : t_hbm;
         if (t_mma > cost) cost = t_mma;
-        cost += (S > 1 ? 0.3 : 0.0) + 0.1 * S;
+        // Rank 0 adds the other ranks' accumulators of the tile's tokens over
+        // distributed shared memory: ~0.02 us per (rank, plane, token) column.
+        const int mt = static_cast<int>(M < bt ? M : bt);
+        cost += (S > 1 ? 0.3 : 0.0) + 0.1 * S + 0.02 * (S - 1) * P * mt;
         if (env_flag("B200Q_DEBUG_PLAN", false))
           fprintf(stderr, "[b200q] planes plan M %lld N %lld K %lld: ka %d c %d S %d stages %d smem %d cost %.2f\n",
                   (long long)M, (long long)N, (long long)K, KA, c, S, stages, smem, cost);
@@ -724,6 +736,10 @@ int launch_planes_gemm(const WpPlan& p, const CUtensorMap& tw, const CUtensorMap
   return finish_launch();
 }
 
+int launch_planes_gemm_nt(const WpPlan& p, const uint8_t* w, int64_t ldw, uint8_t* planes,
+                          float* pscale, int64_t M, int64_t N, int64_t K, const EpiArgs& ep,
+                          cudaStream_t st);
+
 int launch_w8a16_planes(const WpPlan& p, const void* x, int x_dtype, int64_t ldx, const uint8_t* w,
                         int64_t ldw, int64_t M, int64_t N, int64_t K, const EpiArgs& ep,
                         void* workspace, cudaStream_t st) {
@@ -753,6 +769,12 @@ int launch_w8a16_planes(const WpPlan& p, const void* x, int x_dtype, int64_t ldx
   }
   int s = finish_launch();
   if (s != B200Q_OK) return s;
+  return launch_planes_gemm_nt(p, w, ldw, planes, pscale, M, N, K, ep, st);
+}
+
+int launch_planes_gemm_nt(const WpPlan& p, const uint8_t* w, int64_t ldw, uint8_t* planes,
+                          float* pscale, int64_t M, int64_t N, int64_t K, const EpiArgs& ep,
+                          cudaStream_t st) {
   CUtensorMap tw, tx;
   if (!make_tmap(&tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldw, kWpBK, 128,
                  CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -780,6 +802,24 @@ int launch_w8a16_planes(const WpPlan& p, const void* x, int x_dtype, int64_t ldx
     case 256: return launch_planes_gemm<256>(p, tw, tx, args, ep, st);
     default: return B200Q_ERR_INVALID;
   }
+}
+
+// Warp-per-row INT8 quant: VPL 16-byte vectors per lane, the smallest
+// instantiated count covering K / 8 vectors over 32 lanes (K <= 8192).
+template <typename T>
+int launch_quant_warp(int grid, const void* x, int64_t ldx, int8_t* q, int64_t ldq, float* scales,
+                      int64_t M, int64_t K, cudaStream_t st) {
+  const T* xp = static_cast<const T*>(x);
+  const int need = static_cast<int>((K / 8 + 31) / 32);
+  const dim3 blk(kQuantWarpRows * 32);
+  if (need <= 4) quant_rowwise_i8_warp_kernel<T, 4><<<grid, blk, 0, st>>>(xp, ldx, q, ldq, scales, int(M), int(K));
+  else if (need <= 8) quant_rowwise_i8_warp_kernel<T, 8><<<grid, blk, 0, st>>>(xp, ldx, q, ldq, scales, int(M), int(K));
+  else if (need <= 12) quant_rowwise_i8_warp_kernel<T, 12><<<grid, blk, 0, st>>>(xp, ldx, q, ldq, scales, int(M), int(K));
+  else if (need <= 16) quant_rowwise_i8_warp_kernel<T, 16><<<grid, blk, 0, st>>>(xp, ldx, q, ldq, scales, int(M), int(K));
+  else if (need <= 20) quant_rowwise_i8_warp_kernel<T, 20><<<grid, blk, 0, st>>>(xp, ldx, q, ldq, scales, int(M), int(K));
+  else if (need <= 24) quant_rowwise_i8_warp_kernel<T, 24><<<grid, blk, 0, st>>>(xp, ldx, q, ldq, scales, int(M), int(K));
+  else quant_rowwise_i8_warp_kernel<T, 32><<<grid, blk, 0, st>>>(xp, ldx, q, ldq, scales, int(M), int(K));
+  return finish_launch();
 }
 
 int grid_for(int64_t work, int per_block, const DeviceInfo* d) {
@@ -837,6 +877,12 @@ int b200q_quant_rowwise_i8(const void* x, int x_dtype, int64_t M, int64_t K, int
   const int grid = static_cast<int>(M < int64_t(d->num_sms) * 16 ? M : int64_t(d->num_sms) * 16);
   const bool vec = (K % 8 == 0) && (ldx % 8 == 0) && (ldq % 8 == 0) && aligned16(x) &&
                    (reinterpret_cast<uintptr_t>(q) % 8 == 0);
+  if (vec && K <= 8192 && env_flag("B200Q_QUANT_WARP_ROWS", true)) {
+    const int wgrid = static_cast<int>((M + kQuantWarpRows - 1) / kQuantWarpRows);
+    return x_dtype == B200Q_BF16
+               ? launch_quant_warp<__nv_bfloat16>(wgrid, x, ldx, q, ldq, scales, M, K, st)
+               : launch_quant_warp<__half>(wgrid, x, ldx, q, ldq, scales, M, K, st);
+  }
   if (x_dtype == B200Q_BF16) {
     auto* xp = static_cast<const __nv_bfloat16*>(x);
     if (vec) quant_rowwise_i8_vec_kernel<__nv_bfloat16><<<grid, kQuantThreads, 0, st>>>(xp, ldx, q, ldq, scales, int(M), int(K));

@@ -89,6 +89,25 @@ __device__ __forceinline__ float gelu_tanh(float x) {
 __device__ __forceinline__ float gelu_erf(float x) {
   return 0.5f * x * erfcf(-x * 0.7071067811865476f);
 }
+// The same tanh GELU for the W8A16 epilogues, whose outputs are checked to
+// within one bf16/fp16 ULP of the fp32 reference (not bit for bit): the
+// quotient by 1 + t (t in (0, 1], so the divisor is in (1, 2]) is taken as a
+// product with rcp.approx, which stays within a few fp32 ULP of the IEEE
+// quotient here and has no slow-path branch.  With the IEEE divide, the
+// branch kept 16 independent tokens from overlapping and the activation alone
+// took 5 us of a 128-token W8A16 epilogue on B200.
+__device__ __forceinline__ float rcp_approx_ftz(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float gelu_tanh_tol(float x) {
+  const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
+  const float k1 = 0.044715f;
+  const float u = k0 * (x + k1 * x * x * x);
+  const float t = expf(-2.0f * fabsf(u));
+  return (u >= 0.0f ? x : x * t) * rcp_approx_ftz(1.0f + t);
+}
 // SiLU of the reference's SwiGLU kernels (silu_mul_split_bf16,
 // dit_kernels.mm:724-737; i8_swiglu_rot_bf16, int8_gemm.mm:1521-1540):
 //   s = a / (1 + exp(-a)) in fp32, then rounded to bf16.
@@ -150,6 +169,12 @@ __device__ __forceinline__ float swiglu_bf16(float gate, float up) {
 
 __device__ __forceinline__ float apply_act(float v, int act) {
   if (act == kActGeluTanh) return gelu_tanh(v);
+  if (act == kActGeluErf) return gelu_erf(v);
+  return v;
+}
+// Activation of the W8A16 epilogues (tolerance-checked outputs, see gelu_tanh_tol).
+__device__ __forceinline__ float apply_act_tol(float v, int act) {
+  if (act == kActGeluTanh) return gelu_tanh_tol(v);
   if (act == kActGeluErf) return gelu_erf(v);
   return v;
 }

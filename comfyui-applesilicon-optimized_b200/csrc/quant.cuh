@@ -211,6 +211,45 @@ __global__ void __launch_bounds__(kQuantThreads)
   }
 }
 
+// Warp-per-row path for rows of up to 256 * VPL elements (vector-aligned as
+// above): each lane holds VPL 16-byte vectors of its row, so a warp has its
+// whole row in flight at once and reduces with shuffles only.  The CTA-per-row
+// kernel above keeps one or two vectors per thread in flight and serialises
+// load, block reduction and store for each row; at 4096 x 3072 bf16 it ran at
+// ~1.75 TB/s on B200.  Same scale and codes, element for element.
+constexpr int kQuantWarpRows = 8;  // rows (warps) per CTA
+template <typename T, int VPL>
+__global__ void __launch_bounds__(kQuantWarpRows * 32)
+    quant_rowwise_i8_warp_kernel(const T* __restrict__ x, int64_t ldx, int8_t* __restrict__ q,
+                                 int64_t ldq, float* __restrict__ scales, int M, int K) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kQuantWarpRows + (threadIdx.x >> 5);
+  if (row >= M) return;  // whole warps; nothing below synchronises the block
+  const int nvec = K >> 3;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(row) * ldx);
+  uint2* qr = reinterpret_cast<uint2*>(q + static_cast<int64_t>(row) * ldq);
+  uint4 v[VPL];
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int idx = lane + i * 32;
+    v[i] = idx < nvec ? __ldcs(xr + idx) : make_uint4(0u, 0u, 0u, 0u);
+  }
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) amax = fmaxf(amax, absmax8<T>(v[i]));
+  amax = warp_max(amax);
+  const float sc = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);
+  if (lane == 0) scales[row] = sc;
+  float s_math = round_to<T>(sc);
+  if (s_math == 0.0f) s_math = smallest_normal<T>();
+  const float r_math = __frcp_rn(s_math);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int idx = lane + i * 32;
+    if (idx < nvec) qr[idx] = quant8_fast<T>(v[i], s_math, r_math);
+  }
+}
+
 // Scalar path for any K / alignment.
 template <typename T>
 __global__ void __launch_bounds__(kQuantThreads)

@@ -46,6 +46,7 @@
 
 #include <type_traits>
 
+#include "quant.cuh"  // warp_max
 #include "w8a16.cuh"
 
 namespace b200q {
@@ -147,6 +148,37 @@ __device__ __forceinline__ uint16_t e4m3x2_rn(float a, float b, float& da, float
   return static_cast<uint16_t>(c);
 }
 
+// Plane p of 8 consecutive row elements v (the row scaled by 2^e_tot[0] is
+// split into planes 0..p; plane j's remainder is rescaled to plane j+1's range
+// by 2^(e_tot[j+1] - e_tot[j]), all exact), packed as 8 e4m3 codes; rmax takes
+// the largest remainder magnitude after plane p.
+template <int P>
+__device__ __forceinline__ uint2 plane_codes8(const float (&v)[8], float mult0,
+                                              const int (&e_tot)[P], int p, float& rmax) {
+  uint32_t codes[2] = {0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 8; i += 2) {
+    float r0 = v[i] * mult0, r1 = v[i + 1] * mult0;  // exact (power of two)
+    uint16_t c = 0;
+#pragma unroll
+    for (int j = 0; j < P; ++j) {
+      if (j > p) break;
+      if (j > 0) {  // rescale the remainder to plane j's range (exact)
+        const float s = exp2i(e_tot[j] - e_tot[j - 1]);
+        r0 *= s;
+        r1 *= s;
+      }
+      float d0, d1;
+      c = e4m3x2_rn(r0, r1, d0, d1);
+      r0 -= d0;  // exact: the remainder of a rounding to a coarser grid
+      r1 -= d1;
+    }
+    codes[i >> 2] |= static_cast<uint32_t>(c) << ((i & 2) * 8);
+    rmax = fmaxf(rmax, fmaxf(fabsf(r0), fabsf(r1)));
+  }
+  return make_uint2(codes[0], codes[1]);
+}
+
 __device__ __forceinline__ float block_max(float v, float* red) {
 #pragma unroll
   for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -199,7 +231,7 @@ __global__ void __launch_bounds__(kWpPlaneThreads)
   }
   const bool all_finite = __syncthreads_and(finite) != 0;
   amax = block_max(amax, red);
-  int e_tot[P];  // plane p holds x's remainder scaled by 2^e_tot[p]
+  int e_tot[P] = {};  // plane p holds x's remainder scaled by 2^e_tot[p]
   e_tot[0] = plane_exponent(amax, 0);
   int used = e_tot[0];
   const float mult0 = exp2i(e_tot[0]);
@@ -210,30 +242,9 @@ __global__ void __launch_bounds__(kWpPlaneThreads)
   for (int p = 0; p < P; ++p) {
     float rmax = 0.0f;
     for (int i = threadIdx.x; i < nv; i += kWpPlaneThreads) {
-      const int k = i * 8;
       float v[8];
       unpack8f<XT>(srow[i], v);
-      uint32_t codes[2] = {0u, 0u};
-#pragma unroll
-      for (int i = 0; i < 8; i += 2) {
-        float r0 = v[i] * mult0, r1 = v[i + 1] * mult0;  // exact (power of two)
-        uint16_t c = 0;
-#pragma unroll
-        for (int j = 0; j <= p; ++j) {
-          if (j > 0) {  // rescale the remainder to plane j's range (exact)
-            const float s = exp2i(e_tot[j] - e_tot[j - 1]);
-            r0 *= s;
-            r1 *= s;
-          }
-          float d0, d1;
-          c = e4m3x2_rn(r0, r1, d0, d1);
-          r0 -= d0;  // exact: the remainder of a rounding to a coarser grid
-          r1 -= d1;
-        }
-        codes[i >> 2] |= static_cast<uint32_t>(c) << ((i & 2) * 8);
-        rmax = fmaxf(rmax, fmaxf(fabsf(r0), fabsf(r1)));
-      }
-      *reinterpret_cast<uint2*>(out0 + p * plane_stride + k) = make_uint2(codes[0], codes[1]);
+      *reinterpret_cast<uint2*>(out0 + p * plane_stride + i * 8) = plane_codes8<P>(v, mult0, e_tot, p, rmax);
     }
     if (p + 1 < P) {
       rmax = block_max(rmax, red);
@@ -287,7 +298,8 @@ __device__ __forceinline__ void wp_epilogue(const WpArgs& a, const EpiArgs& ep, 
       for (int p = 0; p < P; ++p)
 #pragma unroll
         for (int j = 0; j < 16; ++j)
-          acc[p][j] = __fadd_rn(acc[p][j], ld_dsmem_f32(peer + ((p * BT + t0 + j) * 128 + r) * 4));
+          if (t0 + j < mt)  // peers dumped only the tile's tokens
+            acc[p][j] = __fadd_rn(acc[p][j], ld_dsmem_f32(peer + ((p * BT + t0 + j) * 128 + r) * 4));
     }
     // Tokens t0 .. t0+15 < bt always index valid (if unused) plane columns and
     // scales; only the stores are limited to tokens < M.
@@ -298,7 +310,7 @@ __device__ __forceinline__ void wp_epilogue(const WpArgs& a, const EpiArgs& ep, 
 #pragma unroll
       for (int p = 1; p < P; ++p) v = __fadd_rn(v, __fmul_rn(acc[p][j], s_pscale[p * BT + t0 + j]));
       v = __fadd_rn(__fmul_rn(v, xs), bias_v);
-      out_v[j] = apply_act(v, ACT);
+      out_v[j] = apply_act_tol(v, ACT);
     }
     // Direct typed stores (32 lanes = 32 consecutive output features of one
     // token row); measured 2x faster here than the generic per-element store.
@@ -468,9 +480,13 @@ __global__ void __maxnreg__(120)
   const bool valid = mbar_wait_warp(acc_full, 0u, abort_flag);
   tc_fence_after();
   if (split > 0 && valid) {
-    // Ranks 1..S-1: accumulators -> own shared memory, [column][row].
+    // Ranks 1..S-1: accumulators -> own shared memory, [column][row]; only the
+    // 16-column groups holding tokens of this tile (rank 0 reads nothing else).
+    constexpr int BT = NT / L::kPlanes;
+    const int mt = a.M - tt * BT < BT ? a.M - tt * BT : BT;
 #pragma unroll 1
     for (int c = 16 * half; c < NT; c += 32) {
+      if (c % BT >= mt) continue;
       uint32_t v[16];
       tmem_ld_cols<16>(taddr + c, v);
       tmem_ld_wait();

@@ -95,6 +95,15 @@ def test_scaled_mm_row_major_other(scaled_mm_installed):
     assert torch.equal(out, out_cm)
     ref = oracle.scaled_mm_fp8(a, b, sa.reshape(1), sb.reshape(1), None, None, None)
     assert oracle.elementwise_ulp_ratio(out, ref) <= 1.0
+    # the K-major copy is made once per weight: a second call reuses it, an
+    # in-place update of the weight makes a fresh one
+    from b200q._patches import scaled_mm_fp8 as seam
+    copy1 = seam._k_major_weight(other_rm)
+    again = torch._scaled_mm(a.to(DEV), other_rm, scale_a=sa.to(DEV), scale_b=sb.to(DEV),
+                             out_dtype=torch.bfloat16)
+    assert torch.equal(again, out) and seam._k_major_weight(other_rm) is copy1
+    other_rm.view(torch.uint8).add_(0)  # bumps the (shared) version counter
+    assert seam._k_major_weight(other_rm) is not copy1
 
 
 def test_scaled_mm_passes_through_what_it_does_not_own(scaled_mm_installed):
