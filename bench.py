@@ -147,6 +147,7 @@ class B200Block:
     def __init__(self, spec, M, dev, rank, fused=False, start=0):
         self.spec, self.M, self.dev = spec, M, dev
         self.fused = fused  # activation quant inside the GEMM launch (8-bit routes)
+        self.amax_epilogue = True  # FP8: amax of a chained layer's input from the GEMM before it
         self.weights = []
         self.inputs = {}
         self.gemm_events = []
@@ -201,7 +202,7 @@ class B200Block:
         ops = torch.ops.b200q
         spec = self.spec
         outs = []
-        h = None
+        h = amax = None
         if spec["route"] == "mlp":
             return self._mlp_step(inputs, record)
         for i, (l, (w, s, b)) in enumerate(zip(spec["layers"], self.weights)):
@@ -211,10 +212,15 @@ class B200Block:
                 y = ops.fp8_linear(x, w, s, b, torch.bfloat16, l.act or "none")
                 self._ev_end(ev, record, l)
             elif spec["route"] == "fp8":
-                xq, xs = ops.fp8_quant_tensorwise(x)
+                xq, xs = (ops.fp8_quant_from_amax(x, amax) if amax is not None
+                          else ops.fp8_quant_tensorwise(x))
                 ev = self._ev(record)
-                y = ops.fp8_scaled_mm(xq, w, xs.reshape(1), s, None, b, torch.bfloat16,
-                                      l.act or "none")
+                if self._feeds_next(i):  # the epilogue takes the next quant's amax
+                    y, amax = ops.fp8_scaled_mm_amax(xq, w, xs.reshape(1), s, None, b,
+                                                     torch.bfloat16, l.act or "none")
+                else:
+                    y, amax = ops.fp8_scaled_mm(xq, w, xs.reshape(1), s, None, b, torch.bfloat16,
+                                                l.act or "none"), None
                 self._ev_end(ev, record, l)
             elif spec["route"] == "int8" and self.fused:
                 ev = self._ev(record)
@@ -249,6 +255,14 @@ class B200Block:
         self._ev_end(ev, record, l2)
         return [y]
 
+    def _feeds_next(self, i):
+        """Separate-quant FP8 route: layer i's output is the next layer's input, so
+        its GEMM epilogue also takes that input's amax (the quant skips its amax
+        pass; same codes)."""
+        spec = self.spec
+        return (spec["route"] == "fp8" and not self.fused and self.amax_epilogue
+                and i + 1 < len(spec["layers"]) and i + 1 >= len(spec["inputs"]))
+
     def build_graphs(self, inputs):
         """Captures every op of one step as its own CUDA graph over static buffers.
         Returns [(graph, gemm_flops)] in execution order (flops 0 for quant ops) and
@@ -258,6 +272,7 @@ class B200Block:
         spec = self.spec
         pool = torch.cuda.graph_pool_handle()
         seq, h, self.graph_outs = [], None, []
+        amax = None
         n0 = _native.launch_count()
 
         def capture(fn):
@@ -288,10 +303,18 @@ class B200Block:
             elif spec["route"] == "int8" and self.fused:
                 g, y = capture(lambda: ops.i8_linear(x, w, s, b, torch.bfloat16, act))
             elif spec["route"] == "fp8":
-                g, (xq, xs) = capture(lambda: ops.fp8_quant_tensorwise(x))
+                if amax is not None:
+                    g, (xq, xs) = capture(lambda: ops.fp8_quant_from_amax(x, amax))
+                else:
+                    g, (xq, xs) = capture(lambda: ops.fp8_quant_tensorwise(x))
                 seq.append((g, 0.0))
-                g, y = capture(lambda: ops.fp8_scaled_mm(xq, w, xs.reshape(1), s, None, b,
-                                                         torch.bfloat16, act))
+                if self._feeds_next(i):
+                    g, (y, amax) = capture(lambda: ops.fp8_scaled_mm_amax(
+                        xq, w, xs.reshape(1), s, None, b, torch.bfloat16, act))
+                else:
+                    g, y = capture(lambda: ops.fp8_scaled_mm(xq, w, xs.reshape(1), s, None, b,
+                                                             torch.bfloat16, act))
+                    amax = None
             elif spec["route"] == "int8":
                 g, (xq, xs) = capture(lambda: ops.quant_rowwise_i8(x))
                 seq.append((g, 0.0))
@@ -639,6 +662,7 @@ def run_b200q(args):
     spec = _workload_spec(args.workload, args.m)
     start, M = _split_rows(spec["M"], world, rank)
     blk = B200Block(spec, M, dev, rank, fused=args.prologue == "fused", start=start)
+    blk.amax_epilogue = args.amax_epilogue
     flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
 
     def barrier():
@@ -777,7 +801,10 @@ def run_b200q(args):
                            "convrot + per-token quant launch" if spec["route"] == "mlp" else
                            {"fused": "inside each GEMM launch (quant prologue; fp8: "
                                      "+1 amax-reduction launch per linear)",
-                            "separate": "own launch(es) before each GEMM"}[args.prologue]
+                            "separate": ("own launch(es) before each GEMM" + (
+                                "; fp8: a layer fed by the previous layer's output takes that "
+                                "output's amax from the previous GEMM's epilogue"
+                                if args.amax_epilogue else ""))}[args.prologue]
                            if spec["route"] != "w8a16" else "none (weight-only)"),
                        "launch": ("the step captured once as one CUDA graph, replayed per step (value); "
                                   "each op also captured as its own graph for the per-GEMM events "
@@ -1215,6 +1242,9 @@ def main():
                     help="multi-GPU layout: token rows (default, no communication) or the "
                          "column-parallel N-split with the all-gather fused into each GEMM "
                          "(config 5 only)")
+    ap.add_argument("--no-amax-epilogue", dest="amax_epilogue", action="store_false",
+                    help="fp8 separate-quant route: take every layer input's amax with its own "
+                         "pass, also where the previous GEMM's epilogue could provide it")
     ap.add_argument("--impl", default="b200q", choices=["b200q", "reference"])
     ap.add_argument("--cpu-rows", type=int, default=None,
                     help="token rows of the CPU sample (default: sized to --cpu-step-s)")

@@ -86,6 +86,9 @@ _SIGNATURES = {
     "b200q_ipc_export": ([_vp, _vp, ctypes.POINTER(ctypes.c_uint64)], _int),
     "b200q_ipc_import": ([_vp, ctypes.c_uint64, ctypes.POINTER(_vp), ctypes.POINTER(_vp)], _int),
     "b200q_ipc_close": ([_vp], _int),
+    "b200q_fp8_scaled_mm_amax": ([_vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _vp, _int, _int,
+                                  _vp, _int, _i64, _i64, _i64, _i64, _vp, _vp], _int),
+    "b200q_fp8_quant_from_amax": ([_vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _vp], _int),
     "b200q_fp8_quant_tensorwise": ([_vp, _int, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp], _int),
     "b200q_prologue_sync_bytes": ([_i64], _sz),
     "b200q_i8_linear_fused": ([_vp, _int, _i64, _vp, _i64, _vp, _i64, _vp, _int, _vp, _int, _i64,
@@ -514,6 +517,21 @@ def fp8_quant_tensorwise(x):
     return q, scale
 
 
+def fp8_quant_from_amax(x, amax):
+    """fp8_quant_tensorwise(x) given x's amax (float bits in an int32 [1] tensor,
+    e.g. from fp8_scaled_mm_amax): the same codes and scale, no amax pass."""
+    _require_cuda(x, amax)
+    x = _rows_2d(x.reshape(-1, x.shape[-1]) if x.dim() != 2 else x, "x")
+    if x.dtype not in (torch.bfloat16, torch.float16):
+        raise RuntimeError(f"{TAG} fp8_quant_from_amax expects bf16/f16, got {x.dtype}")
+    M, K = x.shape
+    q = torch.empty((M, K), dtype=torch.float8_e4m3fn, device=x.device)
+    scale = torch.empty((), dtype=torch.float32, device=x.device)
+    _check(lib().b200q_fp8_quant_from_amax(_p(x), _DT[x.dtype], M, K, x.stride(0), _p(amax), _p(q),
+                                           K, _p(scale), _stream(x)))
+    return q, scale
+
+
 def _scale_arg(s, n_ok):
     if s is None:
         return None, 0
@@ -608,6 +626,34 @@ def ipc_import(handle, offset):
 
 def ipc_close(base):
     _check(lib().b200q_ipc_close(ctypes.c_void_p(int(base))))
+
+
+def fp8_scaled_mm_amax(a, w, scale_a=None, scale_b=None, scale_result=None, bias=None,
+                       out_dtype=torch.bfloat16, act=None):
+    """fp8_scaled_mm (bf16/f16 out) plus max |out| as float bits in an int32 [1]
+    tensor, taken in the GEMM epilogue on the CTA-pair route."""
+    _require_cuda(a, w, scale_a, scale_b, scale_result, bias)
+    a, w = _rows_2d(a, "a"), _rows_2d(w, "w")
+    M, K = a.shape
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise RuntimeError(f"{TAG} K mismatch")
+    sa, na = _scale_arg(scale_a, (1, M))
+    sb, nb = _scale_arg(scale_b, (1, N))
+    sr, _ = _scale_arg(scale_result, (1,))
+    code = _out_dtype_code(out_dtype or torch.bfloat16, (torch.bfloat16, torch.float16))
+    bdt = BIAS_NONE
+    if bias is not None:
+        bias = bias.contiguous()
+        if bias.dtype not in _BIAS_DT:
+            bias = bias.float()
+        bdt = _BIAS_DT[bias.dtype]
+    out = torch.empty((M, N), dtype=out_dtype or torch.bfloat16, device=a.device)
+    amax = torch.empty((1,), dtype=torch.int32, device=a.device)
+    _check(lib().b200q_fp8_scaled_mm_amax(_p(a), a.stride(0), _p(w), w.stride(0), _p(sa), na,
+                                          _p(sb), nb, _p(sr), _p(bias), bdt, ACTS[act], _p(out),
+                                          code, N, M, N, K, _p(amax), _stream(a)))
+    return out, amax
 
 
 def fp8_linear(x, w, w_scale=None, bias=None, out_dtype=torch.bfloat16, act=None,
@@ -724,6 +770,10 @@ def _register_ops():
     L.define("i8_linear(Tensor x, Tensor w, Tensor w_scale, Tensor? bias=None, "
              "ScalarType out_dtype=15, str act='none') -> Tensor")
     L.define("fp8_quant_tensorwise(Tensor x) -> (Tensor, Tensor)")
+    L.define("fp8_quant_from_amax(Tensor x, Tensor amax) -> (Tensor, Tensor)")
+    L.define("fp8_scaled_mm_amax(Tensor a, Tensor w, Tensor? scale_a=None, Tensor? scale_b=None, "
+             "Tensor? scale_result=None, Tensor? bias=None, ScalarType out_dtype=15, "
+             "str act='none') -> (Tensor, Tensor)")
     L.define("fp8_linear(Tensor x, Tensor w, Tensor? w_scale=None, Tensor? bias=None, "
              "ScalarType out_dtype=15, str act='none', Tensor? scale_result=None) -> Tensor")
     L.define("fp8_scaled_mm(Tensor a, Tensor w, Tensor? scale_a=None, Tensor? scale_b=None, "
@@ -752,6 +802,9 @@ def _register_ops():
         "rms_rope_partial_": rms_rope_partial_,
         "i8_matmul_nt_fused_cs_qkv_rms_rope": i8_matmul_nt_fused_cs_qkv_rms_rope,
         "fp8_quant_tensorwise": fp8_quant_tensorwise,
+        "fp8_quant_from_amax": fp8_quant_from_amax,
+        "fp8_scaled_mm_amax": lambda a, w, sa=None, sb=None, sr=None, b=None, od=torch.bfloat16,
+        act="none": fp8_scaled_mm_amax(a, w, sa, sb, sr, b, od, act),
         "fp8_linear": fp8_linear,
         "fp8_scaled_mm": lambda a, w, sa=None, sb=None, sr=None, b=None, od=torch.bfloat16,
         act="none": fp8_scaled_mm(a, w, sa, sb, sr, b, od, act),
@@ -795,6 +848,12 @@ def _register_ops():
                                            x.new_empty((), dtype=torch.float32)),
         "fp8_scaled_mm": lambda a, w, sa=None, sb=None, sr=None, b=None, od=torch.bfloat16,
         act="none": a.new_empty((a.shape[0], w.shape[0]), dtype=od),
+        "fp8_scaled_mm_amax": lambda a, w, sa=None, sb=None, sr=None, b=None, od=torch.bfloat16,
+        act="none": (a.new_empty((a.shape[0], w.shape[0]), dtype=od),
+                     a.new_empty((1,), dtype=torch.int32)),
+        "fp8_quant_from_amax": lambda x, amax: (
+            x.new_empty((x.numel() // x.shape[-1], x.shape[-1]), dtype=torch.float8_e4m3fn),
+            x.new_empty((), dtype=torch.float32)),
         "fp8_linear": lambda x, w, ws=None, b=None, od=torch.bfloat16, act="none", sr=None:
         x.new_empty((*x.shape[:-1], w.shape[0]), dtype=od),
         "w8a16_linear": lambda x, w, ws=None, b=None, act="none", od=None: x.new_empty(

@@ -1261,6 +1261,76 @@ int b200q_fp8_scaled_mm(const uint8_t* a, int64_t lda, const uint8_t* w, int64_t
   return gemm8<MmaKind::F8F6F4, kEpiScaled>(a, lda, w, ldw, M, N, K, ep, static_cast<cudaStream_t>(stream));
 }
 
+// b200q_fp8_scaled_mm that also leaves max |out| (of the rounded outputs) in
+// *amax_bits as float bits: on the CTA-pair route the epilogue folds it in while
+// storing; other routes take it with the absmax pass over the output.
+int b200q_fp8_scaled_mm_amax(const uint8_t* a, int64_t lda, const uint8_t* w, int64_t ldw,
+                             const float* scale_a, int64_t scale_a_numel, const float* scale_b,
+                             int64_t scale_b_numel, const float* scale_result, const void* bias,
+                             int bias_dtype, int act, void* out, int out_dtype, int64_t ldo,
+                             int64_t M, int64_t N, int64_t K, unsigned int* amax_bits,
+                             void* stream) {
+  if (!amax_bits || (out_dtype != B200Q_BF16 && out_dtype != B200Q_F16) || !a || !w || !out ||
+      !valid_dims(M, N, K) || K == 0 || lda < K || ldw < K || ldo < N ||
+      (scale_a && scale_a_numel != 1 && scale_a_numel != M) ||
+      (scale_b && scale_b_numel != 1 && scale_b_numel != N) ||
+      bias_dtype < B200Q_BIAS_NONE || bias_dtype > B200Q_BIAS_F32 ||
+      (bias_dtype != B200Q_BIAS_NONE && !bias) || act < B200Q_ACT_NONE || act > B200Q_ACT_GELU_ERF)
+    return B200Q_ERR_INVALID;
+  const DeviceInfo* d = current_device();
+  if (!d) return B200Q_ERR_UNSUPPORTED;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(amax_bits, 0, sizeof(unsigned int), st) != cudaSuccess) return B200Q_ERR_CUDA;
+  if (M == 0 || N == 0) return B200Q_OK;
+  EpiArgs ep = make_epi(out, ldo, out_dtype, M, N);
+  ep.row_scale = scale_a;
+  ep.row_scale_vec = scale_a && scale_a_numel == M && M != 1 ? 1 : 0;
+  ep.col_scale = scale_b;
+  ep.col_scale_vec = scale_b && scale_b_numel == N && N != 1 ? 1 : 0;
+  ep.extra_scale = scale_result;
+  ep.bias = bias;
+  ep.bias_dtype = bias ? bias_dtype : kBiasNone;
+  ep.act = act;
+  const bool pair = gemm8_tc_eligible(a, lda, w, ldw, K) && N > 128 && M >= 256 &&
+                    pair_kernels_enabled();
+  if (pair) {
+    ep.amax_out = amax_bits;
+    return launch_pair<MmaKind::F8F6F4, kEpiScaled, kProNone>(d, a, lda, w, ldw, int(M), int(N),
+                                                              int(K), ep, Prologue{}, st);
+  }
+  const int s = gemm8<MmaKind::F8F6F4, kEpiScaled>(a, lda, w, ldw, M, N, K, ep, st);
+  if (s != B200Q_OK) return s;
+  const int grid = grid_for(M * N / 8 + 1, 256, d);
+  if (out_dtype == B200Q_BF16)
+    absmax_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(out), ldo,
+                                                       M, int(N), amax_bits);
+  else
+    absmax_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(out), ldo, M, int(N),
+                                                amax_bits);
+  return finish_launch();
+}
+
+// Per-tensor e4m3 quant of x with an amax already taken (the second half of
+// b200q_fp8_quant_tensorwise).
+int b200q_fp8_quant_from_amax(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
+                              const unsigned int* amax_bits, uint8_t* q, int64_t ldq,
+                              float* scale, void* stream) {
+  if (!x || !q || !scale || !amax_bits || M < 0 || K <= 0 || ldx < K || ldq < K ||
+      (x_dtype != B200Q_BF16 && x_dtype != B200Q_F16))
+    return B200Q_ERR_INVALID;
+  const DeviceInfo* d = current_device();
+  if (!d) return B200Q_ERR_UNSUPPORTED;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int grid = grid_for(M * K / 8 + 1, 256, d);
+  if (x_dtype == B200Q_BF16)
+    fp8_quantize_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(x), ldx, M, int(K), amax_bits, q, ldq, scale);
+  else
+    fp8_quantize_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(x), ldx, M,
+                                                      int(K), amax_bits, q, ldq, scale);
+  return finish_launch();
+}
+
 // Column-parallel FP8 GEMM with the all-gather in its epilogue.  This rank owns
 // output columns [c0, c0 + N) of an [M, N_total] output held in full by every
 // rank; `out` and peer_outs[i] point at column c0 of this rank's and of the

@@ -719,6 +719,19 @@ struct PeerOuts {
   int n;
 };
 
+// max |v[j]| over the chunk's first `valid` columns into m (one FMNMX per
+// element on whole chunks; the ragged last chunk of a row masks its tail).
+__device__ __forceinline__ void chunk_amax(const float (&v)[32], int valid, float& m) {
+  if (valid >= 32) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) m = fmaxf(m, fabsf(v[j]));
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < valid) m = fmaxf(m, fabsf(v[j]));
+  }
+}
+
 template <int STAGES, int KATOMS = 1, int BN = 256>
 struct Gemm8PairLayout {
   static constexpr int kAtom = 128 * kGemmBK;            // one 128-row x 128-byte box (A)
@@ -925,6 +938,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     constexpr bool kAccInt = KIND == MmaKind::I8;
     constexpr int kChunks = BN / 64;
     constexpr bool kStoreEpi = (EPI == kEpiI8Dequant || EPI == kEpiScaled) && PRO == kProNone;
+    float amax_acc = 0.0f;  // max |out| of this thread's stored outputs (ep.amax_out)
     int it = 0;
     for (int tile = pair; tile < num_tiles; tile += num_pairs, ++it) {
       int mb, nb;
@@ -990,6 +1004,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tmem_ld32(taddr + c * 32, r);
             tmem_ld_wait();
             epilogue_math<EPI, kAccInt>(r, cs, bi, has_bias, rs, xs, ep, v);
+            if (ep.amax_out && row_ok) chunk_amax(v, N - (nb * BN + c * 32), amax_acc);
             uint32_t pk[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j)
@@ -1039,6 +1054,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (row_ok && n0 < N) {
               epilogue_math<EPI, kAccInt>(r, cs, bi, has_bias, rs, xs, ep, v);
               store_chunk(ep, m, n0, v, N);
+              if (ep.amax_out) chunk_amax(v, N - n0, amax_acc);
             }
           }
         }
@@ -1046,6 +1062,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acce_leader + buf * 8);
+    }
+    if (ep.amax_out) {
+      // the stored values are the outputs rounded to their type, and rounding
+      // is monotonic: max |rounded| = rounded max |v|
+      const float rm = ep.out_dtype == kOutF16 ? round_f16(amax_acc)
+                       : ep.out_dtype == kOutBF16 ? round_bf16(amax_acc) : amax_acc;
+      const unsigned int bits = __reduce_max_sync(0xffffffffu, __float_as_uint(rm));
+      if (lane == 0 && bits != 0u) atomicMax(ep.amax_out, bits);
     }
     if constexpr (kStoreEpi) {
       if (ep.tma_store && lane == 0) {

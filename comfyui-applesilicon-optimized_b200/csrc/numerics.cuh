@@ -220,6 +220,10 @@ struct EpiArgs {
   // Pair kernel: the epilogue warps sleep this long between probes of the
   // accumulator barrier (0 = spin on try_wait).
   unsigned int wait_sleep_ns;
+  // Pair kernel, scaled / dequant epilogues: when set, max |out| over the
+  // stored (rounded) outputs is folded into this word with atomicMax on the
+  // float bits, so that a per-tensor quant of the output needs no amax pass.
+  unsigned int* amax_out;
 };
 
 // Element pointer of output (m, n) for 16-bit outputs, in either layout.

@@ -125,6 +125,27 @@ B200Q_API int b200q_fp8_scaled_mm(const uint8_t* a, int64_t lda, const uint8_t* 
                         int bias_dtype, int act, void* out, int out_dtype, int64_t ldo,
                         int64_t M, int64_t N, int64_t K, void* stream);
 
+/* b200q_fp8_scaled_mm (bf16/f16 output) that also writes max |out| over the
+ * stored outputs to *amax_bits (float bits, overwritten), so that the next
+ * layer's per-tensor FP8 quant of this output (b200q_fp8_quant_from_amax) skips
+ * its amax pass: on the CTA-pair route the epilogue takes the max while
+ * storing.  No reference counterpart (the reference quantizes FP8 activations
+ * upstream of torch._scaled_mm, _patches/scaled_mm_fp8.py:149). */
+B200Q_API int b200q_fp8_scaled_mm_amax(const uint8_t* a, int64_t lda, const uint8_t* w,
+                                       int64_t ldw, const float* scale_a, int64_t scale_a_numel,
+                                       const float* scale_b, int64_t scale_b_numel,
+                                       const float* scale_result, const void* bias,
+                                       int bias_dtype, int act, void* out, int out_dtype,
+                                       int64_t ldo, int64_t M, int64_t N, int64_t K,
+                                       unsigned int* amax_bits, void* stream);
+
+/* Per-tensor e4m3 quant of x given its amax (float bits, e.g. from
+ * b200q_fp8_scaled_mm_amax): the same scale and codes as
+ * b200q_fp8_quant_tensorwise without its amax pass. */
+B200Q_API int b200q_fp8_quant_from_amax(const void* x, int x_dtype, int64_t M, int64_t K,
+                                        int64_t ldx, const unsigned int* amax_bits, uint8_t* q,
+                                        int64_t ldq, float* scale, void* stream);
+
 /* Column-parallel (N-split) b200q_fp8_scaled_mm with its all-gather fused in:
  * this rank holds the weight rows of output columns [c0, c0 + N) and computes
  * them for all M tokens; `out` and each of the n_peer_outs (<= 7) peer_outs[i]

@@ -156,6 +156,33 @@ def test_ragged_width_outputs_stay_in_their_columns(native, N):
     assert torch.isnan(out8[:, N:].float()).all()
 
 
+@pytest.mark.parametrize("M,K,N,act", [(512, 640, 1024, "gelu_tanh"), (512, 640, 600, None),
+                                      (300, 1024, 3072, "gelu_tanh"), (100, 512, 384, None),
+                                      (2048, 3072, 12288, "gelu_tanh")])
+def test_fp8_scaled_mm_amax_and_quant_from_amax(native, M, K, N, act):
+    """fp8_scaled_mm_amax gives fp8_scaled_mm's output bit for bit plus the max
+    |out| of that bf16 output (taken in the CTA-pair epilogue for M >= 256 and
+    N > 128, by the absmax pass otherwise, with both store paths of the
+    epilogue: 16-byte row widths and ragged N = 600); fp8_quant_from_amax with it
+    gives fp8_quant_tensorwise's codes and scale bit for bit."""
+    g = _gen(M + N)
+    a = (torch.randn(M, K, generator=g) * 8).to(torch.float8_e4m3fn).to(DEV)
+    w = (torch.randn(N, K, generator=g) * 8).to(torch.float8_e4m3fn).to(DEV)
+    sa, sb = torch.tensor([0.01], device=DEV), torch.tensor([0.02], device=DEV)
+    b = torch.randn(N, generator=g).to(torch.bfloat16).to(DEV)
+    ref = native.fp8_scaled_mm(a, w, sa, sb, None, b, torch.bfloat16, act)
+    for _ in range(2):  # the amax word is rewritten on every call
+        out, amax = native.fp8_scaled_mm_amax(a, w, sa, sb, None, b, torch.bfloat16, act)
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
+        want = ref.float().abs().max().reshape(1).view(torch.int32)
+        assert torch.equal(amax, want)
+    q, s = native.fp8_quant_from_amax(out, amax)
+    q_ref, s_ref = native.fp8_quant_tensorwise(out)
+    assert torch.equal(q.view(torch.uint8), q_ref.view(torch.uint8)) and torch.equal(s, s_ref)
+    assert native.device_status() == 0
+
+
 def test_dequant_epilogue_tensorwise_bit_exact(native):
     g = _gen(7)
     M, K, N = 256, 2560, 1024
