@@ -152,6 +152,13 @@ int launch_gemm8_tc(const DeviceInfo* d, const void* a, int64_t lda, const void*
   return finish_launch();
 }
 
+// Programmatic dependent launch for the CTA-pair GEMM and the warp-per-row
+// quant (read per call; B200Q_PDL=0 launches them plainly).
+bool pdl_launch_on() {
+  const char* e = getenv("B200Q_PDL");
+  return !(e && e[0] == '0');
+}
+
 // CTA-pair kernel: clusters of 2, grid = 2 x min(tiles, SMs / 2).
 // B200Q_TMA_STORE=0 keeps the per-thread global stores in the pair kernel's
 // epilogue (A/B runs).
@@ -218,13 +225,17 @@ int launch_gemm8_tc2(const DeviceInfo* d, const void* a, int64_t lda, const void
   cfg.blockDim = dim3(kGemmThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // the set-up (barriers, TMEM, descriptor prefetch) overlaps the previous
+  // kernel's tail; the kernel waits for it before touching memory
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_launch_on() ? 2 : 1;
   const cudaError_t le =
       cudaLaunchKernelEx(&cfg, kern, ta, tb, to, po, M, N, K, raster_group_m(lda, ldw, M, N, K), ep, pro);
   if (le != cudaSuccess) {
@@ -811,14 +822,23 @@ int launch_quant_warp(int grid, const void* x, int64_t ldx, int8_t* q, int64_t l
                       int64_t M, int64_t K, cudaStream_t st) {
   const T* xp = static_cast<const T*>(x);
   const int need = static_cast<int>((K / 8 + 31) / 32);
-  const dim3 blk(kQuantWarpRows * 32);
-  if (need <= 4) quant_rowwise_i8_warp_kernel<T, 4><<<grid, blk, 0, st>>>(xp, ldx, q, ldq, scales, int(M), int(K));
-  else if (need <= 8) quant_rowwise_i8_warp_kernel<T, 8><<<grid, blk, 0, st>>>(xp, ldx, q, ldq, scales, int(M), int(K));
-  else if (need <= 12) quant_rowwise_i8_warp_kernel<T, 12><<<grid, blk, 0, st>>>(xp, ldx, q, ldq, scales, int(M), int(K));
-  else if (need <= 16) quant_rowwise_i8_warp_kernel<T, 16><<<grid, blk, 0, st>>>(xp, ldx, q, ldq, scales, int(M), int(K));
-  else if (need <= 20) quant_rowwise_i8_warp_kernel<T, 20><<<grid, blk, 0, st>>>(xp, ldx, q, ldq, scales, int(M), int(K));
-  else if (need <= 24) quant_rowwise_i8_warp_kernel<T, 24><<<grid, blk, 0, st>>>(xp, ldx, q, ldq, scales, int(M), int(K));
-  else quant_rowwise_i8_warp_kernel<T, 32><<<grid, blk, 0, st>>>(xp, ldx, q, ldq, scales, int(M), int(K));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(kQuantWarpRows * 32);
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_launch_on() ? 1 : 0;
+  const int Mi = int(M), Ki = int(K);
+  if (need <= 4) cudaLaunchKernelEx(&cfg, quant_rowwise_i8_warp_kernel<T, 4>, xp, ldx, q, ldq, scales, Mi, Ki);
+  else if (need <= 8) cudaLaunchKernelEx(&cfg, quant_rowwise_i8_warp_kernel<T, 8>, xp, ldx, q, ldq, scales, Mi, Ki);
+  else if (need <= 12) cudaLaunchKernelEx(&cfg, quant_rowwise_i8_warp_kernel<T, 12>, xp, ldx, q, ldq, scales, Mi, Ki);
+  else if (need <= 16) cudaLaunchKernelEx(&cfg, quant_rowwise_i8_warp_kernel<T, 16>, xp, ldx, q, ldq, scales, Mi, Ki);
+  else if (need <= 20) cudaLaunchKernelEx(&cfg, quant_rowwise_i8_warp_kernel<T, 20>, xp, ldx, q, ldq, scales, Mi, Ki);
+  else if (need <= 24) cudaLaunchKernelEx(&cfg, quant_rowwise_i8_warp_kernel<T, 24>, xp, ldx, q, ldq, scales, Mi, Ki);
+  else cudaLaunchKernelEx(&cfg, quant_rowwise_i8_warp_kernel<T, 32>, xp, ldx, q, ldq, scales, Mi, Ki);
   return finish_launch();
 }
 

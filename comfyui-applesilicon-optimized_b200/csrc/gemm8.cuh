@@ -829,6 +829,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Launched as a programmatic dependent of the kernel before it (the set-up
+  // above overlaps that kernel's tail): no global memory is touched before it
+  // has finished.
+  griddep_wait();
   float pro_s = 1.0f;  // per-tensor activation scale of the fp8 prologue
   if constexpr (PRO == kProFp8Tensor) {
     pro_s = pro_fp8_scale(pro);

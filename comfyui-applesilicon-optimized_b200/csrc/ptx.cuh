@@ -309,6 +309,18 @@ __device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* map, uint32_
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(x), "r"(y)
       : "memory");
 }
+// Programmatic dependent launch: a grid launched with the programmatic
+// stream-serialisation attribute may start before the kernel ahead of it on the
+// stream has finished; griddepcontrol.wait blocks the calling thread until that
+// kernel is complete and its memory visible (a no-op without the attribute), and
+// launch_dependents lets the next such grid start once every CTA of this one
+// has issued it.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                    smem_u32(dst_smem)),

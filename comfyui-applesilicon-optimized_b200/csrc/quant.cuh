@@ -222,6 +222,11 @@ template <typename T, int VPL>
 __global__ void __launch_bounds__(kQuantWarpRows * 32)
     quant_rowwise_i8_warp_kernel(const T* __restrict__ x, int64_t ldx, int8_t* __restrict__ q,
                                  int64_t ldq, float* __restrict__ scales, int M, int K) {
+  // Launched as a programmatic dependent: wait for the kernel before it, then
+  // let the next one (the GEMM reading these codes, which waits in turn) start
+  // its set-up while the last rows are quantized.
+  griddep_wait();
+  griddep_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * kQuantWarpRows + (threadIdx.x >> 5);
   if (row >= M) return;  // whole warps; nothing below synchronises the block
