@@ -159,6 +159,22 @@ bool pdl_launch_on() {
   return !(e && e[0] == '0');
 }
 
+// A plain 1-D launch of `kern` as a programmatic dependent (when enabled).
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kern)(KArgs...), int grid, int block, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(static_cast<unsigned>(block));
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_launch_on() ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kern, args...);
+  return finish_launch();
+}
+
 // CTA-pair kernel: clusters of 2, grid = 2 x min(tiles, SMs / 2).
 // B200Q_TMA_STORE=0 keeps the per-thread global stores in the pair kernel's
 // epilogue (A/B runs).
@@ -1343,12 +1359,10 @@ int b200q_fp8_quant_from_amax(const void* x, int x_dtype, int64_t M, int64_t K, 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int grid = grid_for(M * K / 8 + 1, 256, d);
   if (x_dtype == B200Q_BF16)
-    fp8_quantize_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(x), ldx, M, int(K), amax_bits, q, ldq, scale);
-  else
-    fp8_quantize_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(x), ldx, M,
-                                                      int(K), amax_bits, q, ldq, scale);
-  return finish_launch();
+    return launch_pdl(fp8_quantize_kernel<__nv_bfloat16>, grid, 256, st,
+                      static_cast<const __nv_bfloat16*>(x), ldx, M, int(K), amax_bits, q, ldq, scale);
+  return launch_pdl(fp8_quantize_kernel<__half>, grid, 256, st, static_cast<const __half*>(x), ldx,
+                    M, int(K), amax_bits, q, ldq, scale);
 }
 
 // Column-parallel FP8 GEMM with the all-gather in its epilogue.  This rank owns
@@ -1488,20 +1502,19 @@ int b200q_fp8_quant_tensorwise(const void* x, int x_dtype, int64_t M, int64_t K,
   if (cudaMemsetAsync(amax_scratch, 0, sizeof(unsigned int), st) != cudaSuccess) return B200Q_ERR_CUDA;
   const int64_t total = M * K;
   const int grid = grid_for(total / 8 + 1, 256, d);
+  // both passes as programmatic dependents (each waits for the kernel before it)
   if (x_dtype == B200Q_BF16) {
     auto* xp = static_cast<const __nv_bfloat16*>(x);
-    absmax_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(xp, ldx, M, int(K), amax_scratch);
-    int s = finish_launch();
+    int s = launch_pdl(absmax_kernel<__nv_bfloat16>, grid, 256, st, xp, ldx, M, int(K), amax_scratch);
     if (s) return s;
-    fp8_quantize_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(xp, ldx, M, int(K), amax_scratch, q, ldq, scale);
-  } else {
-    auto* xp = static_cast<const __half*>(x);
-    absmax_kernel<__half><<<grid, 256, 0, st>>>(xp, ldx, M, int(K), amax_scratch);
-    int s = finish_launch();
-    if (s) return s;
-    fp8_quantize_kernel<__half><<<grid, 256, 0, st>>>(xp, ldx, M, int(K), amax_scratch, q, ldq, scale);
+    return launch_pdl(fp8_quantize_kernel<__nv_bfloat16>, grid, 256, st, xp, ldx, M, int(K),
+                      static_cast<const unsigned int*>(amax_scratch), q, ldq, scale);
   }
-  return finish_launch();
+  auto* xp = static_cast<const __half*>(x);
+  int s = launch_pdl(absmax_kernel<__half>, grid, 256, st, xp, ldx, M, int(K), amax_scratch);
+  if (s) return s;
+  return launch_pdl(fp8_quantize_kernel<__half>, grid, 256, st, xp, ldx, M, int(K),
+                    static_cast<const unsigned int*>(amax_scratch), q, ldq, scale);
 }
 
 }  // extern "C"

@@ -614,6 +614,8 @@ __device__ __forceinline__ void block_atomic_max(float m, unsigned int* amax_bit
 template <typename T>
 __global__ void __launch_bounds__(256)
     absmax_kernel(const T* __restrict__ x, int64_t ldx, int64_t M, int K, unsigned int* amax_bits) {
+  griddep_wait();               // no-ops unless launched as a programmatic dependent
+  griddep_launch_dependents();  // the quantize pass may start (it waits for this grid)
   float m0 = 0.0f, m1 = 0.0f;
   const bool vec = (K % 8 == 0) && (ldx % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0);
   if (vec && ldx == K) {
@@ -651,6 +653,8 @@ __global__ void __launch_bounds__(256)
     fp8_quantize_kernel(const T* __restrict__ x, int64_t ldx, int64_t M, int K,
                         const unsigned int* __restrict__ amax_bits, uint8_t* __restrict__ q,
                         int64_t ldq, float* __restrict__ scale_out) {
+  griddep_wait();               // the amax is complete
+  griddep_launch_dependents();  // the GEMM's set-up may start (it waits for this grid)
   const float s = fp8_scale_from_amax(*amax_bits);
   const float r = __frcp_rn(s);
   if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = s;
