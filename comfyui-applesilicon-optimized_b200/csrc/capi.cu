@@ -559,9 +559,18 @@ int launch_w8a16_gemv(const void* x, int64_t ldx, const uint8_t* w, int64_t ldw,
     return B200Q_ERR_CUDA;
   auto kern = w8a16_gemv_kernel<MT, XF16>;
   if (!set_smem(kern, kGvSmemBytes)) return B200Q_ERR_CUDA;
-  const dim3 grid(static_cast<unsigned>((N + kGvRows - 1) / kGvRows));
-  kern<<<grid, kGvThreads, kGvSmemBytes, st>>>(tw, static_cast<const uint16_t*>(x), ldx, int(M),
-                                               int(N), int(K), ep);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>((N + kGvRows - 1) / kGvRows));
+  cfg.blockDim = dim3(kGvThreads);
+  cfg.dynamicSmemBytes = kGvSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_launch_on() ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kern, tw, static_cast<const uint16_t*>(x), ldx, int(M), int(N), int(K),
+                     ep);
   return finish_launch();
 }
 

@@ -771,6 +771,11 @@ __global__ void __launch_bounds__(kGvThreads, MT == 1 ? 3 : 2)
     tma_prefetch_desc(&tmW);
   }
   __syncthreads();
+  // Launched as a programmatic dependent: the set-up above overlapped the kernel
+  // before it; nothing in global memory is read before that kernel is done.
+  // The next dependent may start its own set-up now (it waits for this grid).
+  griddep_wait();
+  griddep_launch_dependents();
   auto issue = [&](int st) {  // thread 0: stage st into slot st % kGvStages
     const int slot = st % kGvStages;
     uint8_t* dst = ring + slot * kGvStageBytes;
