@@ -619,13 +619,17 @@ bool w8a16_planes_for(int64_t M, int64_t K, bool f16) {
   return M > 16 || (!f16 && K > 4096);
 }
 bool pdl_on() { return env_flag("B200Q_PDL", true); }
-// Tokens per plane tile: the smallest of 16/32/64/128 holding M (bf16) or
-// 16/32/64 (fp16, three planes: P x bt <= 192 plane rows per MMA); larger M is
+// Tokens per plane tile: 16/32/64 for M up to 16/32/128 and 128 above (bf16),
+// at most 64 for fp16 (three planes: P x bt <= 192 plane rows per MMA); M is
 // split into ntt = ceil(M / bt) token tiles.
 constexpr int64_t kWpMaxM = 256;
+// Measured on B200 at 3072 x 12288: 65..128 tokens as two 64-token tiles (192
+// CTAs, half the epilogue each) beat one 128-token tile (96 CTAs) by ~4%
+// (21.9 vs 22.8 us at M = 128); above 128 tokens 128-token tiles stay ahead
+// (31.7 vs 45.6 us at M = 256).
 int wp_bt(int64_t M, int P) {
   const int cap = P == 3 ? 64 : 128;
-  const int bt = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
+  const int bt = M <= 16 ? 16 : M <= 32 ? 32 : M <= 128 ? 64 : 128;
   return bt < cap ? bt : cap;
 }
 int wp_ntt(int64_t M, int bt) { return static_cast<int>((M + bt - 1) / bt); }
@@ -668,7 +672,12 @@ WpPlan w8a16_planes_plan(const DeviceInfo* d, int64_t M, int64_t N, int64_t K, b
       N < 1 || N > (int64_t(1) << 24))
     return best;
   const int P = f16 ? 3 : 2;
-  const int bt = wp_bt(M, P);
+  int bt = wp_bt(M, P);
+  {  // measurement switch: a smaller token tile (more CTAs per weight tile)
+    const char* fb = getenv("B200Q_W8A16_PLANES_BT");
+    const int want = fb ? atoi(fb) : 0;
+    if ((want == 16 || want == 32 || want == 64) && want < bt) bt = want;
+  }
   const int ntt = wp_ntt(M, bt);
   const int nt = P * bt;
   const int dump = nt * 128 * 4;
