@@ -727,9 +727,12 @@ WpPlan w8a16_planes_plan(const DeviceInfo* d, int64_t M, int64_t N, int64_t K, b
         double cost = t_cta > t_hbm ? t_cta : t_hbm;
         if (t_mma > cost) cost = t_mma;
         // Rank 0 adds the other ranks' accumulators of the tile's tokens over
-        // distributed shared memory: ~0.02 us per (rank, plane, token) column.
+        // distributed shared memory and runs the whole epilogue: ~0.045 us per
+        // (rank, plane, token) column (3072 x 12288: two K-halves win at 16
+        // tokens, one CTA per weight tile from 24 tokens on: 14.3 vs 15.1 us at
+        // 32, 15.7 vs 18.5 us at 48).
         const int mt = static_cast<int>(M < bt ? M : bt);
-        cost += (S > 1 ? 0.3 : 0.0) + 0.1 * S + 0.02 * (S - 1) * P * mt;
+        cost += (S > 1 ? 0.3 : 0.0) + 0.1 * S + 0.045 * (S - 1) * P * mt;
         if (env_flag("B200Q_DEBUG_PLAN", false))
           fprintf(stderr, "[b200q] planes plan M %lld N %lld K %lld: ka %d c %d S %d stages %d smem %d cost %.2f\n",
                   (long long)M, (long long)N, (long long)K, KA, c, S, stages, smem, cost);
