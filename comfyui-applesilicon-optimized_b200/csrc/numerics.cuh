@@ -276,7 +276,7 @@ __device__ __forceinline__ float epi_scaled(float acc, float rs, float cs, float
   if (e.col_scale) v = __fmul_rn(v, cs);
   if (e.extra_scale) v = __fmul_rn(v, xs);
   if (e.bias_dtype != kBiasNone) v = __fadd_rn(v, load_bias(e.bias, e.bias_dtype, n));
-  return apply_act(v, e.act);
+  return apply_act_tol(v, e.act);  // the same activation form as the tile kernels' FP8 epilogue
 }
 
 __device__ __forceinline__ void store_out(const EpiArgs& e, int64_t m, int n, float v) {
