@@ -239,17 +239,12 @@ __device__ __forceinline__ void epilogue_math(const uint32_t (&r)[32], const flo
     }
   }
   if (e.act == kActGeluTanh) {
-    // FP8 / 16-bit-operand outputs are checked to 1 ULP of the fp32 reference:
-    // the branch-free reciprocal form (the IEEE divide's slow-path branch
-    // serialised the 32 columns; the up projection's epilogue outlasted its
-    // mainloop).  INT8 dequant outputs keep the IEEE quotient (bit-exact).
-    if constexpr (EPI == kEpiScaled) {
+    // The activation is checked to 1 ULP of the reference after the output
+    // rounding (the INT8 dequant before it stays bit-exact): the branch-free
+    // reciprocal form.  The IEEE divide's slow-path branch serialised the 32
+    // columns, and an up projection's epilogue outlasted its mainloop.
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = gelu_tanh_tol(v[j]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
-    }
+    for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
   } else if (e.act == kActGeluErf) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);

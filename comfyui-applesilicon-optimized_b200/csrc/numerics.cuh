@@ -74,39 +74,30 @@ __device__ __forceinline__ uint32_t e4m3x2_to_bf16x2(uint16_t two) {
 // written without cancellation: for negative x the textbook forms
 // 0.5 x (1 + tanh(u)) and 0.5 x (1 + erf(x / sqrt 2)) subtract two numbers close
 // to 1 and lose most of fp32's digits (several fp16 ULPs at x ~ -4).  Identities
-// used: 1 + tanh(u) = 2 / (1 + exp(-2u)) and 1 + erf(z) = erfc(-z).  For u < 0
-// the tanh form is evaluated as x t / (1 + t) with t = exp(2u) <= 1, so nothing
-// overflows: x / (1 + exp(-2u)) turned the tiny negative tail (x below about
-// -10, results near 1e-38) into -0.  The divide is the IEEE one (the fast
-// __fdividef returns 0 once the divisor passes 2^126).
-__device__ __forceinline__ float gelu_tanh(float x) {
-  const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
-  const float k1 = 0.044715f;
-  const float u = k0 * (x + k1 * x * x * x);
-  const float t = expf(-2.0f * fabsf(u));
-  return __fdiv_rn(u >= 0.0f ? x : x * t, 1.0f + t);
-}
-__device__ __forceinline__ float gelu_erf(float x) {
-  return 0.5f * x * erfcf(-x * 0.7071067811865476f);
-}
-// The same tanh GELU for the W8A16 epilogues, whose outputs are checked to
-// within one bf16/fp16 ULP of the fp32 reference (not bit for bit): the
-// quotient by 1 + t (t in (0, 1], so the divisor is in (1, 2]) is taken as a
-// product with rcp.approx, which stays within a few fp32 ULP of the IEEE
-// quotient here and has no slow-path branch.  With the IEEE divide, the
-// branch kept 16 independent tokens from overlapping and the activation alone
-// took 5 us of a 128-token W8A16 epilogue on B200.
+// used: 1 + tanh(u) = 2 / (1 + exp(-2u)) and 1 + erf(z) = erfc(-z).  The tanh form
+// is x / (1 + t) for u >= 0 and x t / (1 + t) for u < 0, with t = exp(-2|u|) in
+// (0, 1], so nothing overflows (x / (1 + exp(-2u)) turned the tiny negative tail,
+// x below about -10 and results near 1e-38, into -0) and the divisor lies in
+// (1, 2]: the quotient is taken as a product with rcp.approx, within a few fp32
+// ULP of the IEEE quotient there.  Every activated output is checked to one
+// bf16/fp16 ULP of the reference after its rounding; the IEEE divide's slow-path
+// branch had kept the independent columns of an epilogue chunk from overlapping
+// (5 us of a 128-token W8A16 epilogue; an FP8 up projection's epilogue outlasted
+// its mainloop).
 __device__ __forceinline__ float rcp_approx_ftz(float x) {
   float r;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
   return r;
 }
-__device__ __forceinline__ float gelu_tanh_tol(float x) {
+__device__ __forceinline__ float gelu_tanh(float x) {
   const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
   const float k1 = 0.044715f;
   const float u = k0 * (x + k1 * x * x * x);
   const float t = expf(-2.0f * fabsf(u));
   return (u >= 0.0f ? x : x * t) * rcp_approx_ftz(1.0f + t);
+}
+__device__ __forceinline__ float gelu_erf(float x) {
+  return 0.5f * x * erfcf(-x * 0.7071067811865476f);
 }
 // SiLU of the reference's SwiGLU kernels (silu_mul_split_bf16,
 // dit_kernels.mm:724-737; i8_swiglu_rot_bf16, int8_gemm.mm:1521-1540):
@@ -169,12 +160,6 @@ __device__ __forceinline__ float swiglu_bf16(float gate, float up) {
 
 __device__ __forceinline__ float apply_act(float v, int act) {
   if (act == kActGeluTanh) return gelu_tanh(v);
-  if (act == kActGeluErf) return gelu_erf(v);
-  return v;
-}
-// Activation of the W8A16 epilogues (tolerance-checked outputs, see gelu_tanh_tol).
-__device__ __forceinline__ float apply_act_tol(float v, int act) {
-  if (act == kActGeluTanh) return gelu_tanh_tol(v);
   if (act == kActGeluErf) return gelu_erf(v);
   return v;
 }
@@ -276,7 +261,7 @@ __device__ __forceinline__ float epi_scaled(float acc, float rs, float cs, float
   if (e.col_scale) v = __fmul_rn(v, cs);
   if (e.extra_scale) v = __fmul_rn(v, xs);
   if (e.bias_dtype != kBiasNone) v = __fadd_rn(v, load_bias(e.bias, e.bias_dtype, n));
-  return apply_act_tol(v, e.act);  // the same activation form as the tile kernels' FP8 epilogue
+  return apply_act(v, e.act);
 }
 
 __device__ __forceinline__ void store_out(const EpiArgs& e, int64_t m, int n, float v) {

@@ -118,7 +118,7 @@ __device__ __forceinline__ void splitk_reduce_store(const W8A16Args& a, const Ep
         if (s2 < a.splits) v = __fadd_rn(v, p[s2][jj]);
       if (ep.extra_scale) v = __fmul_rn(v, xs);
       if (ep.bias_dtype != kBiasNone) v = __fadd_rn(v, bias_v);
-      store_out(ep, t0 + j0 + jj, n, apply_act_tol(v, ep.act));
+      store_out(ep, t0 + j0 + jj, n, apply_act(v, ep.act));
     }
   }
 }
@@ -309,7 +309,7 @@ __global__ void __launch_bounds__(kW16Threads, 1)
               } else {
                 float v = ep.extra_scale ? __fmul_rn(acc, xs) : acc;
                 if (ep.bias_dtype != kBiasNone) v = __fadd_rn(v, bias_v);
-                store_out(ep, tok, n, apply_act_tol(v, ep.act));
+                store_out(ep, tok, n, apply_act(v, ep.act));
               }
             }
           }
@@ -661,7 +661,7 @@ __global__ void __launch_bounds__(kWsThreads, 1)
               } else {
                 float vv = ep.extra_scale ? __fmul_rn(acc, xs) : acc;
                 if (ep.bias_dtype != kBiasNone) vv = __fadd_rn(vv, bias_v);
-                store_out(ep, tok, n, apply_act_tol(vv, ep.act));
+                store_out(ep, tok, n, apply_act(vv, ep.act));
               }
             }
           }
@@ -904,7 +904,7 @@ __global__ void __launch_bounds__(kGvThreads, MT == 1 ? 3 : 2)
     for (int w2 = 1; w2 < kGvWarps; ++w2) v = __fadd_rn(v, red[w2][tok][r]);
     if (ep.extra_scale) v = __fmul_rn(v, xs);
     if (ep.bias_dtype != kBiasNone) v = __fadd_rn(v, load_bias(ep.bias, ep.bias_dtype, n));
-    store_out(ep, tok, n, apply_act_tol(v, ep.act));
+    store_out(ep, tok, n, apply_act(v, ep.act));
   }
 }
 
@@ -945,7 +945,7 @@ __global__ void __launch_bounds__(256)
     if (m >= M) continue;
     float v = ep.extra_scale ? __fmul_rn(acc[i], xs) : acc[i];
     if (ep.bias_dtype != kBiasNone) v = __fadd_rn(v, load_bias(ep.bias, ep.bias_dtype, n));
-    store_out(ep, m, n, apply_act_tol(v, ep.act));
+    store_out(ep, m, n, apply_act(v, ep.act));
   }
 }
 

@@ -304,7 +304,7 @@ __device__ __forceinline__ void wp_epilogue(const WpArgs& a, const EpiArgs& ep, 
 #pragma unroll
       for (int p = 1; p < P; ++p) v = __fadd_rn(v, __fmul_rn(acc[p][j], s_pscale[p * BT + t0 + j]));
       v = __fadd_rn(__fmul_rn(v, xs), bias_v);
-      out_v[j] = apply_act_tol(v, ACT);
+      out_v[j] = apply_act(v, ACT);
     }
     // Direct typed stores (32 lanes = 32 consecutive output features of one
     // token row); measured 2x faster here than the generic per-element store.
