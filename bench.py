@@ -826,7 +826,10 @@ def run_b200q(args):
                                          "at bf16_tflops (burst)"),
                           "traffic": None, "traffic_source": None,
                           "algorithmic_bytes_per_launch": bytes_per_launch // len(spec["layers"]),
-                          "kernel": ("w8a16_gemv_kernel" if M <= 16 and spec["layers"][0].K <= 4096 else
+                          "kernel": ("x_planes_kernel + w8a16_pgemv_kernel (activation planes on "
+                                     "warp-level e4m3 MMAs, one call = both launches)"
+                                     if 2 * M <= 8 and os.environ.get("B200Q_W8A16_PGEMV", "1") != "0"
+                                     else "w8a16_gemv_kernel" if M <= 16 and spec["layers"][0].K <= 4096 else
                                      "x_planes_kernel + w8a16_planes_kernel (activation planes on "
                                      "kind::f8f6f4, one call = both launches)"),
                           "peak_source": (f"{'bf16_tflops (burst)' if small_bound == 'tensor' else 'hbm_gbs'}"

@@ -788,14 +788,12 @@ int launch_planes_gemm_nt(const WpPlan& p, const uint8_t* w, int64_t ldw, uint8_
                           float* pscale, int64_t M, int64_t N, int64_t K, const EpiArgs& ep,
                           cudaStream_t st);
 
-int launch_w8a16_planes(const WpPlan& p, const void* x, int x_dtype, int64_t ldx, const uint8_t* w,
-                        int64_t ldw, int64_t M, int64_t N, int64_t K, const EpiArgs& ep,
-                        void* workspace, cudaStream_t st) {
-  uint8_t* planes = static_cast<uint8_t*>(workspace);
-  float* pscale = reinterpret_cast<float*>(planes + wp_plane_bytes(p.P, p.bt, p.ntt, K));
+// The planes pass over M token rows (token tiles of bt rows): a programmatic
+// dependent of the previous kernel on the stream too, it waits for it
+// (griddepcontrol.wait) before touching memory.
+int launch_x_planes(const void* x, int x_dtype, int64_t ldx, int64_t M, int64_t K, int bt,
+                    uint8_t* planes, float* pscale, cudaStream_t st) {
   const int row_smem = static_cast<int>(K) * 2;
-  // The planes pass is a programmatic dependent of the previous kernel on the
-  // stream too: it waits for it (griddepcontrol.wait) before touching memory.
   cudaLaunchConfig_t pcfg = {};
   pcfg.gridDim = dim3(static_cast<unsigned>(M));
   pcfg.blockDim = dim3(kWpPlaneThreads);
@@ -809,15 +807,70 @@ int launch_w8a16_planes(const WpPlan& p, const void* x, int x_dtype, int64_t ldx
   if (x_dtype == B200Q_F16) {
     if (!set_smem(x_planes_kernel<__half, 3>, row_smem)) return B200Q_ERR_CUDA;
     cudaLaunchKernelEx(&pcfg, x_planes_kernel<__half, 3>, static_cast<const __half*>(x), ldx,
-                       int(K), p.bt, planes, pscale);
+                       int(K), bt, planes, pscale);
   } else {
     if (!set_smem(x_planes_kernel<__nv_bfloat16, 2>, row_smem)) return B200Q_ERR_CUDA;
     cudaLaunchKernelEx(&pcfg, x_planes_kernel<__nv_bfloat16, 2>,
-                       static_cast<const __nv_bfloat16*>(x), ldx, int(K), p.bt, planes, pscale);
+                       static_cast<const __nv_bfloat16*>(x), ldx, int(K), bt, planes, pscale);
   }
-  int s = finish_launch();
+  return finish_launch();
+}
+
+int launch_w8a16_planes(const WpPlan& p, const void* x, int x_dtype, int64_t ldx, const uint8_t* w,
+                        int64_t ldw, int64_t M, int64_t N, int64_t K, const EpiArgs& ep,
+                        void* workspace, cudaStream_t st) {
+  uint8_t* planes = static_cast<uint8_t*>(workspace);
+  float* pscale = reinterpret_cast<float*>(planes + wp_plane_bytes(p.P, p.bt, p.ntt, K));
+  const int s = launch_x_planes(x, x_dtype, ldx, M, K, p.bt, planes, pscale, st);
   if (s != B200Q_OK) return s;
   return launch_planes_gemm_nt(p, w, ldw, planes, pscale, M, N, K, ep, st);
+}
+
+// Planes GEMV (w8a16_pgemv_kernel): one 8-column MMA group of plane rows, i.e.
+// M <= 4 bf16 or M <= 2 fp16 tokens, one token tile of M rows.  Measured on
+// B200 at 3072 x 12288 (back-to-back calls in a CUDA graph, weights larger than
+// L2) against the decode-in-kernel GEMV: bf16 10.5 vs 12.2 us per call at M = 1,
+// 10.8 vs 12.3 at M = 4; fp16 10.6 vs 10.3 (its GEMV decodes with one
+// instruction per weight pair); two column groups (bf16 M = 8) 13.9 vs 12.5, so
+// the kernel's NG = 2 form is not routed.  B200Q_W8A16_PGEMV: unset = bf16
+// activations only, "1" = fp16 too, "0" = never (read per call).
+int pg_planes(int x_dtype) { return x_dtype == B200Q_F16 ? 3 : 2; }
+bool w8a16_pgemv_for(int64_t M, int P, int64_t K) {
+  const char* e = getenv("B200Q_W8A16_PGEMV");
+  const bool on = e ? e[0] != '0' : P == 2;
+  return on && M >= 1 && P * M <= 8 && K % 16 == 0 && K <= kWpMaxK;
+}
+size_t pg_workspace_bytes(int P, int64_t M, int64_t K) {
+  return wp_workspace_bytes(P, static_cast<int>(M), 1, K);
+}
+
+int launch_w8a16_pgemv(const void* x, int x_dtype, int64_t ldx, const uint8_t* w, int64_t ldw,
+                       int64_t M, int64_t N, int64_t K, const EpiArgs& ep, void* workspace,
+                       cudaStream_t st) {
+  const int P = pg_planes(x_dtype);
+  uint8_t* planes = static_cast<uint8_t*>(workspace);
+  float* pscale = reinterpret_cast<float*>(planes + wp_plane_bytes(P, int(M), 1, K));
+  CUtensorMap tw;
+  if (!make_tmap(&tw, w, CU_TENSOR_MAP_DATA_TYPE_UINT8, K, N, ldw, 128, kGvRows,
+                 CU_TENSOR_MAP_SWIZZLE_128B))
+    return B200Q_ERR_CUDA;
+  int s = launch_x_planes(x, x_dtype, ldx, M, K, int(M), planes, pscale, st);
+  if (s != B200Q_OK) return s;
+  auto kern = w8a16_pgemv_kernel<1>;
+  if (!set_smem(kern, kGvSmemBytes)) return B200Q_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>((N + kGvRows - 1) / kGvRows));
+  cfg.blockDim = dim3(kGvThreads);
+  cfg.dynamicSmemBytes = kGvSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl_on() ? 1 : 0;
+  cudaLaunchKernelEx(&cfg, kern, tw, static_cast<const uint8_t*>(planes),
+                     static_cast<const float*>(pscale), P, int(M), int(N), int(K), ep);
+  return finish_launch();
 }
 
 int launch_planes_gemm_nt(const WpPlan& p, const uint8_t* w, int64_t ldw, uint8_t* planes,
@@ -1558,6 +1611,8 @@ size_t b200q_w8a16_workspace_size(int64_t M, int64_t N, int64_t K) {
   if (M <= 0 || N <= 0 || K <= 0) return ws;
   const size_t planes = wp_workspace_any(M, K);
   if (planes > ws) ws = planes;
+  for (int P = 2; P <= 3; ++P)
+    if (w8a16_pgemv_for(M, P, K) && pg_workspace_bytes(P, M, K) > ws) ws = pg_workspace_bytes(P, M, K);
   if (!w8a16_decode_selected(M, N, K)) return ws;
   const size_t dec = w8a16_decode_bytes(N, K);
   return dec > ws ? dec : ws;
@@ -1605,6 +1660,9 @@ int w8a16_linear_impl(const void* x, int x_dtype, int64_t ldx, const uint8_t* w,
       w8a16_simt_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(x), ldx, w, ldw, int(M), int(N), int(K), ep);
     return finish_launch();
   }
+  if (workspace && aligned16(workspace) && w8a16_pgemv_for(M, pg_planes(x_dtype), K) &&
+      workspace_bytes >= pg_workspace_bytes(pg_planes(x_dtype), M, K))
+    return launch_w8a16_pgemv(x, x_dtype, ldx, w, ldw, M, N, K, ep, workspace, st);
   if (workspace && aligned16(workspace)) {
     const WpPlan wp = w8a16_planes_plan(d, M, N, K, x_dtype == B200Q_F16);
     if (wp.ok && workspace_bytes >= wp_workspace_bytes(wp.P, wp.bt, wp.ntt, K))
@@ -1719,13 +1777,14 @@ int noalloc_scratch(void** out) {
 
 // Scratch bytes the call will use, following w8a16_linear_impl's route order
 // with the decoded-weight route off: SIMT kernel (unaligned operands) -> none;
-// planes route when planned and its planes fit the static array; GEMV (M <= 32)
+// planes GEMV (up to 16 plane rows) -> its planes; planes route when planned and its planes fit the static array; GEMV (M <= 32)
 // -> none; otherwise the weight-stationary kernel's split-K partials + tile
 // counters (0 when it runs unsplit).  B200Q_NOALLOC_SCRATCH_BYTES + 1 means the
 // route needs more than the array holds.
 size_t noalloc_route_bytes(const DeviceInfo* d, const void* x, int x_dtype, int64_t ldx,
                            const uint8_t* w, int64_t ldw, int64_t M, int64_t N, int64_t K) {
   if (M == 0 || N == 0 || !w8a16_tc_operands(x, ldx, w, ldw, K)) return 0;
+  if (w8a16_pgemv_for(M, pg_planes(x_dtype), K)) return pg_workspace_bytes(pg_planes(x_dtype), M, K);
   const WpPlan wp = w8a16_planes_plan(d, M, N, K, x_dtype == B200Q_F16);
   if (wp.ok) {
     const size_t b = wp_workspace_bytes(wp.P, wp.bt, wp.ntt, K);

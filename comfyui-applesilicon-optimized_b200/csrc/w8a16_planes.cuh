@@ -508,4 +508,179 @@ __global__ void __maxnreg__(120)
   if (warp == 2) tmem_dealloc(tmem_d, L::kTmemCols);
 }
 
+// ---------------------------------------------------------------------------
+// Planes GEMV: 8 plane rows per MMA column group (4 bf16 tokens x 2 planes, 2 fp16
+// tokens x 3), NG groups.
+// The weight stream of the GEMV (32-row CTAs, the same TMA ring and 128-byte
+// swizzle, three CTAs per SM) multiplied on warp-level e4m3 MMAs
+// (mma.sync m16n8k32, fp32 accumulation) against the planes of the planes pass,
+// so no instruction decodes a weight: 16 weight rows are the MMA's M, plane rows
+// (plane p of token t is column p * M + t, the planes pass's layout with a token
+// tile of M rows) its N = 8 columns.  Lane (g, q) reads 16 bytes of weight rows g
+// and g + 8 of a 16-row group at K [16q, 16q + 16) of its warp's 64-byte slice;
+// bytes 8kk .. 8kk + 3 and 8kk + 4 .. 8kk + 7 feed MMA kk (kk = 0, 1) as logical
+// k 4q .. 4q + 3 and 16 + 4q .. 16 + 4q + 3, and the plane row's bytes at the
+// same K positions form the B fragment (one 16-byte load per lane and column
+// group), so the dot product is unchanged.  A stage's two MMAs start from zero
+// and are added into fp32 sums, so the tensor core's own accumulation spans 64
+// products.  The warps' sums meet in shared memory in warp order and the planes
+// are combined as in the planes route's epilogue.
+// The planes pass waited for every earlier kernel before it released this grid,
+// so the weight is final when this grid starts: the first stages are issued
+// before griddepcontrol.wait, which only guards the planes and their scales.
+constexpr int kPgMaxCols = 16;  // NG <= 2
+
+__device__ __forceinline__ void mma_e4m3_16832(float (&d)[4], uint32_t a0, uint32_t a1,
+                                               uint32_t a2, uint32_t a3, uint32_t b0,
+                                               uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.f32.e4m3.e4m3.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// NG = 8-column groups (1: up to 8 plane rows, 2: up to 16).  Requires K % 16 ==
+// 0 (whole 16-byte plane chunks) and P * M <= 8 * NG (the host checks).
+template <int NG>
+__global__ void __launch_bounds__(kGvThreads, 3)
+    w8a16_pgemv_kernel(const __grid_constant__ CUtensorMap tmW, const uint8_t* __restrict__ planes,
+                       const float* __restrict__ pscale, int P, int M, int N, int K, EpiArgs ep) {
+  __shared__ float red[kGvWarps][NG * 8][kGvRows + 1];
+  __shared__ float s_ps[kPgMaxCols];
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + kGvStages * kGvStageBytes);
+  uint64_t* empty = full + kGvStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + kGvStages);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int n0 = blockIdx.x * kGvRows;
+  const int nst = (K + kGvStageK - 1) / kGvStageK;
+  const int cols = P * M;
+
+  if (threadIdx.x == 0) {
+    for (int s2 = 0; s2 < kGvStages; ++s2) {
+      mbar_init(&full[s2], 1);
+      mbar_init(&empty[s2], kGvWarps);
+    }
+    *abort_flag = 0;
+    fence_mbarrier_init();
+    tma_prefetch_desc(&tmW);
+  }
+  __syncthreads();
+  auto issue = [&](int st) {  // thread 0: stage st into slot st % kGvStages
+    const int slot = st % kGvStages;
+    uint8_t* dst = ring + slot * kGvStageBytes;
+    mbar_arrive_expect_tx(&full[slot], kGvStageBytes);
+#pragma unroll
+    for (int b = 0; b < kGvStageK / 128; ++b)
+      tma_load_2d(&tmW, &full[slot], dst + b * (kGvRows * 128), st * kGvStageK + b * 128, n0);
+  };
+  if (threadIdx.x == 0)
+    for (int st = 0; st < kGvStages && st < nst; ++st) issue(st);
+  griddep_wait();  // the planes and plane scales of the planes pass
+  griddep_launch_dependents();
+  if (threadIdx.x < cols) s_ps[threadIdx.x] = __ldg(pscale + threadIdx.x);
+
+  // Plane rows of this lane: column 8 ng + g; columns past P * M read as zero.
+  const uint8_t* prow[NG];
+  bool pok[NG];
+#pragma unroll
+  for (int ng = 0; ng < NG; ++ng) {
+    const int c = 8 * ng + g;
+    pok[ng] = c < cols;
+    prow[ng] = planes + static_cast<int64_t>(pok[ng] ? c : 0) * K + 16 * q;
+  }
+  uint4 pa[NG], pn[NG];
+  auto load_p = [&](int st, uint4 (&dst)[NG]) {
+    const int k0 = st * kGvStageK + 64 * warp;
+    const bool kin = st < nst && k0 + 16 * q < K;
+#pragma unroll
+    for (int ng = 0; ng < NG; ++ng)
+      dst[ng] = (pok[ng] && kin) ? __ldg(reinterpret_cast<const uint4*>(prow[ng] + k0))
+                                 : make_uint4(0u, 0u, 0u, 0u);
+  };
+  load_p(0, pn);
+  float acc[2][NG][4];
+#pragma unroll
+  for (int rg = 0; rg < 2; ++rg)
+#pragma unroll
+    for (int ng = 0; ng < NG; ++ng)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[rg][ng][i] = 0.0f;
+  const int box = warp >> 1;
+  const int chunk = (warp & 1) * 4 + q;
+
+  bool ok = true;
+  for (int st = 0; st < nst && ok; ++st) {
+    const int slot = st % kGvStages;
+    const uint32_t ph = (st / kGvStages) & 1u;
+#pragma unroll
+    for (int ng = 0; ng < NG; ++ng) pa[ng] = pn[ng];
+    load_p(st + 1, pn);
+    if (!mbar_wait_warp(&full[slot], ph, abort_flag)) { ok = false; break; }
+    const int k0 = st * kGvStageK + 64 * warp;
+    if (k0 < K) {
+      const uint8_t* sb = ring + slot * kGvStageBytes + box * (kGvRows * 128);
+      uint4 wv[4];  // rows 8 gr + g
+#pragma unroll
+      for (int gr = 0; gr < 4; ++gr) {
+        const int r = 8 * gr + g;
+        wv[gr] = *reinterpret_cast<const uint4*>(sb + r * 128 + ((chunk ^ (r & 7)) << 4));
+      }
+#pragma unroll
+      for (int rg = 0; rg < 2; ++rg)
+#pragma unroll
+        for (int ng = 0; ng < NG; ++ng) {
+          float d[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+          const uint4 lo = wv[2 * rg], hi = wv[2 * rg + 1];
+          mma_e4m3_16832(d, lo.x, hi.x, lo.y, hi.y, pa[ng].x, pa[ng].y);
+          mma_e4m3_16832(d, lo.z, hi.z, lo.w, hi.w, pa[ng].z, pa[ng].w);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[rg][ng][i] += d[i];
+        }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+    if (threadIdx.x == 0 && st + kGvStages < nst) {
+      if (!mbar_wait(&empty[slot], ph, abort_flag)) { ok = false; break; }
+      issue(st + kGvStages);
+    }
+  }
+  if (!ok && threadIdx.x == 0) {
+    for (int s2 = 0; s2 < kGvStages; ++s2) mbar_wait_drain(&full[s2], 0);
+  }
+
+  // D fragment: acc[rg][ng][i] is weight row 16 rg + g + 8 (i >> 1), plane
+  // column 8 ng + 2q + (i & 1).
+#pragma unroll
+  for (int rg = 0; rg < 2; ++rg)
+#pragma unroll
+    for (int ng = 0; ng < NG; ++ng)
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        red[warp][8 * ng + 2 * q + (i & 1)][16 * rg + g + 8 * (i >> 1)] = acc[rg][ng][i];
+  __syncthreads();
+  if (*abort_flag) return;
+  const float xs = ep.extra_scale ? __ldg(ep.extra_scale) : 1.0f;
+  for (int e = threadIdx.x; e < M * kGvRows; e += kGvThreads) {
+    const int tok = e / kGvRows, r = e % kGvRows;
+    const int n = n0 + r;
+    if (n >= N) continue;
+    float v = 0.0f;
+    for (int p = 0; p < P; ++p) {
+      const int c = p * M + tok;
+      float s = red[0][c][r];
+#pragma unroll
+      for (int w2 = 1; w2 < kGvWarps; ++w2) s = __fadd_rn(s, red[w2][c][r]);
+      v = p == 0 ? __fmul_rn(s, s_ps[c]) : __fadd_rn(v, __fmul_rn(s, s_ps[c]));
+    }
+    if (ep.extra_scale) v = __fmul_rn(v, xs);
+    if (ep.bias_dtype != kBiasNone) v = __fadd_rn(v, load_bias(ep.bias, ep.bias_dtype, n));
+    store_out(ep, tok, n, apply_act(v, ep.act));
+  }
+}
+
 }  // namespace b200q

@@ -39,8 +39,11 @@ def _case(M, K, N, dtype, seed, outliers=True):
 @pytest.fixture(autouse=True)
 def _planes_route(monkeypatch):
     """Every eligible call takes the planes route here (by default it runs only
-    for the token counts where it measured fastest)."""
+    for the token counts where it measured fastest); the planes GEMV, which takes
+    calls of up to 16 plane rows before it, is switched off
+    (test_gpu_w8a16_pgemv covers it)."""
     monkeypatch.setenv("B200Q_W8A16_PLANES", "1")
+    monkeypatch.setenv("B200Q_W8A16_PGEMV", "0")
 
 
 def _launches(native, fn):

@@ -24,8 +24,9 @@ FP8_RMS_TOL = 0.02
 def _decode_in_kernel_routes(monkeypatch):
     """These kernels are the fallback of the planes route (test_gpu_w8a16_planes):
     they run when no workspace is given or no planes plan fits the shape, so the
-    planes route is switched off here to keep them covered."""
+    planes route and the planes GEMV are switched off here to keep them covered."""
     monkeypatch.setenv("B200Q_W8A16_PLANES", "0")
+    monkeypatch.setenv("B200Q_W8A16_PGEMV", "0")
 
 
 def _gen(seed):
