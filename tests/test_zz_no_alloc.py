@@ -6,8 +6,8 @@ front, or a runtime whose device-memory budget is fixed before the model runs).
 Its scratch is a static device array inside the library.  These tests check,
 through ctypes on the shared library, that two calls in a row match the
 workspace-taking entry point and the CPU oracle within the tolerance the other
-W8A16 tests use, on both routes that use the array (the small-M planes route
-and the split-K weight-stationary kernel); that the calls allocate no device
+W8A16 tests use, on the routes that use the array (the planes GEMV, the
+small-M planes route and the split-K weight-stationary kernel); that the calls allocate no device
 memory; that a shape whose route fits is accepted even when another route would
 not fit; and that a shape whose route does not fit is rejected with the clear
 error status without launching anything.
@@ -112,6 +112,14 @@ def test_noalloc_planes_route_matches_twice(native, abi, dtype, M, K, N):
     """17 <= M <= 256: the planes route, its planes and plane scales in the
     static array (written by the planes pass, read by the GEMM)."""
     x, w, ws, bias = _inputs(torch.Generator().manual_seed(M + K), M, K, N, dtype)
+    _check_twice(native, abi, x, w, ws, bias)
+
+
+@pytest.mark.parametrize("M", [1, 4])
+def test_noalloc_planes_gemv_matches_twice(native, abi, M):
+    """bf16, M <= 4: the planes GEMV, its planes and plane scales in the static
+    array (written by the planes pass, read by the GEMV's warps)."""
+    x, w, ws, bias = _inputs(torch.Generator().manual_seed(M + 7), M, 3072, 4096, torch.bfloat16)
     _check_twice(native, abi, x, w, ws, bias)
 
 
