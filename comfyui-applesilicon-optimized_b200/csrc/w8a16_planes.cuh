@@ -42,6 +42,10 @@
 //   order through distributed shared memory (fixed order, so results are
 //   bit-reproducible), combines the planes and runs the epilogue.  No global
 //   workspace, counters or memset node is involved.
+//   w8a16_pgemv_kernel<NG>
+//     the planes GEMV for up to 8 * NG plane rows (a few tokens): the GEMV's
+//     32-row CTAs and TMA weight ring, every warp multiplying its own K slice
+//     on warp-level e4m3 MMAs (mma.sync m16n8k32) against the planes.
 #pragma once
 
 #include <type_traits>
