@@ -62,6 +62,26 @@ def test_abi_rejects_bad_arguments_without_a_gpu():
                                                      4, 384, 16, None) == 1
 
 
+def test_w8a16_workspace_size_follows_the_routes(monkeypatch):
+    """The size query covers the route a call takes (a host query, no device
+    work): the planes GEMV's planes + plane scales for M <= 4 (bf16, 2 planes;
+    with B200Q_W8A16_PGEMV=1 also fp16's 3 planes for M <= 2), nothing for the
+    decode-in-kernel GEMV (M 5..16 at K <= 4096), the planes route above 16."""
+    L = _native.lib()
+    N, K = 12288, 3072
+    monkeypatch.delenv("B200Q_W8A16_PGEMV", raising=False)
+    monkeypatch.delenv("B200Q_W8A16_PLANES", raising=False)
+    for M in (1, 2, 3, 4):
+        assert L.b200q_w8a16_workspace_size(M, N, K) == -(-2 * M * K // 256) * 256 + 2 * M * 4
+    for M in (5, 8, 16):
+        assert L.b200q_w8a16_workspace_size(M, N, K) == 0
+    assert L.b200q_w8a16_workspace_size(17, N, K) > 0
+    monkeypatch.setenv("B200Q_W8A16_PGEMV", "0")
+    assert L.b200q_w8a16_workspace_size(1, N, K) == 0
+    monkeypatch.setenv("B200Q_W8A16_PGEMV", "1")
+    assert L.b200q_w8a16_workspace_size(2, N, K) == 3 * 2 * K + 3 * 2 * 4
+
+
 def test_torch_ops_registered_with_fake_kernels():
     for name in ("quant_rowwise_i8", "int_mm", "i8_matmul_nt", "i8_matmul_nt_fused",
                  "i8_matmul_nt_fused_cs", "i8_linear", "fp8_quant_tensorwise", "fp8_scaled_mm",
