@@ -134,6 +134,51 @@ def test_pgemv_nonfinite_row(native):
     assert oracle.fp8_errors(out[[0, 2]], ref)[0] <= 1e-5
 
 
+def _wide_row(K, g):
+    """A bf16 row whose magnitudes span 2^20 (exponents uniform in [-10, 10])."""
+    e = torch.rand(K, generator=g) * 20 - 10
+    return (torch.randn(K, generator=g) * torch.exp2(e)).to(torch.bfloat16)
+
+
+def test_pgemv_wide_dynamic_range_rows(native):
+    """Rows spanning 2^20: elements more than ~2^13 below their row maximum lose
+    bits under e4m3's subnormal spacing (below 2^-21 of the maximum each); the
+    fp32 output stays within 2% of the row's RMS, the FP8 routes' bound."""
+    M, K, N = 3, 2048, 1024
+    x, w, ws, b = _case(M, K, N, torch.bfloat16, 21, outliers=False)
+    g = torch.Generator().manual_seed(22)
+    for r in range(M):
+        x[r] = _wide_row(K, g)
+    ref = oracle.w8a16_linear(x, w, ws, b, None, out_dtype="fp32")
+    out32 = native.w8a16_linear(x.to(DEV), w.to(DEV), ws.to(DEV), b.to(DEV), None,
+                                torch.float32).cpu()
+    for r in range(M):
+        assert oracle.fp8_errors(out32[r], ref[r])[0] <= FP8_RMS_TOL
+
+
+def test_nonfinite_row_planes_vs_decode_route(native, monkeypatch):
+    """With an inf in a row the planes GEMV returns a NaN row, while the
+    decode-in-kernel GEMV (the reference's decode-then-matmul arithmetic)
+    propagates the infinity: every output of the row is +-inf with the sign of
+    the weight at that K (all nonzero here).  Other rows match the oracle."""
+    M, K, N = 3, 1024, 256
+    x, w, ws, b = _case(M, K, N, torch.bfloat16, 23, outliers=False)
+    x[1, 7] = float("inf")
+    xd, wd = x.to(DEV), w.to(DEV)
+    planes = native.w8a16_linear(xd, wd, None, None, None, torch.float32).cpu()
+    monkeypatch.setenv("B200Q_W8A16_PGEMV", "0")
+    monkeypatch.setenv("B200Q_W8A16_PLANES", "0")
+    dec = native.w8a16_linear(xd, wd, None, None, None, torch.float32).cpu()
+    assert torch.isnan(planes[1]).all()
+    col = w[:, 7].float()
+    assert (col != 0).all()
+    inf = torch.full_like(col, float("inf"))
+    assert torch.equal(dec[1], torch.where(col > 0, inf, -inf))
+    ref = oracle.w8a16_linear(x[[0, 2]], w, None, None, None, out_dtype="fp32")
+    assert oracle.fp8_errors(planes[[0, 2]], ref)[0] <= 1e-5
+    assert oracle.fp8_errors(dec[[0, 2]], ref)[0] <= 1e-4
+
+
 def test_pgemv_strided_activation(native):
     M, K, N = 4, 2048, 640
     g = torch.Generator().manual_seed(5)

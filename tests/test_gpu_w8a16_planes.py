@@ -133,6 +133,24 @@ def test_planes_nonfinite_row(native):
     assert oracle.fp8_errors(out[[0, 2]], ref)[0] <= 1e-5
 
 
+def test_planes_wide_dynamic_range_rows(native):
+    """Rows spanning 2^20 (exponents uniform in [-10, 10]): elements more than
+    ~2^13 below their row maximum lose bits under e4m3's subnormal spacing (below
+    2^-21 of the maximum each); the fp32 output stays within 2% of each row's
+    RMS, the FP8 routes' bound."""
+    M, K, N = 20, 2048, 1024
+    x, w, ws, b = _case(M, K, N, torch.bfloat16, 21, outliers=False)
+    g = torch.Generator().manual_seed(22)
+    for r in range(M):
+        e = torch.rand(K, generator=g) * 20 - 10
+        x[r] = (torch.randn(K, generator=g) * torch.exp2(e)).to(torch.bfloat16)
+    ref = oracle.w8a16_linear(x, w, ws, b, None, out_dtype="fp32")
+    out32 = native.w8a16_linear(x.to(DEV), w.to(DEV), ws.to(DEV), b.to(DEV), None,
+                                torch.float32).cpu()
+    for r in range(M):
+        assert oracle.fp8_errors(out32[r], ref[r])[0] <= FP8_RMS_TOL
+
+
 def test_planes_strided_activation(native):
     M, K, N = 8, 2048, 640
     g = torch.Generator().manual_seed(5)
