@@ -1777,8 +1777,8 @@ int noalloc_scratch(void** out) {
 
 // Scratch bytes the call will use, following w8a16_linear_impl's route order
 // with the decoded-weight route off: SIMT kernel (unaligned operands) -> none;
-// planes GEMV (up to 16 plane rows) -> its planes; planes route when planned and its planes fit the static array; GEMV (M <= 32)
-// -> none; otherwise the weight-stationary kernel's split-K partials + tile
+// planes GEMV (up to 8 plane rows) -> its planes; planes route when planned and
+// its planes fit the static array; GEMV (M <= 32) -> none; otherwise the weight-stationary kernel's split-K partials + tile
 // counters (0 when it runs unsplit).  B200Q_NOALLOC_SCRATCH_BYTES + 1 means the
 // route needs more than the array holds.
 size_t noalloc_route_bytes(const DeviceInfo* d, const void* x, int x_dtype, int64_t ldx,
