@@ -575,7 +575,8 @@ int launch_w8a16_gemv(const void* x, int64_t ldx, const uint8_t* w, int64_t ldw,
 }
 
 // W8A16 with <= 32 tokens takes the weight-streaming GEMV when the operands are
-// 16-byte aligned (the caller checks).  B200Q_W8A16_GEMV=0 turns it off (A/B runs).
+// 16-byte aligned (the caller checks) and neither the planes GEMV nor the planes
+// route took the call.  B200Q_W8A16_GEMV=0 turns it off (A/B runs).
 bool w8a16_gemv_selected(int64_t M) {
   static const bool on = [] {
     const char* e = getenv("B200Q_W8A16_GEMV");
